@@ -1,0 +1,513 @@
+#!/usr/bin/env python
+"""Benchmark of the int8 weight-only (W8A16) hot path on B200.
+
+Workload (the configuration the headline metric is
+quoted on): the talker's four linear shapes -- fused qkv 4096x2048, o_proj
+2048x2048, gate_up 12288x2048, down 2048x6144 -- at M in {1,2,4,8,16,32,64},
+weights fp32 ~N(0, 0.02) quantized per output row to int8 (bf16 scales, as
+Int8WeightOnlyMethod stores them), activations bf16 ~N(0, 1), seed 0.
+
+One step = the sweep at the reference benchmark's own call count: every
+(shape, M) point runs 2016 calls (the reference times 10 calls x 200 replays
+per point, examples/kernels/tune_w8_gemm.py:48-70), as 9 replays of a CUDA
+graph of 224 calls through ``qtts_b200.quant.kernels.w8_gemm``. Each call
+reads a different copy of the weight: per shape a pool of at least 256 MB
+(> 2x the 126 MB L2), reused only after a full pool, so every call streams its
+weights from HBM.
+
+``value`` = algorithmic bytes of all calls (int8 W + bf16 scale + bf16 x +
+bf16 out) / device time, aggregated over ranks; ``e2e`` adds, per point, the
+host->device copy of x from pinned memory and the device->host copy of the
+output. ``--impl reference`` times the reference's eager CPU path
+(``F.linear(x, q.to(bf16) * scale)``, restated in ``oracle/``) on the host
+cores instead.
+
+Multi-GPU: one process per GPU under torchrun; each rank runs the full sweep
+on its own GPU (independent replicas, weak scaling), timing is the max over
+ranks.
+"""
+
+from __future__ import annotations
+
+import argparse
+import json
+import os
+import statistics
+import subprocess
+import sys
+import threading
+import time
+from pathlib import Path
+
+ROOT = Path(__file__).resolve().parent
+for _p in (str(ROOT), str(ROOT / "tts-inference_b200")):
+    if _p not in sys.path:
+        sys.path.insert(0, _p)
+
+import torch  # noqa: E402
+
+SHAPES = [("qkv", 4096, 2048), ("o_proj", 2048, 2048), ("gate_up", 12288, 2048), ("down_proj", 2048, 6144)]
+ROWS = (1, 2, 4, 8, 16, 32, 64)
+CALLS_PER_GRAPH = 224  # multiple of every pool size below
+REPLAYS_PER_POINT = 9  # 9 x 224 = 2016 calls per point
+POOL_MIN_BYTES = 256 << 20
+METRIC = "int8 W8A16 GEMM HBM GB/s (talker linear sweep, M=1..64)"
+
+
+def algo_bytes(n: int, k: int, m: int) -> int:
+    """Algorithmic bytes of one call: int8 weight, bf16 scale, bf16 x, bf16 out."""
+    return n * k + 2 * n + 2 * m * k + 2 * m * n
+
+
+def pool_size(n: int, k: int) -> int:
+    """Smallest divisor of CALLS_PER_GRAPH whose copies hold >= POOL_MIN_BYTES."""
+    need = -(-POOL_MIN_BYTES // (n * k))
+    for d in range(1, CALLS_PER_GRAPH + 1):
+        if CALLS_PER_GRAPH % d == 0 and d >= need:
+            return d
+    return CALLS_PER_GRAPH
+
+
+def peaks() -> dict:
+    p = ROOT / "MEASURED_PEAKS.json"
+    if p.exists():
+        d = json.loads(p.read_text())
+        return {"hbm_gbs": float(d["hbm_gbs"]), "source": "measured"}
+    return {"hbm_gbs": 6650.0, "source": "fallback"}
+
+
+# ----------------------------------------------------------------------------- clocks
+
+
+class ClockSampler:
+    """nvidia-smi clock/throttle sampling during the timed region."""
+
+    FIELDS = (
+        "index,clocks.sm,clocks.max.sm,power.draw,clocks_event_reasons.hw_slowdown,"
+        "clocks_event_reasons.hw_thermal_slowdown,clocks_event_reasons.sw_thermal_slowdown,"
+        "clocks_event_reasons.sw_power_cap"
+    )
+
+    def __init__(self, device_index: int, log_path: Path | None = None):
+        self.device_index = device_index
+        self.lines: list[str] = []
+        self.proc = None
+        self.log_path = log_path
+        self._thread = None
+
+    def start(self):
+        try:
+            self.proc = subprocess.Popen(
+                ["nvidia-smi", f"--query-gpu={self.FIELDS}", "--format=csv,noheader,nounits", "-lms", "100",
+                 "-i", str(self.device_index)],
+                stdout=subprocess.PIPE, stderr=subprocess.DEVNULL, text=True,
+            )
+        except OSError:
+            self.proc = None
+            return
+        self._thread = threading.Thread(target=self._read, daemon=True)
+        self._thread.start()
+
+    def _read(self):
+        assert self.proc is not None and self.proc.stdout is not None
+        for line in self.proc.stdout:
+            self.lines.append(line.strip())
+
+    def stop(self) -> dict:
+        if self.proc is None:
+            return {"sm_mhz": None, "sm_max_mhz": None, "reasons": ["nvidia-smi unavailable"], "samples": 0}
+        self.proc.terminate()
+        try:
+            self.proc.wait(timeout=5)
+        except subprocess.TimeoutExpired:
+            self.proc.kill()
+        if self._thread is not None:
+            self._thread.join(timeout=2)
+        sm, sm_max, reasons = [], [], set()
+        names = ["hw_slowdown", "hw_thermal_slowdown", "sw_thermal_slowdown", "sw_power_cap"]
+        for line in self.lines:
+            parts = [p.strip() for p in line.split(",")]
+            if len(parts) < 8:
+                continue
+            try:
+                sm.append(float(parts[1]))
+                sm_max.append(float(parts[2]))
+            except ValueError:
+                continue
+            for name, flag in zip(names, parts[4:8]):
+                if flag.lower().startswith("active"):
+                    reasons.add(name)
+        if self.log_path is not None:
+            self.log_path.write_text("\n".join(self.lines) + "\n")
+        return {
+            "sm_mhz": statistics.median(sm) if sm else None,
+            "sm_max_mhz": max(sm_max) if sm_max else None,
+            "reasons": sorted(reasons),
+            "samples": len(sm),
+        }
+
+
+# ----------------------------------------------------------------------------- distributed
+
+
+def dist_init():
+    world = int(os.environ.get("WORLD_SIZE", "1"))
+    rank = int(os.environ.get("RANK", "0"))
+    local = int(os.environ.get("LOCAL_RANK", "0"))
+    if world > 1:
+        import datetime
+
+        import torch.distributed as dist
+
+        torch.cuda.set_device(local)
+        dist.init_process_group("nccl", timeout=datetime.timedelta(seconds=120),
+                                device_id=torch.device("cuda", local))
+    elif torch.cuda.is_available():
+        torch.cuda.set_device(0)
+    return world, rank, local
+
+
+def barrier(world):
+    if world > 1:
+        import torch.distributed as dist
+
+        dist.barrier()
+
+
+def max_over_ranks(world, value: float) -> float:
+    if world == 1:
+        return value
+    import torch.distributed as dist
+
+    t = torch.tensor([value], dtype=torch.float64, device="cuda")
+    dist.all_reduce(t, op=dist.ReduceOp.MAX)
+    return float(t.item())
+
+
+# ----------------------------------------------------------------------------- CPU reference arm
+
+
+def cpu_port_sample(budget_s: float, rows=ROWS) -> dict:
+    """The reference's eager dequant-then-matmul on host cores (oracle port)."""
+    import oracle.cpu_baseline as cb
+
+    return cb.time_sweep(SHAPES, rows, budget_s=budget_s)
+
+
+def run_reference_arm(args) -> None:
+    world = int(os.environ.get("WORLD_SIZE", "1"))
+    rank = int(os.environ.get("RANK", "0"))
+    if rank != 0:
+        return
+    import oracle.cpu_baseline as cb
+
+    threads = cb.use_all_threads()
+    work = cb.SweepWork(SHAPES, ROWS, seed=0)
+    for _ in range(args.warmup):
+        work.step()
+    t0 = time.perf_counter()
+    for _ in range(args.steps):
+        work.step()
+    elapsed = time.perf_counter() - t0
+    bytes_per_step = work.bytes_per_step
+    value = bytes_per_step * args.steps / elapsed / 1e9
+    line = {
+        "impl": "reference",
+        "metric": METRIC,
+        "value": value,
+        "unit": "GB/s",
+        "n_gpus": world,
+        "steps": args.steps,
+        "warmup": args.warmup,
+        "ms_per_step": elapsed / args.steps * 1e3,
+        "higher_is_better": True,
+        "scaling": "weak",
+        "vs_baseline": None,
+        "dtype": "bf16",
+        "data": "synthetic",
+        "config": {
+            "workload": "config-2 talker linear sweep on the host CPU: 4 shapes x M in {1,2,4,8,16,32,64}, "
+            "one call per point per step (a bounded sample of the GPU step's 2016 calls per point)",
+        },
+        "cpu_baseline": {
+            "value": value,
+            "unit": "GB/s",
+            "cores": threads,
+            "kind": "port",
+            "sample": "one eager F.linear(x, q.to(bf16) * scale[:, None]) per (shape, M) point per step",
+        },
+        "e2e": {"value": value, "unit": "GB/s", "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0},
+    }
+    print(json.dumps(line), flush=True)
+
+
+# ----------------------------------------------------------------------------- GPU arm
+
+
+class Point:
+    def __init__(self, label, n, k, m):
+        self.label, self.n, self.k, self.m = label, n, k, m
+        self.bytes = algo_bytes(n, k, m)
+        self.graph = None
+        self.bf16_graph = None
+
+
+def build_pools(device, seed: int):
+    from qtts_b200.quant import kernels as qk
+
+    gen = torch.Generator(device=device)
+    gen.manual_seed(seed)
+    pools = {}
+    for label, n, k in SHAPES:
+        p = pool_size(n, k)
+        qs = torch.empty((p, n, k), dtype=torch.int8, device=device)
+        ss = torch.empty((p, n), dtype=torch.bfloat16, device=device)
+        for i in range(p):
+            w = torch.randn((n, k), generator=gen, device=device) * 0.02
+            q, s = qk.quantize_int8_rows(w)
+            qs[i].copy_(q)
+            ss[i].copy_(s.to(torch.bfloat16))
+            del w, q, s
+        pools[label] = (qs, ss)
+    torch.cuda.synchronize()
+    return pools
+
+
+def capture(fn):
+    side = torch.cuda.Stream()
+    side.wait_stream(torch.cuda.current_stream())
+    with torch.cuda.stream(side):
+        fn()
+    torch.cuda.current_stream().wait_stream(side)
+    torch.cuda.synchronize()
+    g = torch.cuda.CUDAGraph()
+    with torch.cuda.graph(g):
+        fn()
+    torch.cuda.synchronize()
+    return g
+
+
+def run_gpu_arm(args) -> None:
+    from qtts_b200 import _native as nat
+    from qtts_b200.quant import kernels as qk
+
+    world, rank, local = dist_init()
+    device = torch.device("cuda", local)
+    ok, reason = qk.kernel_available()
+    if not ok:
+        raise RuntimeError(reason)
+    pools = build_pools(device, seed=args.seed)
+    gen = torch.Generator(device=device)
+    gen.manual_seed(args.seed + 1)
+
+    points: list[Point] = []
+    xs, outs, xs_host, outs_host = {}, {}, {}, {}
+    for m in ROWS:
+        for label, n, k in SHAPES:
+            pt = Point(label, n, k, m)
+            x = torch.randn((m, k), generator=gen, device=device).to(torch.bfloat16)
+            out = torch.empty((m, n), dtype=torch.bfloat16, device=device)
+            xs[(label, m)], outs[(label, m)] = x, out
+            xs_host[(label, m)] = x.cpu().pin_memory()
+            outs_host[(label, m)] = torch.empty((m, n), dtype=torch.bfloat16).pin_memory()
+            qs, ss = pools[label]
+            variant = nat.VARIANT_AUTO if args.variant is None else int(args.variant, 0)
+
+            def calls(x=x, out=out, qs=qs, ss=ss, variant=variant):
+                p = qs.shape[0]
+                for c in range(CALLS_PER_GRAPH):
+                    qk.w8_gemm(x, qs[c % p], ss[c % p], None, out=out, variant=variant)
+
+            pt.graph = capture(calls)
+            points.append(pt)
+
+    bytes_per_step = sum(pt.bytes for pt in points) * CALLS_PER_GRAPH * REPLAYS_PER_POINT
+    launches_per_step = len(points) * CALLS_PER_GRAPH * REPLAYS_PER_POINT
+    stream = torch.cuda.current_stream()
+
+    def step(events=None):
+        for i, pt in enumerate(points):
+            for _ in range(REPLAYS_PER_POINT):
+                pt.graph.replay()
+            if events is not None:
+                events[i].record(stream)
+
+    for _ in range(args.warmup):
+        step()
+    torch.cuda.synchronize()
+    barrier(world)
+
+    sampler = ClockSampler(local, ROOT / "gpurun_out" / "bench_clocks.csv" if (ROOT / "gpurun_out").is_dir() else None)
+    sampler.start()
+    time.sleep(0.3)
+    torch.cuda.synchronize()
+    barrier(world)
+    start = torch.cuda.Event(enable_timing=True)
+    end = torch.cuda.Event(enable_timing=True)
+    point_events = [[torch.cuda.Event(enable_timing=True) for _ in points] for _ in range(args.steps)]
+    start.record(stream)
+    for s in range(args.steps):
+        step(point_events[s])
+    end.record(stream)
+    torch.cuda.synchronize()
+    barrier(world)
+    clocks = sampler.stop()
+    elapsed_ms = start.elapsed_time(end)
+    elapsed_ms_max = max_over_ranks(world, elapsed_ms)
+
+    # per-point device time, averaged over steps
+    per_point_ms = [0.0] * len(points)
+    for s in range(args.steps):
+        prev = start if s == 0 else point_events[s - 1][-1]
+        for i, ev in enumerate(point_events[s]):
+            per_point_ms[i] += (prev.elapsed_time(ev)) / args.steps
+            prev = ev
+
+    value = bytes_per_step * args.steps * world / (elapsed_ms_max * 1e-3) / 1e9
+    pk = peaks()
+    calls_per_point = CALLS_PER_GRAPH * REPLAYS_PER_POINT
+    per_point = {}
+    for pt, ms in zip(points, per_point_ms):
+        us = ms * 1e3 / calls_per_point
+        per_point.setdefault(pt.label, {})[str(pt.m)] = {
+            "us": round(us, 3),
+            "gbs": round(pt.bytes / (us * 1e-6) / 1e9, 1),
+        }
+
+    # ---- cuBLAS bf16 comparison (outside the timed region)
+    if args.bf16_compare:
+        bf16_pools = {}
+        for label, n, k in SHAPES:
+            qs, ss = pools[label]
+            p = pool_size(n, k)
+            bf16_pools[label] = [(qs[i].to(torch.bfloat16) * ss[i][:, None]) for i in range(p)]
+        for pt in points:
+            x, out = xs[(pt.label, pt.m)], outs[(pt.label, pt.m)]
+            wl = bf16_pools[pt.label]
+
+            def bcalls(x=x, wl=wl):
+                for c in range(CALLS_PER_GRAPH):
+                    torch.nn.functional.linear(x, wl[c % len(wl)])
+
+            g = capture(bcalls)
+            e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+            g.replay()
+            e0.record(stream)
+            for _ in range(3):
+                g.replay()
+            e1.record(stream)
+            torch.cuda.synchronize()
+            us = e0.elapsed_time(e1) * 1e3 / (3 * CALLS_PER_GRAPH)
+            d = per_point[pt.label][str(pt.m)]
+            d["bf16_us"] = round(us, 3)
+            d["speedup_vs_bf16"] = round(us / d["us"], 3)
+            del g
+        del bf16_pools
+        torch.cuda.empty_cache()
+
+    # ---- end to end: host buffers in, results out, through the public API
+    h2d = sum(pt.m * pt.k * 2 for pt in points)
+    d2h = sum(pt.m * pt.n * 2 for pt in points)
+
+    def e2e_step():
+        for pt in points:
+            key = (pt.label, pt.m)
+            xs[key].copy_(xs_host[key], non_blocking=True)
+            for _ in range(REPLAYS_PER_POINT):
+                pt.graph.replay()
+            outs_host[key].copy_(outs[key], non_blocking=True)
+
+    for _ in range(max(1, args.warmup)):
+        e2e_step()
+    torch.cuda.synchronize()
+    barrier(world)
+    e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    e0.record(stream)
+    for _ in range(args.steps):
+        e2e_step()
+    e1.record(stream)
+    torch.cuda.synchronize()
+    e2e_ms = max_over_ranks(world, e0.elapsed_time(e1))
+    e2e_value = bytes_per_step * args.steps * world / (e2e_ms * 1e-3) / 1e9
+
+    status = nat.device_status()
+    cpu = None
+    if rank == 0 and world == 1 and not args.no_cpu_baseline:
+        cpu = cpu_port_sample(args.cpu_seconds)
+
+    if rank == 0:
+        line = {
+            "metric": METRIC,
+            "value": round(value, 1),
+            "unit": "GB/s",
+            "n_gpus": world,
+            "steps": args.steps,
+            "warmup": args.warmup,
+            "ms_per_step": round(elapsed_ms_max / args.steps, 4),
+            "higher_is_better": True,
+            "scaling": "weak",
+            "vs_baseline": None,
+            "dtype": "bf16",
+            "data": "synthetic",
+            "config": {
+                "workload": "config-2 talker linear sweep: qkv 4096x2048, o_proj 2048x2048, gate_up 12288x2048, "
+                "down 2048x6144 at M in {1,2,4,8,16,32,64}; 2016 calls per point per step",
+                "global_batch": None,
+                "l2": "weights rotate through >= 256 MB per shape (> 2x L2); every call reads its weight from HBM",
+                "parallelism": f"replicas x{world}" if world > 1 else "single GPU",
+                "variant": args.variant or "auto",
+            },
+            "roofline": {
+                "bound": "hbm",
+                "kernel": "skinny_w8a16_kernel",
+                "achieved": round(value / world, 1),
+                "peak": pk["hbm_gbs"],
+                "unit": "GB/s",
+                "frac": round(value / world / pk["hbm_gbs"], 4),
+                "peak_source": pk["source"],
+                "traffic": None,
+            },
+            "cpu_baseline": cpu,
+            "e2e": {
+                "value": round(e2e_value, 1),
+                "unit": "GB/s",
+                "h2d_bytes_per_step": h2d,
+                "d2h_bytes_per_step": d2h,
+            },
+            "clocks": clocks,
+            "gpu_launches": launches_per_step * args.steps,
+            "device_status": status,
+            "per_point": per_point,
+        }
+        print(json.dumps(line), flush=True)
+    if world > 1:
+        import torch.distributed as dist
+
+        for pt in points:
+            pt.graph = None
+        dist.destroy_process_group()
+
+
+def main(argv=None) -> int:
+    ap = argparse.ArgumentParser(description=__doc__, formatter_class=argparse.RawDescriptionHelpFormatter)
+    ap.add_argument("--gpus", type=int, default=1)
+    ap.add_argument("--steps", type=int, default=10)
+    ap.add_argument("--warmup", type=int, default=3)
+    ap.add_argument("--impl", choices=["ours", "reference"], default="ours")
+    ap.add_argument("--seed", type=int, default=0)
+    ap.add_argument("--variant", default=None, help="force a kernel variant (e.g. 0x104); default: library choice")
+    ap.add_argument("--no-bf16-compare", dest="bf16_compare", action="store_false")
+    ap.add_argument("--no-cpu-baseline", action="store_true")
+    ap.add_argument("--cpu-seconds", type=float, default=15.0)
+    args = ap.parse_args(argv)
+    if args.warmup < 3:
+        print("warning: fewer than 3 warm-up steps", file=sys.stderr)
+    if args.impl == "reference":
+        run_reference_arm(args)
+    else:
+        run_gpu_arm(args)
+    return 0
+
+
+if __name__ == "__main__":
+    sys.exit(main())

@@ -1,0 +1,194 @@
+/*
+ * qtts_b200.h -- C ABI of the B200 (sm_100a) quantized-linear library.
+ *
+ * This library replaces the device code behind the `LinearBase.quant_method`
+ * hook of qtts (danielhua23/tts-inference):
+ *
+ *   - int8 weight-only GEMM/GEMV (W8A16), the Triton kernel `_w8_gemm_kernel`
+ *     and its launcher `w8_gemm` (qtts/quant/kernels.py:89-135, 138-177);
+ *   - fp8-e4m3 W8A8: the eager per-token activation quantization plus
+ *     `torch._scaled_mm` of `Fp8Method.apply` (qtts/quant/fp8.py:72-89);
+ *   - the load-time quantizers `quantize_weight_per_channel`
+ *     (qtts/quant/int8.py:45-56) and `quantize_weight_fp8`
+ *     (qtts/quant/fp8.py:45-49).
+ *
+ * Conventions shared by every entry point:
+ *   - All pointers are device pointers owned by the caller; the library never
+ *     allocates or frees device memory and never synchronizes the stream.
+ *   - Matrices are row-major with an explicit leading dimension in ELEMENTS.
+ *     Weights are [N, K] (output channel major, K contiguous), activations
+ *     [M, K], outputs [M, N].
+ *   - `stream` is a cudaStream_t (NULL = legacy default stream). Every launch
+ *     goes to that stream only, so calls are CUDA-graph capturable.
+ *   - Return value is a status code (QTTS_OK on success). Validation happens
+ *     on the host before any launch: a non-OK status means nothing was
+ *     launched. Device-side failures (an expired bounded wait) are recorded in
+ *     a per-device status word readable with qtts_device_status().
+ *   - No C++ exceptions cross this boundary.
+ */
+#ifndef QTTS_B200_H
+#define QTTS_B200_H
+
+#include <stddef.h>
+#include <stdint.h>
+
+#ifdef __cplusplus
+extern "C" {
+#endif
+
+#define QTTS_ABI_VERSION 1
+
+#if defined(__GNUC__)
+#define QTTS_API __attribute__((visibility("default")))
+#else
+#define QTTS_API
+#endif
+
+/* ---- status codes ------------------------------------------------------ */
+enum qtts_status {
+  QTTS_OK = 0,
+  QTTS_ERR_NULL = 1,    /* a required pointer is NULL                        */
+  QTTS_ERR_SHAPE = 2,   /* M/N/K/G or a leading dimension is out of range    */
+  QTTS_ERR_ALIGN = 3,   /* pointer or stride misaligned for the variant      */
+  QTTS_ERR_DTYPE = 4,   /* unsupported dtype code or dtype combination       */
+  QTTS_ERR_ARCH = 5,    /* no sm_100 device, or a driver entry point missing */
+  QTTS_ERR_LAUNCH = 6,  /* the kernel launch itself failed                   */
+  QTTS_ERR_VARIANT = 7, /* unknown variant, or not applicable to the shape   */
+  QTTS_ERR_TIMEOUT = 8, /* a device-side bounded wait expired                */
+  QTTS_ERR_CUDA = 9     /* another CUDA runtime error                        */
+};
+
+/* ---- dtype codes ------------------------------------------------------- */
+enum qtts_dtype {
+  QTTS_BF16 = 0,
+  QTTS_FP16 = 1,
+  QTTS_FP32 = 2,
+  QTTS_E4M3 = 3, /* float8_e4m3fn, one byte per element */
+  QTTS_INT8 = 4
+};
+
+/* ---- launch flags ------------------------------------------------------ */
+/* Launch with programmatic dependent launch: the kernel starts while the
+ * previous kernel of the stream drains and streams its (constant) weights in
+ * before waiting on the dependency. Activations, scales, bias and outputs are
+ * touched only after the wait. The weights must not be written by the
+ * immediately preceding kernel of the same stream. */
+#define QTTS_FLAG_PDL 0x1u
+
+/* ---- kernel variants ---------------------------------------------------- */
+/* 0 lets the library choose from (M, N, K). The others force one kernel;
+ * calibration (qtts_b200.quant.calibrate) times them per shape. */
+#define QTTS_VARIANT_AUTO 0
+#define QTTS_VARIANT_GENERIC 1 /* SIMT kernel: any shape, stride, dtype    */
+/* TMA-streamed weights + mma.sync, split-K over a thread-block cluster of
+ * `split` CTAs (1, 2, 4 or 8) reduced through distributed shared memory. */
+#define QTTS_VARIANT_SKINNY(split) (0x100 | (split))
+/* tcgen05/TMEM tile kernel (weights dequantized to bf16 in shared memory,
+ * accumulator in tensor memory), split-K over a cluster of `split` CTAs. */
+#define QTTS_VARIANT_UMMA(split) (0x200 | (split))
+
+/* ---- library information ------------------------------------------------ */
+QTTS_API int qtts_abi_version(void);
+QTTS_API const char* qtts_status_str(int status);
+
+/* Reads (and, when `reset` != 0, clears) the device-side status word of the
+ * current device. Returns QTTS_OK when no kernel has recorded a failure.
+ * This call synchronizes with the device (it copies 4 bytes). */
+QTTS_API int qtts_device_status(int reset);
+
+/* Sets the bounded-wait limit (nanoseconds) of subsequent launches on the
+ * current device; 0 restores the default of 2 s. Returns the previous
+ * limit. */
+QTTS_API uint64_t qtts_set_wait_limit_ns(uint64_t limit_ns);
+
+/* ---- int8 weight-only (W8A16) ---------------------------------------------
+ * out[m, n] = cast_out( sum_k float(x[m, k]) * float(w[n, k]) * float(scale[n])
+ *                       + float(bias[n]) )
+ * accumulated in fp32, the scale applied once after the K loop.
+ *
+ * Replaces: w8_gemm (qtts/quant/kernels.py:138-177) and _w8_gemm_kernel
+ * (qtts/quant/kernels.py:89-135).
+ *   x      [M, K] of x_dtype (BF16, FP16 or FP32), leading dimension ldx
+ *   w      [N, K] int8, leading dimension ldw
+ *   scale  [N] of scale_dtype (BF16, FP16 or FP32)
+ *   bias   [N] of x_dtype, or NULL
+ *   out    [M, N] of x_dtype, leading dimension ldo
+ * M == 0 is a no-op. The skinny and UMMA variants need K % 16 == 0, 16-byte
+ * aligned x/w rows and a BF16 or FP16 x; AUTO falls back to the SIMT kernel
+ * otherwise. */
+QTTS_API int qtts_w8a16_gemm(const void* x, int64_t ldx, int x_dtype,
+                    const int8_t* w, int64_t ldw,
+                    const void* scale, int scale_dtype,
+                    const void* bias,
+                    void* out, int64_t ldo,
+                    int M, int N, int K,
+                    int variant, unsigned flags, void* stream);
+
+/* Grouped W8A16 over G independent problems of one shape: the 15 codebook
+ * heads of the code predictor, lm_head[i] 1024->2048
+ * (qtts/models/code_predictor.py:159-161, 235), in one launch.
+ *   x     group g at x + g*group_stride_x, [M, K] with leading dim ldx
+ *   w     [G*N, K] int8, group g owns rows [g*N, (g+1)*N)
+ *   scale [G*N];  bias [G*N] or NULL
+ *   out   group g at out + g*group_stride_out, [M, N] with leading dim ldo
+ * When `group_index` (device pointer to one int64) is non-NULL, exactly one
+ * group is computed -- the one whose index is read on the device at run
+ * time -- with x and out taken WITHOUT the group offset. That is the
+ * graph-capturable "head chosen on the device" form; G then only bounds the
+ * index (an index outside [0, G) records QTTS_ERR_SHAPE on the device and
+ * writes nothing). */
+QTTS_API int qtts_w8a16_grouped_gemm(const void* x, int64_t group_stride_x, int64_t ldx, int x_dtype,
+                            const int8_t* w, int64_t ldw,
+                            const void* scale, int scale_dtype,
+                            const void* bias,
+                            void* out, int64_t group_stride_out, int64_t ldo,
+                            int G, int M, int N, int K,
+                            const int64_t* group_index,
+                            int variant, unsigned flags, void* stream);
+
+/* ---- load-time weight quantizers ------------------------------------------
+ * Symmetric per-output-channel int8, bit-exact with
+ * quantize_weight_per_channel (qtts/quant/int8.py:45-56):
+ *   scale[n] = max(max_k |float(w[n,k])|, 1e-12f) / 127
+ *   q[n,k]   = clamp(round_half_even(float(w[n,k]) / scale[n]), -127, 127)
+ * w: [N, K] of w_dtype (BF16, FP16, FP32); q: [N, K] int8 (ld = K);
+ * scale: [N] fp32. */
+QTTS_API int qtts_quantize_int8_rows(const void* w, int64_t ldw, int w_dtype,
+                            int8_t* q, float* scale, int N, int K, void* stream);
+
+/* Symmetric per-output-channel e4m3, bit-exact with quantize_weight_fp8
+ * (qtts/quant/fp8.py:45-49):
+ *   scale[n] = max(max_k |float(w[n,k])|, 1e-12f) / 448
+ *   q[n,k]   = e4m3_rne(float(w[n,k]) / scale[n])
+ * q: [N, K] e4m3 bytes (ld = K); scale: [N] fp32. */
+QTTS_API int qtts_quantize_fp8_rows(const void* w, int64_t ldw, int w_dtype,
+                           uint8_t* q, float* scale, int N, int K, void* stream);
+
+/* ---- fp8 e4m3 W8A8 ---------------------------------------------------------
+ * Per-token dynamic activation quantization, bit-exact with
+ * Fp8Method.apply (qtts/quant/fp8.py:77-78):
+ *   amax_m     = max_k |x[m,k]|                (in x_dtype, exact)
+ *   scale_x[m] = float(max(amax_m, x_dtype(1e-6))) / 448
+ *   q[m,k]     = e4m3_rne(float(x[m,k]) / scale_x[m])
+ * x: [M, K] (BF16/FP16/FP32, ld ldx); q: [M, K] e4m3 (ld = K); scale_x: [M]. */
+QTTS_API int qtts_fp8_quant_rows(const void* x, int64_t ldx, int x_dtype,
+                        uint8_t* q, float* scale_x, int M, int K,
+                        unsigned flags, void* stream);
+
+/* Scaled e4m3 GEMM, the torch._scaled_mm call of Fp8Method.apply
+ * (qtts/quant/fp8.py:79-88):
+ *   out[m,n] = cast_out( (sum_k xq[m,k] * wq[n,k]) * scale_x[m] * scale_w[n]
+ *                        + float(bias[n]) )
+ * xq: [M, K] e4m3 (ld ldxq); wq: [N, K] e4m3 (ld ldw); out: [M, N] of out_dtype
+ * (BF16/FP16/FP32) with leading dim ldo; bias [N] of out_dtype or NULL.
+ * Needs K % 16 == 0 and 16-byte aligned rows. */
+QTTS_API int qtts_fp8_gemm(const uint8_t* xq, int64_t ldxq, const float* scale_x,
+                  const uint8_t* wq, int64_t ldw, const float* scale_w,
+                  const void* bias, void* out, int64_t ldo, int out_dtype,
+                  int M, int N, int K, int variant, unsigned flags, void* stream);
+
+#ifdef __cplusplus
+}
+#endif
+
+#endif /* QTTS_B200_H */

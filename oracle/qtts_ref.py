@@ -1,0 +1,186 @@
+"""numpy restatement of the reference's quantized-linear arithmetic (test oracle).
+
+TEST INFRASTRUCTURE ONLY -- imported by tests/, __graft_entry__.smoke() and the
+CPU-baseline leg of bench.py, never by the library.
+
+Every function names the reference lines it restates (paths relative to the
+danielhua23/tts-inference checkout). Floating-point steps are done in the
+precision the reference uses, so integer outputs (int8 codes, e4m3 codes) and
+fp32 scales are bit-exact, and GEMM outputs are computed in float64 as the
+exact value the fp32-accumulating kernels approximate.
+"""
+
+from __future__ import annotations
+
+import numpy as np
+
+_F32 = np.float32
+
+# ----------------------------------------------------------------------------
+# 16-bit and 8-bit float formats
+
+
+def bf16_round(a) -> np.ndarray:
+    """float32 -> nearest bf16 (round half to even), returned as float32 values."""
+    a = np.asarray(a, dtype=np.float32)
+    bits = a.view(np.uint32).astype(np.uint64)
+    rounded = ((bits + 0x7FFF + ((bits >> 16) & 1)) & 0xFFFF0000).astype(np.uint32)
+    out = rounded.view(np.float32)
+    return np.where(np.isnan(a), a, out).astype(np.float32)
+
+
+def fp16_round(a) -> np.ndarray:
+    return np.asarray(a, dtype=np.float32).astype(np.float16).astype(np.float32)
+
+
+def round_to(a, dtype: str) -> np.ndarray:
+    if dtype == "bf16":
+        return bf16_round(a)
+    if dtype == "fp16":
+        return fp16_round(a)
+    return np.asarray(a, dtype=np.float32)
+
+
+def _e4m3_table() -> np.ndarray:
+    """Value of every float8_e4m3fn code: 1 sign, 4 exponent (bias 7), 3 mantissa bits,
+    subnormals at exponent 0, no infinities, S.1111.111 is NaN."""
+    vals = np.zeros(256, dtype=np.float64)
+    for code in range(256):
+        s = -1.0 if code & 0x80 else 1.0
+        e = (code >> 3) & 0xF
+        m = code & 0x7
+        if e == 0xF and m == 0x7:
+            vals[code] = np.nan
+        elif e == 0:
+            vals[code] = s * (m / 8.0) * 2.0**-6
+        else:
+            vals[code] = s * (1.0 + m / 8.0) * 2.0 ** (e - 7)
+    return vals
+
+
+_E4M3 = _e4m3_table()
+_E4M3_POS = _E4M3[:127]  # codes 0..126: 0 .. 448 ascending
+
+
+def e4m3_decode(codes) -> np.ndarray:
+    return _E4M3[np.asarray(codes, dtype=np.uint8)].astype(np.float32)
+
+
+def e4m3_encode(v) -> np.ndarray:
+    """float32 -> float8_e4m3fn codes, round to nearest even.
+
+    Magnitudes of 464 and above (half-way to the NaN code and beyond) give NaN,
+    as torch's non-saturating cast does; the quantizers never produce them.
+    """
+    v = np.asarray(v, dtype=np.float32).astype(np.float64)
+    mag = np.abs(v)
+    hi = np.clip(np.searchsorted(_E4M3_POS, mag, side="left"), 0, 126)
+    lo = np.clip(hi - 1, 0, 126)
+    d_hi = np.abs(_E4M3_POS[hi] - mag)
+    d_lo = np.abs(mag - _E4M3_POS[lo])
+    pick_hi = (d_hi < d_lo) | ((d_hi == d_lo) & (hi % 2 == 0))
+    code = np.where(pick_hi, hi, lo).astype(np.uint8)
+    code = np.where(mag >= 464.0, np.uint8(0x7F), code)
+    code = np.where(np.isnan(mag), np.uint8(0x7F), code)
+    sign = np.signbit(v).astype(np.uint8) << 7
+    return (code | sign).astype(np.uint8)
+
+
+# ----------------------------------------------------------------------------
+# Weight quantizers
+
+
+def quantize_weight_per_channel(weight) -> tuple[np.ndarray, np.ndarray]:
+    """qtts/quant/int8.py:45-56 -- symmetric per-output-channel int8.
+
+    fp32 throughout: scale = max(rowabsmax, 1e-12) / 127, q = clamp(round(w /
+    scale), -127, 127) with round half to even (torch.round).
+    """
+    w = np.asarray(weight, dtype=np.float32)
+    amax = np.abs(w).max(axis=1)
+    scale = (np.maximum(amax, _F32(1e-12)) / _F32(127.0)).astype(np.float32)
+    q = np.clip(np.rint(w / scale[:, None]), -127, 127).astype(np.int8)
+    return q, scale
+
+
+def tune_quantize(weight_bf16) -> tuple[np.ndarray, np.ndarray]:
+    """examples/kernels/tune_w8_gemm.py:82-85 -- the tuning script's quantizer.
+
+    scale = bf16(amax / 127) (no 1e-12 floor), packed = round(w / float(scale)).
+    """
+    w = np.asarray(weight_bf16, dtype=np.float32)
+    scale = bf16_round(np.abs(w).max(axis=1) / _F32(127.0))
+    q = np.clip(np.rint(w / scale[:, None]), -127, 127).astype(np.int8)
+    return q, scale
+
+
+def quantize_weight_fp8(weight) -> tuple[np.ndarray, np.ndarray]:
+    """qtts/quant/fp8.py:45-49 -- per-output-channel e4m3, scale = max(amax, 1e-12) / 448."""
+    w = np.asarray(weight, dtype=np.float32)
+    amax = np.abs(w).max(axis=1)
+    scale = (np.maximum(amax, _F32(1e-12)) / _F32(448.0)).astype(np.float32)
+    return e4m3_encode(w / scale[:, None]), scale
+
+
+def quantize_act_fp8(x, dtype: str = "bf16") -> tuple[np.ndarray, np.ndarray]:
+    """qtts/quant/fp8.py:77-78 -- per-token dynamic activation quantization.
+
+    amax in the activation dtype (exact), clamp_min(1e-6) in that dtype (the
+    bound is 1e-6 rounded to it), then ``.float() / 448`` and the e4m3 cast of
+    ``x.float() / scale``.
+    """
+    xv = np.asarray(x, dtype=np.float32)
+    amax = np.abs(xv).max(axis=1)
+    floor = round_to(np.array([1e-6], dtype=np.float32), dtype)[0]
+    scale = (np.maximum(amax, floor) / _F32(448.0)).astype(np.float32)
+    return e4m3_encode(xv / scale[:, None]), scale
+
+
+# ----------------------------------------------------------------------------
+# GEMMs
+
+
+def w8a16_reference(x, q, scale, bias=None) -> np.ndarray:
+    """The fused kernel's math (qtts/quant/kernels.py:114-135) in float64.
+
+    ``x`` holds the activation values (already representable in their dtype),
+    ``q`` the int8 weight, ``scale`` the per-channel scale values (as stored,
+    e.g. bf16-rounded). acc = x @ q.T; out = acc * scale (+ bias).
+    """
+    acc = np.asarray(x, dtype=np.float64) @ np.asarray(q, dtype=np.float64).T
+    out = acc * np.asarray(scale, dtype=np.float64)[None, :]
+    if bias is not None:
+        out = out + np.asarray(bias, dtype=np.float64)[None, :]
+    return out
+
+
+def naive_dequant_linear(x_bf16, q, scale_bf16) -> np.ndarray:
+    """examples/kernels/tune_w8_gemm.py:73-79 -- the reference's eager path.
+
+    ``F.linear(x, q.to(bf16) * scale[:, None])``: the dequantized weight is
+    rounded to bf16, the product accumulated in fp32 and rounded to bf16.
+    """
+    w = bf16_round(np.asarray(q, dtype=np.float32) * np.asarray(scale_bf16, dtype=np.float32)[:, None])
+    acc = np.asarray(x_bf16, dtype=np.float32) @ w.T
+    return bf16_round(acc)
+
+
+def fp8_scaled_mm_reference(xq, scale_x, wq, scale_w, bias=None) -> np.ndarray:
+    """qtts/quant/fp8.py:79-88 -- ``_scaled_mm(q, W.t(), scale_a, scale_b) + bias`` in float64."""
+    a = e4m3_decode(xq).astype(np.float64)
+    b = e4m3_decode(wq).astype(np.float64)
+    out = (a @ b.T) * np.asarray(scale_x, dtype=np.float64).reshape(-1, 1)
+    out = out * np.asarray(scale_w, dtype=np.float64).reshape(1, -1)
+    if bias is not None:
+        out = out + np.asarray(bias, dtype=np.float64)[None, :]
+    return out
+
+
+def rel_err(out, ref) -> float:
+    """examples/kernels/tune_w8_gemm.py:121 -- max|out - ref| / max|ref|."""
+    out = np.asarray(out, dtype=np.float64)
+    ref = np.asarray(ref, dtype=np.float64)
+    denom = np.abs(ref).max()
+    if denom == 0:
+        return float(np.abs(out - ref).max())
+    return float(np.abs(out - ref).max() / denom)

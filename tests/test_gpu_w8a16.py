@@ -1,0 +1,305 @@
+"""Parity of the sm_100a W8A16 kernels with the CPU oracle, through the C ABI.
+
+Bar (north star): max|out - ref| / max|ref| <= 1e-2 against the reference's
+eager dequantize-then-matmul on the same seeded inputs. The kernels are held
+to a tighter, elementwise bar as well: against the float64 value of the fused
+math (int8 weight, per-channel scale after an fp32 K loop,
+qtts/quant/kernels.py:114-135) every output is within one bf16 rounding of
+the exact value plus 1e-3 of max|ref| for the fp32 summation order.
+"""
+
+from __future__ import annotations
+
+import numpy as np
+import pytest
+import torch
+
+import oracle
+from conftest import require_b200
+from qtts_b200 import _native as nat
+from qtts_b200.quant import kernels as qk
+
+pytestmark = pytest.mark.gpu
+
+SHAPES = [("qkv", 4096, 2048), ("o_proj", 2048, 2048), ("gate_up", 12288, 2048), ("down_proj", 2048, 6144)]
+ROWS = (1, 2, 3, 4, 5, 8, 9, 16, 17, 32, 33, 64)
+
+
+@pytest.fixture(scope="module", autouse=True)
+def _device():
+    require_b200()
+    nat.device_status(reset=True)
+    yield
+    torch.cuda.synchronize()
+    assert nat.device_status() == 0, "a kernel recorded a device-side failure"
+
+
+def seeded_case(n, k, m, seed=0, x_dtype=torch.bfloat16):
+    """Seeded CPU tensors: W ~ N(0, 0.02) quantized per row, x ~ N(0, 1)."""
+    g = torch.Generator().manual_seed(seed)
+    w = torch.randn(n, k, generator=g) * 0.02
+    x = torch.randn(m, k, generator=g).to(x_dtype)
+    q, s = oracle.quantize_weight_per_channel(w.numpy())
+    return x, q, s
+
+
+def to_dev(x, q, s, scale_dtype=torch.bfloat16):
+    return (
+        x.cuda(),
+        torch.from_numpy(q).cuda(),
+        torch.from_numpy(s).to(scale_dtype).cuda(),
+    )
+
+
+def scale_values(s, scale_dtype):
+    return torch.from_numpy(s).to(scale_dtype).float().numpy()
+
+
+def assert_close_to_oracle(out, ref, what=""):
+    out = out.float().cpu().numpy().astype(np.float64)
+    err = oracle.rel_err(out, ref)
+    assert err <= 1e-2, f"{what}: rel err {err:.3e}"
+    bound = np.abs(ref) * 2.0**-8 + 1e-3 * np.abs(ref).max() + 1e-30
+    bad = np.abs(out - ref) > bound
+    assert not bad.any(), f"{what}: {bad.sum()} elements beyond one bf16 step (rel err {err:.3e})"
+    return err
+
+
+@pytest.mark.parametrize("label,n,k", SHAPES)
+def test_talker_shapes_all_rows(label, n, k):
+    x, q, s = seeded_case(n, k, max(ROWS))
+    ref_all = oracle.w8a16_reference(x.float().numpy(), q, scale_values(s, torch.bfloat16))
+    xd, qd, sd = to_dev(x, q, s)
+    for m in ROWS:
+        out = qk.w8_gemm(xd[:m], qd, sd)
+        assert out.shape == (m, n) and out.dtype == torch.bfloat16
+        assert_close_to_oracle(out, ref_all[:m], f"{label} M={m}")
+
+
+@pytest.mark.parametrize("label,n,k", SHAPES)
+def test_matches_reference_eager_path(label, n, k):
+    # The north-star check: the reference's eager dequant-then-matmul
+    # (examples/kernels/tune_w8_gemm.py:73-79) on the same inputs, <= 1e-2.
+    x, q, s = seeded_case(n, k, 4, seed=1)
+    s_bf16 = scale_values(s, torch.bfloat16)
+    naive = oracle.naive_dequant_linear(x.float().numpy(), q, s_bf16)
+    out = qk.w8_gemm(*to_dev(x, q, s))
+    assert oracle.rel_err(out.float().cpu().numpy(), naive) <= 1e-2
+
+
+@pytest.mark.parametrize("variant", ["skinny1", "skinny2", "skinny4", "skinny8", "generic"])
+@pytest.mark.parametrize("m", [1, 8, 16, 64])
+def test_every_variant_agrees(variant, m):
+    n, k = 2048, 6144
+    x, q, s = seeded_case(n, k, m, seed=2)
+    ref = oracle.w8a16_reference(x.float().numpy(), q, scale_values(s, torch.bfloat16))
+    v = nat.VARIANT_GENERIC if variant == "generic" else nat.variant_skinny(int(variant[-1]))
+    out = qk.w8_gemm(*to_dev(x, q, s), variant=v)
+    assert_close_to_oracle(out, ref, f"{variant} M={m}")
+
+
+@pytest.mark.parametrize(
+    "n,k,m",
+    [(80, 272, 3), (64, 128, 1), (65, 144, 7), (1000, 3072, 12), (2048, 1024, 65), (2048, 1024, 100),
+     (300, 2048, 130), (7, 40, 2), (33, 1000, 5), (1, 16, 1)],
+)
+def test_ragged_shapes(n, k, m):
+    x, q, s = seeded_case(n, k, m, seed=3)
+    ref = oracle.w8a16_reference(x.float().numpy(), q, scale_values(s, torch.bfloat16))
+    out = qk.w8_gemm(*to_dev(x, q, s))
+    assert_close_to_oracle(out, ref, f"N={n} K={k} M={m}")
+
+
+def test_forced_skinny_rejects_unaligned_k():
+    x, q, s = seeded_case(8, 40, 2)
+    with pytest.raises(RuntimeError, match="misaligned"):
+        qk.w8_gemm(*to_dev(x, q, s), variant=nat.variant_skinny(1))
+
+
+@pytest.mark.parametrize("x_dtype", [torch.bfloat16, torch.float16, torch.float32])
+@pytest.mark.parametrize("scale_dtype", [torch.bfloat16, torch.float32, torch.float16])
+def test_dtypes_and_bias(x_dtype, scale_dtype):
+    n, k, m = 1024, 2048, 6
+    x, q, s = seeded_case(n, k, m, seed=4, x_dtype=x_dtype)
+    g = torch.Generator().manual_seed(9)
+    bias = torch.randn(n, generator=g).to(x_dtype)
+    ref = oracle.w8a16_reference(x.float().numpy(), q, scale_values(s, scale_dtype), bias.float().numpy())
+    xd, qd, sd = to_dev(x, q, s, scale_dtype)
+    out = qk.w8_gemm(xd, qd, sd, bias.cuda())
+    assert out.dtype == x_dtype
+    err = oracle.rel_err(out.float().cpu().numpy(), ref)
+    assert err <= (1e-2 if x_dtype == torch.bfloat16 else 2e-3)
+
+
+def test_strided_activations_and_batch_dims():
+    n, k = 1024, 2048
+    x, q, s = seeded_case(n, k, 6, seed=5)
+    ref = oracle.w8a16_reference(x.float().numpy(), q, scale_values(s, torch.bfloat16))
+    xd, qd, sd = to_dev(x, q, s)
+    big = torch.zeros(6, k + 64, dtype=torch.bfloat16, device="cuda")
+    big[:, 32 : 32 + k] = xd
+    out = qk.w8_gemm(big[:, 32 : 32 + k], qd, sd)  # ldx = k + 64, 64-byte offset
+    assert_close_to_oracle(out, ref, "strided")
+    out3 = qk.w8_gemm(xd.reshape(2, 3, k), qd, sd)
+    assert out3.shape == (2, 3, n)
+    assert_close_to_oracle(out3.reshape(6, n), ref, "3-D")
+
+
+def test_output_canaries_untouched():
+    n, k, m = 2048, 2048, 5
+    x, q, s = seeded_case(n, k, m, seed=6)
+    xd, qd, sd = to_dev(x, q, s)
+    buf = torch.full((m + 2, n + 64), 7.0, dtype=torch.bfloat16, device="cuda")
+    view = buf[1 : m + 1, :n]
+    qk.w8_gemm(xd, qd, sd, out=view)
+    torch.cuda.synchronize()
+    assert buf[0].eq(7).all() and buf[m + 1].eq(7).all() and buf[1 : m + 1, n:].eq(7).all()
+    ref = oracle.w8a16_reference(x.float().numpy(), q, scale_values(s, torch.bfloat16))
+    assert_close_to_oracle(view, ref, "canary")
+
+
+def test_empty_and_deterministic():
+    n, k = 2048, 2048
+    x, q, s = seeded_case(n, k, 8, seed=7)
+    xd, qd, sd = to_dev(x, q, s)
+    assert qk.w8_gemm(xd[:0], qd, sd).shape == (0, n)
+    a = qk.w8_gemm(xd, qd, sd)
+    b = qk.w8_gemm(xd, qd, sd)
+    assert torch.equal(a, b)
+
+
+def test_cuda_graph_capture_and_replay():
+    n, k, m = 4096, 2048, 8
+    x, q, s = seeded_case(n, k, m, seed=8)
+    xd, qd, sd = to_dev(x, q, s)
+    static_x = xd.clone()
+    side = torch.cuda.Stream()
+    side.wait_stream(torch.cuda.current_stream())
+    with torch.cuda.stream(side):
+        qk.w8_gemm(static_x, qd, sd)
+    torch.cuda.current_stream().wait_stream(side)
+    graph = torch.cuda.CUDAGraph()
+    with torch.cuda.graph(graph):
+        static_out = qk.w8_gemm(static_x, qd, sd)
+    for seed in (11, 12):
+        g = torch.Generator().manual_seed(seed)
+        xn = torch.randn(m, k, generator=g).to(torch.bfloat16)
+        static_x.copy_(xn.cuda())
+        graph.replay()
+        torch.cuda.synchronize()
+        ref = oracle.w8a16_reference(xn.float().numpy(), q, scale_values(s, torch.bfloat16))
+        assert_close_to_oracle(static_out, ref, f"graph replay {seed}")
+
+
+@pytest.mark.parametrize("in_graph", [False, True])
+def test_pdl_chain_respects_dependencies(in_graph):
+    # Each GEMM consumes the previous one's output. The weights are streamed
+    # before the dependency wait; the activations must not be. Each step is
+    # checked against the oracle applied to the GPU's own previous output.
+    k = 2048
+    steps = 8
+    ws = [seeded_case(k, k, 1, seed=20 + i)[1:] for i in range(steps)]
+    wd = [(torch.from_numpy(q).cuda(), torch.from_numpy(s).to(torch.bfloat16).cuda()) for q, s in ws]
+    x0 = torch.randn(4, k, generator=torch.Generator().manual_seed(30)).to(torch.bfloat16).cuda()
+
+    def chain(x):
+        outs = []
+        for qd, sd in wd:
+            x = qk.w8_gemm(x, qd, sd)
+            x = -x  # a torch kernel in between (exact in bf16)
+            outs.append(x)
+            x = qk.w8_gemm(x, qd, sd)  # and a direct ours -> ours dependency
+            outs.append(x)
+        return outs
+
+    if in_graph:
+        xs = x0.clone()
+        side = torch.cuda.Stream()
+        side.wait_stream(torch.cuda.current_stream())
+        with torch.cuda.stream(side):
+            chain(xs)
+        torch.cuda.current_stream().wait_stream(side)
+        graph = torch.cuda.CUDAGraph()
+        with torch.cuda.graph(graph):
+            outs = chain(xs)
+        graph.replay()
+    else:
+        outs = chain(x0)
+    torch.cuda.synchronize()
+    prev = x0
+    for i, out in enumerate(outs):
+        q, s = ws[i // 2]
+        ref = oracle.w8a16_reference(prev.float().cpu().numpy(), q, scale_values(s, torch.bfloat16))
+        got = -out if i % 2 == 0 else out
+        assert_close_to_oracle(got, ref, f"chain step {i}")
+        prev = out
+
+
+def test_grouped_heads_one_launch():
+    groups, n, k, m = 15, 2048, 1024, 8
+    g = torch.Generator().manual_seed(40)
+    w = torch.randn(groups * n, k, generator=g) * 0.02
+    q, s = oracle.quantize_weight_per_channel(w.numpy())
+    x = torch.randn(groups, m, k, generator=g).to(torch.bfloat16)
+    out = qk.w8_grouped_gemm(x.cuda(), torch.from_numpy(q).cuda(), torch.from_numpy(s).to(torch.bfloat16).cuda())
+    sv = scale_values(s, torch.bfloat16)
+    for i in range(groups):
+        ref = oracle.w8a16_reference(x[i].float().numpy(), q[i * n : (i + 1) * n], sv[i * n : (i + 1) * n])
+        assert_close_to_oracle(out[i], ref, f"group {i}")
+
+
+def test_device_indexed_head_in_graph():
+    groups, n, k, m = 15, 2048, 1024, 8
+    g = torch.Generator().manual_seed(41)
+    w = torch.randn(groups * n, k, generator=g) * 0.02
+    q, s = oracle.quantize_weight_per_channel(w.numpy())
+    qd = torch.from_numpy(q).cuda()
+    sd = torch.from_numpy(s).to(torch.bfloat16).cuda()
+    sv = scale_values(s, torch.bfloat16)
+    x = torch.randn(m, k, generator=g).to(torch.bfloat16).cuda()
+    idx = torch.zeros(1, dtype=torch.int64, device="cuda")
+    out = torch.empty(m, n, dtype=torch.bfloat16, device="cuda")
+    qk.w8_indexed_gemm(x, qd, sd, idx, groups, out=out)
+    graph = torch.cuda.CUDAGraph()
+    with torch.cuda.graph(graph):
+        qk.w8_indexed_gemm(x, qd, sd, idx, groups, out=out)
+    for head in (0, 7, 14, 3):
+        idx.fill_(head)
+        graph.replay()
+        torch.cuda.synchronize()
+        ref = oracle.w8a16_reference(x.float().cpu().numpy(), q[head * n : (head + 1) * n], sv[head * n : (head + 1) * n])
+        assert_close_to_oracle(out, ref, f"head {head}")
+
+
+def test_device_index_out_of_range_records_status():
+    groups, n, k = 3, 64, 128
+    q = torch.zeros(groups * n, k, dtype=torch.int8, device="cuda")
+    s = torch.ones(groups * n, dtype=torch.bfloat16, device="cuda")
+    x = torch.ones(2, k, dtype=torch.bfloat16, device="cuda")
+    out = torch.full((2, n), 5.0, dtype=torch.bfloat16, device="cuda")
+    idx = torch.full((1,), 9, dtype=torch.int64, device="cuda")
+    torch.cuda.synchronize()
+    nat.device_status(reset=True)
+    qk.w8_indexed_gemm(x, q, s, idx, groups, out=out)
+    torch.cuda.synchronize()
+    assert nat.device_status(reset=True) == 2  # QTTS_ERR_SHAPE recorded on the device
+    assert out.eq(5).all()  # nothing written
+
+
+@pytest.mark.parametrize("src", ["f32", "bf16"])
+def test_int8_weight_quantizer_bit_exact(golden, src):
+    w = torch.from_numpy(golden[f"w_{src}"])
+    if src == "bf16":
+        w = w.to(torch.bfloat16)
+    q, s = qk.quantize_int8_rows(w.cuda())
+    np.testing.assert_array_equal(q.cpu().numpy(), golden[f"int8_q_{src}"])
+    np.testing.assert_array_equal(s.cpu().numpy().view(np.uint32), golden[f"int8_scale_{src}"].view(np.uint32))
+
+
+def test_int8_weight_quantizer_full_size():
+    g = torch.Generator().manual_seed(50)
+    w = torch.randn(12288, 2048, generator=g) * 0.02
+    q, s = qk.quantize_int8_rows(w.cuda())
+    qo, so = oracle.quantize_weight_per_channel(w.numpy())
+    np.testing.assert_array_equal(q.cpu().numpy(), qo)
+    np.testing.assert_array_equal(s.cpu().numpy(), so)

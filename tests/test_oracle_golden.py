@@ -1,0 +1,100 @@
+"""Pin the CPU oracle to the reference: golden vectors made by the reference's own code.
+
+The vectors come from tests/golden/make_golden.py, which runs the reference's
+``qtts.quant`` functions and tuning script. Integer and e4m3 outputs and fp32
+scales must match bit for bit; the eager bf16 GEMM within one bf16 rounding
+step (its fp32 summation order is the BLAS library's).
+"""
+
+from __future__ import annotations
+
+import numpy as np
+import pytest
+
+import oracle
+
+
+@pytest.mark.parametrize("src", ["f32", "bf16"])
+def test_int8_quantizer_bit_exact(golden, src):
+    q, s = oracle.quantize_weight_per_channel(golden[f"w_{src}"])
+    np.testing.assert_array_equal(q, golden[f"int8_q_{src}"])
+    np.testing.assert_array_equal(s.view(np.uint32), golden[f"int8_scale_{src}"].view(np.uint32))
+
+
+def test_int8_quantizer_zero_row_floor(golden):
+    q, s = oracle.quantize_weight_per_channel(golden["w_f32"])
+    assert s[7] == np.float32(1e-12) / np.float32(127.0)
+    assert not q[7].any()
+
+
+@pytest.mark.parametrize("src", ["f32", "bf16"])
+def test_fp8_weight_quantizer_bit_exact(golden, src):
+    q, s = oracle.quantize_weight_fp8(golden[f"w_{src}"])
+    np.testing.assert_array_equal(q, golden[f"fp8_q_{src}"])
+    np.testing.assert_array_equal(s.view(np.uint32), golden[f"fp8_scale_{src}"].view(np.uint32))
+
+
+@pytest.mark.parametrize("dtype", ["bf16", "fp16", "f32"])
+def test_fp8_activation_quantizer_bit_exact(golden, dtype):
+    x = golden[f"act_x_{dtype}"]
+    q, s = oracle.quantize_act_fp8(x, "fp32" if dtype == "f32" else dtype)
+    np.testing.assert_array_equal(s.view(np.uint32), golden[f"act_scale_{dtype}"].view(np.uint32))
+    np.testing.assert_array_equal(q, golden[f"act_q_{dtype}"])
+
+
+def test_tune_quantizer_bit_exact(golden):
+    q, s = oracle.tune_quantize(golden["tune_w"])
+    np.testing.assert_array_equal(q, golden["tune_q"])
+    np.testing.assert_array_equal(s.view(np.uint32), golden["tune_scale"].view(np.uint32))
+
+
+@pytest.mark.parametrize("m", [1, 3, 8])
+def test_naive_dequant_linear(golden, m):
+    y = oracle.naive_dequant_linear(golden[f"naive_x_m{m}"], golden["tune_q"], golden["tune_scale"])
+    ref = golden[f"naive_y_m{m}"]
+    # one bf16 step (2^-8 relative) of headroom for the BLAS summation order
+    np.testing.assert_allclose(y, ref, rtol=2.0**-7, atol=1e-6)
+    # and the fused-kernel math in float64 is within the reference's own error bar
+    exact = oracle.w8a16_reference(golden[f"naive_x_m{m}"], golden["tune_q"], golden["tune_scale"])
+    assert oracle.rel_err(ref, exact) < 1e-2
+
+
+def test_e4m3_table_round_trip():
+    codes = np.arange(256, dtype=np.uint8)
+    vals = oracle.e4m3_decode(codes)
+    finite = ~np.isnan(vals)
+    np.testing.assert_array_equal(oracle.e4m3_encode(vals[finite]), codes[finite])
+    assert np.nanmax(vals) == 448.0
+    assert oracle.e4m3_decode(np.array([1], dtype=np.uint8))[0] == 2.0**-9
+
+
+def test_e4m3_ties_round_to_even():
+    # 1 + 1/16 lies halfway between 1 (code 0x38, even) and 1.125 (0x39, odd)
+    assert oracle.e4m3_encode(np.array([1.0625], dtype=np.float32))[0] == 0x38
+    # 1.1875 is halfway between 1.125 (0x39) and 1.25 (0x3A, even)
+    assert oracle.e4m3_encode(np.array([1.1875], dtype=np.float32))[0] == 0x3A
+    assert oracle.e4m3_encode(np.array([-1.1875], dtype=np.float32))[0] == 0xBA
+
+
+def test_e4m3_matches_torch_cast():
+    torch = pytest.importorskip("torch")
+    rng = np.random.default_rng(1)
+    v = np.concatenate(
+        [rng.standard_normal(4096) * s for s in (1e-4, 1e-2, 1.0, 30.0, 200.0)]
+        + [np.array([0.0, -0.0, 448.0, -448.0, 2.0**-10, 3 * 2.0**-10, 447.9, 463.0])]
+    ).astype(np.float32)
+    ref = torch.from_numpy(v).to(torch.float8_e4m3fn).view(torch.uint8).numpy()
+    np.testing.assert_array_equal(oracle.e4m3_encode(v), ref)
+
+
+def test_bf16_round_matches_torch():
+    torch = pytest.importorskip("torch")
+    rng = np.random.default_rng(2)
+    v = (rng.standard_normal(10000) * 10.0 ** rng.integers(-8, 8, 10000)).astype(np.float32)
+    ref = torch.from_numpy(v).to(torch.bfloat16).float().numpy()
+    np.testing.assert_array_equal(oracle.bf16_round(v), ref)
+
+
+def test_rel_err_metric():
+    assert oracle.rel_err(np.array([1.0, 2.0]), np.array([1.0, 2.0])) == 0.0
+    assert oracle.rel_err(np.array([1.0, 2.5]), np.array([1.0, 2.0])) == pytest.approx(0.25)

@@ -1,0 +1,546 @@
+// C ABI of the library (include/qtts_b200.h): host-side validation, variant
+// dispatch and the small kernels that need no pipeline -- the SIMT fallback
+// GEMMs, the load-time weight quantizers and the per-token fp8 activation
+// quantizer.
+#include <cuda_fp8.h>
+
+#include <atomic>
+#include <mutex>
+
+#include "common.cuh"
+#include "kernels.h"
+
+namespace qtts {
+
+__device__ int g_device_status = 0;
+
+namespace {
+
+std::atomic<uint64_t> g_wait_limit_ns{2000000000ull};
+
+bool is_float_dtype(int d) { return d == QTTS_BF16 || d == QTTS_FP16 || d == QTTS_FP32; }
+size_t dtype_size(int d) {
+  switch (d) {
+    case QTTS_BF16:
+    case QTTS_FP16:
+      return 2;
+    case QTTS_FP32:
+      return 4;
+    default:
+      return 1;
+  }
+}
+bool aligned16(const void* p) { return (reinterpret_cast<uintptr_t>(p) & 15u) == 0; }
+
+// ---- device capability ------------------------------------------------------------
+int check_device() {
+  int dev = 0;
+  if (cudaGetDevice(&dev) != cudaSuccess) return QTTS_ERR_ARCH;
+  static int cc_major[64] = {0};
+  if (dev < 0 || dev >= 64) return QTTS_ERR_ARCH;
+  if (cc_major[dev] == 0) {
+    int major = 0;
+    if (cudaDeviceGetAttribute(&major, cudaDevAttrComputeCapabilityMajor, dev) != cudaSuccess) return QTTS_ERR_ARCH;
+    cc_major[dev] = major;
+  }
+  return cc_major[dev] == 10 ? QTTS_OK : QTTS_ERR_ARCH;
+}
+
+// ---- driver entry point for tensor-map encoding -------------------------------------
+typedef CUresult (*EncodeTiledFn)(CUtensorMap*, CUtensorMapDataType, cuuint32_t, void*, const cuuint64_t*,
+                                  const cuuint64_t*, const cuuint32_t*, const cuuint32_t*, CUtensorMapInterleave,
+                                  CUtensorMapSwizzle, CUtensorMapL2promotion, CUtensorMapFloatOOBfill);
+
+EncodeTiledFn get_encode_fn() {
+  static EncodeTiledFn fn = nullptr;
+  static std::once_flag once;
+  std::call_once(once, [] {
+    void* p = nullptr;
+    cudaDriverEntryPointQueryResult q;
+    if (cudaGetDriverEntryPoint("cuTensorMapEncodeTiled", &p, cudaEnableDefault, &q) == cudaSuccess &&
+        q == cudaDriverEntryPointSuccess) {
+      fn = reinterpret_cast<EncodeTiledFn>(p);
+    }
+  });
+  return fn;
+}
+
+// ---- SIMT fallback: W8A16 ---------------------------------------------------------
+// One warp per output channel and up to 8 activation rows; lanes stride K.
+struct GenericArgs {
+  const void* x;
+  int64_t ldx, gsx;
+  const int8_t* w;
+  int64_t ldw;
+  const void* scale;
+  int scale_dtype;
+  const void* bias;
+  void* out;
+  int64_t ldo, gso;
+  int M, N, K, G;
+  const int64_t* group_index;
+};
+
+template <typename XT>
+__global__ void __launch_bounds__(256) generic_w8a16_kernel(const GenericArgs a) {
+  pdl_launch_dependents();
+  pdl_wait();
+  const int warp = threadIdx.x >> 5;
+  const int lane = threadIdx.x & 31;
+  const int n = blockIdx.x * 8 + warp;
+  const int m0 = blockIdx.y * 8;
+  int group = blockIdx.z;
+  if (a.group_index != nullptr) {
+    const int64_t gi = __ldcg(a.group_index);
+    if (gi < 0 || gi >= a.G) {
+      if (threadIdx.x == 0 && blockIdx.x == 0 && blockIdx.y == 0) record_status(QTTS_ERR_SHAPE);
+      return;
+    }
+    group = static_cast<int>(gi);
+  }
+  if (n >= a.N) return;
+  const int64_t ch = static_cast<int64_t>(group) * a.N + n;
+  const int64_t goff_x = a.group_index ? 0 : static_cast<int64_t>(group) * a.gsx;
+  const int64_t goff_o = a.group_index ? 0 : static_cast<int64_t>(group) * a.gso;
+  const XT* xg = static_cast<const XT*>(a.x) + goff_x;
+  XT* og = static_cast<XT*>(a.out) + goff_o;
+  const int8_t* wr = a.w + ch * a.ldw;
+  float acc[8];
+#pragma unroll
+  for (int i = 0; i < 8; ++i) acc[i] = 0.f;
+  for (int k = lane; k < a.K; k += 32) {
+    const float wv = static_cast<float>(wr[k]);
+#pragma unroll
+    for (int i = 0; i < 8; ++i) {
+      if (m0 + i < a.M) acc[i] += to_float(xg[static_cast<int64_t>(m0 + i) * a.ldx + k]) * wv;
+    }
+  }
+#pragma unroll
+  for (int i = 0; i < 8; ++i) {
+#pragma unroll
+    for (int o = 16; o > 0; o >>= 1) acc[i] += __shfl_xor_sync(0xffffffffu, acc[i], o);
+  }
+  if (lane == 0) {
+    const float s = load_as_float(a.scale, a.scale_dtype, ch);
+    const float b = a.bias != nullptr ? to_float(static_cast<const XT*>(a.bias)[ch]) : 0.f;
+#pragma unroll
+    for (int i = 0; i < 8; ++i) {
+      if (m0 + i < a.M) og[static_cast<int64_t>(m0 + i) * a.ldo + n] = from_float<XT>(acc[i] * s + b);
+    }
+  }
+}
+
+template <typename KernT, typename ArgT>
+int launch_simple(KernT kern, dim3 grid, dim3 block, const ArgT& args, bool pdl, cudaStream_t stream) {
+  cudaLaunchConfig_t cfg = {};
+  cfg.gridDim = grid;
+  cfg.blockDim = block;
+  cfg.dynamicSmemBytes = 0;
+  cfg.stream = stream;
+  cudaLaunchAttribute attr[1];
+  if (pdl) {
+    attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+    attr[0].val.programmaticStreamSerializationAllowed = 1;
+    cfg.attrs = attr;
+    cfg.numAttrs = 1;
+  }
+  return cudaLaunchKernelEx(&cfg, kern, args) == cudaSuccess ? QTTS_OK : QTTS_ERR_LAUNCH;
+}
+
+int launch_generic_w8a16(const GenericArgs& a, int x_dtype, bool pdl, cudaStream_t stream) {
+  const int zg = a.group_index != nullptr ? 1 : a.G;
+  const dim3 grid((a.N + 7) / 8, (a.M + 7) / 8, zg);
+  if (grid.y > 65535u) return QTTS_ERR_SHAPE;
+  switch (x_dtype) {
+    case QTTS_BF16:
+      return launch_simple(generic_w8a16_kernel<__nv_bfloat16>, grid, dim3(256), a, pdl, stream);
+    case QTTS_FP16:
+      return launch_simple(generic_w8a16_kernel<__half>, grid, dim3(256), a, pdl, stream);
+    case QTTS_FP32:
+      return launch_simple(generic_w8a16_kernel<float>, grid, dim3(256), a, pdl, stream);
+    default:
+      return QTTS_ERR_DTYPE;
+  }
+}
+
+// ---- SIMT fallback: fp8 scaled GEMM --------------------------------------------------
+struct GenericFp8Args {
+  const uint8_t* xq;
+  int64_t ldxq;
+  const float* scale_x;
+  const uint8_t* wq;
+  int64_t ldw;
+  const float* scale_w;
+  const void* bias;
+  void* out;
+  int64_t ldo;
+  int M, N, K;
+};
+
+__device__ __forceinline__ float e4m3_to_float(uint8_t v) {
+  const __half_raw h = __nv_cvt_fp8_to_halfraw(static_cast<__nv_fp8_storage_t>(v), __NV_E4M3);
+  return __half2float(__half(h));
+}
+
+template <typename OT>
+__global__ void __launch_bounds__(256) generic_fp8_kernel(const GenericFp8Args a) {
+  pdl_launch_dependents();
+  pdl_wait();
+  const int warp = threadIdx.x >> 5;
+  const int lane = threadIdx.x & 31;
+  const int n = blockIdx.x * 8 + warp;
+  const int m0 = blockIdx.y * 8;
+  if (n >= a.N) return;
+  const uint8_t* wr = a.wq + static_cast<int64_t>(n) * a.ldw;
+  float acc[8];
+#pragma unroll
+  for (int i = 0; i < 8; ++i) acc[i] = 0.f;
+  for (int k = lane; k < a.K; k += 32) {
+    const float wv = e4m3_to_float(wr[k]);
+#pragma unroll
+    for (int i = 0; i < 8; ++i) {
+      if (m0 + i < a.M) acc[i] += e4m3_to_float(a.xq[static_cast<int64_t>(m0 + i) * a.ldxq + k]) * wv;
+    }
+  }
+#pragma unroll
+  for (int i = 0; i < 8; ++i) {
+#pragma unroll
+    for (int o = 16; o > 0; o >>= 1) acc[i] += __shfl_xor_sync(0xffffffffu, acc[i], o);
+  }
+  if (lane == 0) {
+    const float sw = a.scale_w[n];
+    const float b = a.bias != nullptr ? to_float(static_cast<const OT*>(a.bias)[n]) : 0.f;
+    OT* o = static_cast<OT*>(a.out);
+#pragma unroll
+    for (int i = 0; i < 8; ++i) {
+      if (m0 + i < a.M) {
+        o[static_cast<int64_t>(m0 + i) * a.ldo + n] = from_float<OT>(acc[i] * a.scale_x[m0 + i] * sw + b);
+      }
+    }
+  }
+}
+
+// ---- row quantizers ---------------------------------------------------------------------
+template <typename T>
+__device__ __forceinline__ float ld_elem(const void* p, int64_t i) {
+  return to_float(static_cast<const T*>(p)[i]);
+}
+
+__device__ __forceinline__ float block_max_256(float v, float* sh) {
+#pragma unroll
+  for (int o = 16; o > 0; o >>= 1) v = fmaxf(v, __shfl_xor_sync(0xffffffffu, v, o));
+  const int warp = threadIdx.x >> 5;
+  if ((threadIdx.x & 31) == 0) sh[warp] = v;
+  __syncthreads();
+  float r = sh[0];
+#pragma unroll
+  for (int i = 1; i < 8; ++i) r = fmaxf(r, sh[i]);
+  __syncthreads();
+  return r;
+}
+
+// mode 0: int8 (quant/int8.py:45-56), mode 1: e4m3 weights (quant/fp8.py:45-49).
+template <typename T>
+__global__ void __launch_bounds__(256) quantize_rows_kernel(const void* w, int64_t ldw, void* q, float* scale,
+                                                            int N, int K, int mode) {
+  __shared__ float sh[8];
+  pdl_launch_dependents();
+  pdl_wait();
+  const int n = blockIdx.x;
+  const int64_t row = static_cast<int64_t>(n) * ldw;
+  float amax = 0.f;
+  for (int k = threadIdx.x; k < K; k += 256) amax = fmaxf(amax, fabsf(ld_elem<T>(w, row + k)));
+  amax = block_max_256(amax, sh);
+  const float s = fmaxf(amax, 1e-12f) / (mode == 0 ? 127.0f : 448.0f);
+  if (threadIdx.x == 0) scale[n] = s;
+  const int64_t qrow = static_cast<int64_t>(n) * K;
+  for (int k = threadIdx.x; k < K; k += 256) {
+    const float v = ld_elem<T>(w, row + k) / s;
+    if (mode == 0) {
+      const float r = fminf(fmaxf(rintf(v), -127.0f), 127.0f);
+      static_cast<int8_t*>(q)[qrow + k] = static_cast<int8_t>(r);
+    } else {
+      static_cast<uint8_t*>(q)[qrow + k] =
+          static_cast<uint8_t>(__nv_cvt_float_to_fp8(v, __NV_SATFINITE, __NV_E4M3));
+    }
+  }
+}
+
+// Per-token activation quantization (quant/fp8.py:77-78). The amax and the
+// clamp happen in the activation dtype (exact for a max), the division in fp32.
+template <typename T>
+__global__ void __launch_bounds__(256) fp8_quant_rows_kernel(const void* x, int64_t ldx, uint8_t* q, float* scale_x,
+                                                             int M, int K) {
+  __shared__ float sh[8];
+  pdl_launch_dependents();
+  pdl_wait();
+  const int m = blockIdx.x;
+  const int64_t row = static_cast<int64_t>(m) * ldx;
+  float amax = 0.f;
+  for (int k = threadIdx.x; k < K; k += 256) amax = fmaxf(amax, fabsf(ld_elem<T>(x, row + k)));
+  amax = block_max_256(amax, sh);
+  // clamp_min(1e-6) in the activation dtype: the bound is 1e-6 rounded to T.
+  const float floor_t = to_float(from_float<T>(1e-6f));
+  const float s = fmaxf(amax, floor_t) / 448.0f;
+  if (threadIdx.x == 0) scale_x[m] = s;
+  const int64_t qrow = static_cast<int64_t>(m) * K;
+  for (int k = threadIdx.x; k < K; k += 256) {
+    const float v = ld_elem<T>(x, row + k) / s;
+    q[qrow + k] = static_cast<uint8_t>(__nv_cvt_float_to_fp8(v, __NV_SATFINITE, __NV_E4M3));
+  }
+}
+
+}  // namespace
+
+uint64_t current_wait_limit_ns() { return g_wait_limit_ns.load(std::memory_order_relaxed); }
+
+int make_tmap_u8_2d(CUtensorMap* map, const void* base, uint64_t rows, uint64_t cols, uint64_t pitch_bytes,
+                    uint32_t box_rows, uint32_t box_cols) {
+  EncodeTiledFn fn = get_encode_fn();
+  if (fn == nullptr) return QTTS_ERR_ARCH;
+  const cuuint64_t dims[2] = {cols, rows};
+  const cuuint64_t strides[1] = {pitch_bytes};
+  const cuuint32_t box[2] = {box_cols, box_rows};
+  const cuuint32_t estr[2] = {1, 1};
+  const CUresult r = fn(map, CU_TENSOR_MAP_DATA_TYPE_UINT8, 2, const_cast<void*>(base), dims, strides, box, estr,
+                        CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B,
+                        CU_TENSOR_MAP_L2_PROMOTION_L2_256B, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
+  return r == CUDA_SUCCESS ? QTTS_OK : QTTS_ERR_ALIGN;
+}
+
+}  // namespace qtts
+
+using namespace qtts;
+
+// ======================================================================================
+// Exported C ABI
+// ======================================================================================
+
+extern "C" {
+
+int qtts_abi_version(void) { return QTTS_ABI_VERSION; }
+
+const char* qtts_status_str(int status) {
+  switch (status) {
+    case QTTS_OK:
+      return "ok";
+    case QTTS_ERR_NULL:
+      return "a required pointer is null";
+    case QTTS_ERR_SHAPE:
+      return "shape or leading dimension out of range";
+    case QTTS_ERR_ALIGN:
+      return "pointer or stride misaligned for the requested kernel";
+    case QTTS_ERR_DTYPE:
+      return "unsupported dtype";
+    case QTTS_ERR_ARCH:
+      return "no sm_100 device or missing driver entry point";
+    case QTTS_ERR_LAUNCH:
+      return "kernel launch failed";
+    case QTTS_ERR_VARIANT:
+      return "unknown or inapplicable kernel variant";
+    case QTTS_ERR_TIMEOUT:
+      return "device-side bounded wait expired";
+    case QTTS_ERR_CUDA:
+      return "CUDA runtime error";
+    default:
+      return "unknown status";
+  }
+}
+
+int qtts_device_status(int reset) {
+  int v = 0;
+  if (cudaMemcpyFromSymbol(&v, g_device_status, sizeof(int)) != cudaSuccess) return QTTS_ERR_CUDA;
+  if (reset) {
+    const int zero = 0;
+    if (cudaMemcpyToSymbol(g_device_status, &zero, sizeof(int)) != cudaSuccess) return QTTS_ERR_CUDA;
+  }
+  return v;
+}
+
+uint64_t qtts_set_wait_limit_ns(uint64_t limit_ns) {
+  return g_wait_limit_ns.exchange(limit_ns == 0 ? 2000000000ull : limit_ns);
+}
+
+static int w8a16_dispatch(const void* x, int64_t gsx, int64_t ldx, int x_dtype, const int8_t* w, int64_t ldw,
+                          const void* scale, int scale_dtype, const void* bias, void* out, int64_t gso,
+                          int64_t ldo, int G, int M, int N, int K, const int64_t* group_index, int variant,
+                          unsigned flags, void* stream_ptr) {
+  if (M < 0 || N < 0 || K < 0 || G < 1) return QTTS_ERR_SHAPE;
+  if (M == 0 || N == 0) return QTTS_OK;
+  if (x == nullptr || w == nullptr || scale == nullptr || out == nullptr) return QTTS_ERR_NULL;
+  if (!is_float_dtype(x_dtype) || !is_float_dtype(scale_dtype)) return QTTS_ERR_DTYPE;
+  if (ldx < K || ldw < K || ldo < N) return QTTS_ERR_SHAPE;
+  if (G > 1 && group_index == nullptr && (gsx < static_cast<int64_t>(M) * ldx || gso < static_cast<int64_t>(M) * ldo))
+    return QTTS_ERR_SHAPE;
+  const int dev_ok = check_device();
+  if (dev_ok != QTTS_OK) return dev_ok;
+  cudaStream_t stream = static_cast<cudaStream_t>(stream_ptr);
+  const bool pdl = (flags & QTTS_FLAG_PDL) != 0;
+  const size_t xs = dtype_size(x_dtype);
+
+  const bool skinny_ok = (x_dtype == QTTS_BF16 || x_dtype == QTTS_FP16) && K % 16 == 0 && K > 0 && aligned16(x) &&
+                         aligned16(w) && (ldx * xs) % 16 == 0 && (gsx * xs) % 16 == 0 && ldw % 16 == 0;
+  int family = variant & 0xF00;
+  int split = variant & 0xFF;
+  if (variant == QTTS_VARIANT_AUTO) {
+    family = skinny_ok ? 0x100 : 0;
+    split = 0;
+  }
+  if (variant == QTTS_VARIANT_GENERIC || family == 0) {
+    if (variant != QTTS_VARIANT_AUTO && variant != QTTS_VARIANT_GENERIC) return QTTS_ERR_VARIANT;
+    GenericArgs ga{x, ldx, gsx, w, ldw, scale, scale_dtype, bias, out, ldo, gso, M, N, K, G, group_index};
+    return launch_generic_w8a16(ga, x_dtype, pdl, stream);
+  }
+  if (family == 0x100) {
+    if (!skinny_ok) return QTTS_ERR_ALIGN;
+    if (!(split == 0 || split == 1 || split == 2 || split == 4 || split == 8)) return QTTS_ERR_VARIANT;
+    const int zg = group_index != nullptr ? 1 : G;
+    const SkinnyPlan plan = plan_skinny(M, N, K, zg, split);
+    if (plan.grid.z > 65535u) return QTTS_ERR_SHAPE;
+    CUtensorMap map;
+    const uint64_t rows = static_cast<uint64_t>(G) * N;
+    const int r = make_tmap_u8_2d(&map, w, rows, static_cast<uint64_t>(K), static_cast<uint64_t>(ldw), 64, 128);
+    if (r != QTTS_OK) return r;
+    SkinnyArgs sa{};
+    sa.x = x;
+    sa.ldx = ldx;
+    sa.gsx = gsx;
+    sa.scale = scale;
+    sa.scale_dtype = scale_dtype;
+    sa.bias = bias;
+    sa.out = out;
+    sa.ldo = ldo;
+    sa.gso = gso;
+    sa.M = M;
+    sa.N = N;
+    sa.K = K;
+    sa.G = G;
+    sa.k_per_cta = plan.k_per_cta;
+    sa.stages = plan.stages;
+    sa.x_pitch = plan.x_pitch;
+    sa.m_chunks = plan.m_chunks;
+    sa.group_index = group_index;
+    sa.wait_ns = current_wait_limit_ns();
+    return launch_skinny_w8a16(plan, map, sa, x_dtype, pdl, stream);
+  }
+  return QTTS_ERR_VARIANT;
+}
+
+int qtts_w8a16_gemm(const void* x, int64_t ldx, int x_dtype, const int8_t* w, int64_t ldw, const void* scale,
+                    int scale_dtype, const void* bias, void* out, int64_t ldo, int M, int N, int K, int variant,
+                    unsigned flags, void* stream) {
+  return w8a16_dispatch(x, 0, ldx, x_dtype, w, ldw, scale, scale_dtype, bias, out, 0, ldo, 1, M, N, K, nullptr,
+                        variant, flags, stream);
+}
+
+int qtts_w8a16_grouped_gemm(const void* x, int64_t group_stride_x, int64_t ldx, int x_dtype, const int8_t* w,
+                            int64_t ldw, const void* scale, int scale_dtype, const void* bias, void* out,
+                            int64_t group_stride_out, int64_t ldo, int G, int M, int N, int K,
+                            const int64_t* group_index, int variant, unsigned flags, void* stream) {
+  return w8a16_dispatch(x, group_stride_x, ldx, x_dtype, w, ldw, scale, scale_dtype, bias, out, group_stride_out,
+                        ldo, G, M, N, K, group_index, variant, flags, stream);
+}
+
+static int quantize_rows(const void* w, int64_t ldw, int w_dtype, void* q, float* scale, int N, int K, int mode,
+                         void* stream) {
+  if (N < 0 || K < 0) return QTTS_ERR_SHAPE;
+  if (N == 0) return QTTS_OK;
+  if (w == nullptr || q == nullptr || scale == nullptr) return QTTS_ERR_NULL;
+  if (ldw < K) return QTTS_ERR_SHAPE;
+  const int dev_ok = check_device();
+  if (dev_ok != QTTS_OK) return dev_ok;
+  cudaStream_t s = static_cast<cudaStream_t>(stream);
+  const dim3 grid(N), block(256);
+  switch (w_dtype) {
+    case QTTS_BF16:
+      quantize_rows_kernel<__nv_bfloat16><<<grid, block, 0, s>>>(w, ldw, q, scale, N, K, mode);
+      break;
+    case QTTS_FP16:
+      quantize_rows_kernel<__half><<<grid, block, 0, s>>>(w, ldw, q, scale, N, K, mode);
+      break;
+    case QTTS_FP32:
+      quantize_rows_kernel<float><<<grid, block, 0, s>>>(w, ldw, q, scale, N, K, mode);
+      break;
+    default:
+      return QTTS_ERR_DTYPE;
+  }
+  return cudaGetLastError() == cudaSuccess ? QTTS_OK : QTTS_ERR_LAUNCH;
+}
+
+int qtts_quantize_int8_rows(const void* w, int64_t ldw, int w_dtype, int8_t* q, float* scale, int N, int K,
+                            void* stream) {
+  return quantize_rows(w, ldw, w_dtype, q, scale, N, K, 0, stream);
+}
+
+int qtts_quantize_fp8_rows(const void* w, int64_t ldw, int w_dtype, uint8_t* q, float* scale, int N, int K,
+                           void* stream) {
+  return quantize_rows(w, ldw, w_dtype, q, scale, N, K, 1, stream);
+}
+
+int qtts_fp8_quant_rows(const void* x, int64_t ldx, int x_dtype, uint8_t* q, float* scale_x, int M, int K,
+                        unsigned flags, void* stream) {
+  if (M < 0 || K < 0) return QTTS_ERR_SHAPE;
+  if (M == 0) return QTTS_OK;
+  if (x == nullptr || q == nullptr || scale_x == nullptr) return QTTS_ERR_NULL;
+  if (ldx < K) return QTTS_ERR_SHAPE;
+  const int dev_ok = check_device();
+  if (dev_ok != QTTS_OK) return dev_ok;
+  cudaStream_t s = static_cast<cudaStream_t>(stream);
+  const bool pdl = (flags & QTTS_FLAG_PDL) != 0;
+  const dim3 grid(M), block(256);
+  cudaLaunchConfig_t cfg = {};
+  cfg.gridDim = grid;
+  cfg.blockDim = block;
+  cfg.stream = s;
+  cudaLaunchAttribute attr[1];
+  if (pdl) {
+    attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+    attr[0].val.programmaticStreamSerializationAllowed = 1;
+    cfg.attrs = attr;
+    cfg.numAttrs = 1;
+  }
+  cudaError_t e;
+  switch (x_dtype) {
+    case QTTS_BF16:
+      e = cudaLaunchKernelEx(&cfg, fp8_quant_rows_kernel<__nv_bfloat16>, x, ldx, q, scale_x, M, K);
+      break;
+    case QTTS_FP16:
+      e = cudaLaunchKernelEx(&cfg, fp8_quant_rows_kernel<__half>, x, ldx, q, scale_x, M, K);
+      break;
+    case QTTS_FP32:
+      e = cudaLaunchKernelEx(&cfg, fp8_quant_rows_kernel<float>, x, ldx, q, scale_x, M, K);
+      break;
+    default:
+      return QTTS_ERR_DTYPE;
+  }
+  return e == cudaSuccess ? QTTS_OK : QTTS_ERR_LAUNCH;
+}
+
+int qtts_fp8_gemm(const uint8_t* xq, int64_t ldxq, const float* scale_x, const uint8_t* wq, int64_t ldw,
+                  const float* scale_w, const void* bias, void* out, int64_t ldo, int out_dtype, int M, int N, int K,
+                  int variant, unsigned flags, void* stream) {
+  if (M < 0 || N < 0 || K < 0) return QTTS_ERR_SHAPE;
+  if (M == 0 || N == 0) return QTTS_OK;
+  if (xq == nullptr || scale_x == nullptr || wq == nullptr || scale_w == nullptr || out == nullptr)
+    return QTTS_ERR_NULL;
+  if (!is_float_dtype(out_dtype)) return QTTS_ERR_DTYPE;
+  if (ldxq < K || ldw < K || ldo < N) return QTTS_ERR_SHAPE;
+  const int dev_ok = check_device();
+  if (dev_ok != QTTS_OK) return dev_ok;
+  cudaStream_t s = static_cast<cudaStream_t>(stream);
+  const bool pdl = (flags & QTTS_FLAG_PDL) != 0;
+  if (variant != QTTS_VARIANT_AUTO && variant != QTTS_VARIANT_GENERIC) return QTTS_ERR_VARIANT;
+  GenericFp8Args ga{xq, ldxq, scale_x, wq, ldw, scale_w, bias, out, ldo, M, N, K};
+  const dim3 grid((N + 7) / 8, (M + 7) / 8);
+  if (grid.y > 65535u) return QTTS_ERR_SHAPE;
+  switch (out_dtype) {
+    case QTTS_BF16:
+      return launch_simple(generic_fp8_kernel<__nv_bfloat16>, grid, dim3(256), ga, pdl, s);
+    case QTTS_FP16:
+      return launch_simple(generic_fp8_kernel<__half>, grid, dim3(256), ga, pdl, s);
+    default:
+      return launch_simple(generic_fp8_kernel<float>, grid, dim3(256), ga, pdl, s);
+  }
+}
+
+}  // extern "C"

@@ -1,0 +1,245 @@
+// Device-side building blocks shared by the sm_100a kernels of this library:
+// mbarrier pipeline primitives with bounded waits, TMA tile loads, programmatic
+// dependent launch controls, int8/e4m3 -> bf16/fp16 register dequantization and
+// the legacy mma.sync fragments used by the skinny (decode-M) kernel.
+#pragma once
+
+#include <cuda.h>
+#include <cuda_bf16.h>
+#include <cuda_fp16.h>
+#include <cuda_runtime.h>
+#include <stdint.h>
+
+#include "../../include/qtts_b200.h"
+
+namespace qtts {
+
+// Per-device status word. Kernels record the first failure here (bounded wait
+// expired, device-side index out of range); the host reads it with
+// qtts_device_status(). Defined in capi.cu.
+extern __device__ int g_device_status;
+// Bounded-wait limit in nanoseconds, set per launch from the host.
+struct WaitLimit {
+  uint64_t ns;
+};
+
+__device__ __forceinline__ void record_status(int code) {
+  atomicCAS(&g_device_status, 0, code);
+}
+
+__device__ __forceinline__ uint64_t globaltimer_ns() {
+  uint64_t t;
+  asm volatile("mov.u64 %0, %%globaltimer;" : "=l"(t));
+  return t;
+}
+
+__device__ __forceinline__ uint32_t smem_u32(const void* p) {
+  return static_cast<uint32_t>(__cvta_generic_to_shared(p));
+}
+
+// ---- mbarrier ---------------------------------------------------------------
+
+__device__ __forceinline__ void mbar_init(uint64_t* bar, uint32_t count) {
+  asm volatile("mbarrier.init.shared::cta.b64 [%0], %1;" ::"r"(smem_u32(bar)), "r"(count));
+}
+
+__device__ __forceinline__ void fence_mbarrier_init() {
+  asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
+}
+
+__device__ __forceinline__ void mbar_arrive(uint64_t* bar) {
+  asm volatile("mbarrier.arrive.shared::cta.b64 _, [%0];" ::"r"(smem_u32(bar)) : "memory");
+}
+
+__device__ __forceinline__ void mbar_arrive_expect_tx(uint64_t* bar, uint32_t bytes) {
+  asm volatile("mbarrier.arrive.expect_tx.shared::cta.b64 _, [%0], %1;" ::"r"(smem_u32(bar)), "r"(bytes)
+               : "memory");
+}
+
+__device__ __forceinline__ bool mbar_try_wait(uint64_t* bar, uint32_t parity) {
+  uint32_t ok;
+  asm volatile(
+      "{\n"
+      ".reg .pred p;\n"
+      "mbarrier.try_wait.parity.shared::cta.b64 p, [%1], %2;\n"
+      "selp.u32 %0, 1, 0, p;\n"
+      "}\n"
+      : "=r"(ok)
+      : "r"(smem_u32(bar)), "r"(parity)
+      : "memory");
+  return ok != 0;
+}
+
+// Waits for the phase with the given parity to complete. Gives up after
+// `limit_ns` of wall time and returns false; the caller records the failure
+// and takes its error path (which never waits unboundedly again).
+__device__ __forceinline__ bool mbar_wait_bounded(uint64_t* bar, uint32_t parity, uint64_t limit_ns) {
+  if (mbar_try_wait(bar, parity)) return true;
+  const uint64_t t0 = globaltimer_ns();
+  uint32_t spins = 0;
+  while (true) {
+    if (mbar_try_wait(bar, parity)) return true;
+    if ((++spins & 63u) == 0 && globaltimer_ns() - t0 > limit_ns) return false;
+  }
+}
+
+// ---- TMA ----------------------------------------------------------------------
+
+__device__ __forceinline__ void tma_prefetch_desc(const CUtensorMap* map) {
+  asm volatile("prefetch.tensormap [%0];" ::"l"(reinterpret_cast<uint64_t>(map)) : "memory");
+}
+
+// 2-D tiled bulk tensor load into this CTA's shared memory, completion counted
+// on `bar` in bytes. c0 is the innermost (contiguous) coordinate.
+__device__ __forceinline__ void tma_load_2d(void* dst, const CUtensorMap* map, int c0, int c1, uint64_t* bar) {
+  asm volatile(
+      "cp.async.bulk.tensor.2d.shared::cluster.global.mbarrier::complete_tx::bytes"
+      " [%0], [%1, {%2, %3}], [%4];" ::"r"(smem_u32(dst)),
+      "l"(reinterpret_cast<uint64_t>(map)), "r"(c0), "r"(c1), "r"(smem_u32(bar))
+      : "memory");
+}
+
+// ---- programmatic dependent launch ------------------------------------------
+
+// Blocks until the preceding grid of the stream has completed and its memory
+// operations are visible. A no-op when the kernel was launched without the
+// programmatic-serialization attribute.
+__device__ __forceinline__ void pdl_wait() { asm volatile("griddepcontrol.wait;" ::: "memory"); }
+
+// Allows the next grid of the stream (if launched with PDL) to start launching.
+__device__ __forceinline__ void pdl_launch_dependents() {
+  asm volatile("griddepcontrol.launch_dependents;" ::: "memory");
+}
+
+// ---- named barriers ------------------------------------------------------------
+
+__device__ __forceinline__ void named_bar_sync(int id, int nthreads) {
+  asm volatile("bar.sync %0, %1;" ::"r"(id), "r"(nthreads) : "memory");
+}
+
+// ---- shared memory vector loads ------------------------------------------------
+
+__device__ __forceinline__ uint4 lds128(uint32_t addr) {
+  uint4 v;
+  asm volatile("ld.shared.v4.u32 {%0, %1, %2, %3}, [%4];"
+               : "=r"(v.x), "=r"(v.y), "=r"(v.z), "=r"(v.w)
+               : "r"(addr));
+  return v;
+}
+
+// ---- int8 -> 16-bit float dequantization in registers ----------------------------
+//
+// A 32-bit word holds four int8 weights b0..b3 (little endian). Each routine
+// returns two packed 16-bit pairs: lo = (b0, b1), hi = (b2, b3), exactly.
+//
+// bf16 route: bf16 has 8 significant bits, so a signed byte cannot be placed in
+// one binade of it directly. Flip the sign bit (u = b + 128, 0..255), place u in
+// the low mantissa byte of the fp32 2^23 (the exponent makes the mantissa an
+// integer), subtract 2^23 + 128 in fp32 (exact), and keep the top half of each
+// fp32 -- truncation is exact because |b| <= 128 needs at most 8 bits.
+__device__ __forceinline__ void i8x4_to_bf16x2x2(uint32_t w, uint32_t& lo, uint32_t& hi) {
+  const uint32_t u = w ^ 0x80808080u;
+  const float kBias = 8388736.0f;  // 2^23 + 128
+  const float f0 = __uint_as_float(__byte_perm(u, 0x4B000000u, 0x7540)) - kBias;
+  const float f1 = __uint_as_float(__byte_perm(u, 0x4B000000u, 0x7541)) - kBias;
+  const float f2 = __uint_as_float(__byte_perm(u, 0x4B000000u, 0x7542)) - kBias;
+  const float f3 = __uint_as_float(__byte_perm(u, 0x4B000000u, 0x7543)) - kBias;
+  lo = __byte_perm(__float_as_uint(f0), __float_as_uint(f1), 0x7632);
+  hi = __byte_perm(__float_as_uint(f2), __float_as_uint(f3), 0x7632);
+}
+
+// fp16 route: fp16 has 11 significant bits, so u = b + 128 fits the mantissa of
+// 1024 (0x6400 | u == 1024 + u); one half-precision subtract of 1152 gives b.
+__device__ __forceinline__ void i8x4_to_f16x2x2(uint32_t w, uint32_t& lo, uint32_t& hi) {
+  const uint32_t u = w ^ 0x80808080u;
+  uint32_t a = __byte_perm(u, 0x64646464u, 0x4140);
+  uint32_t b = __byte_perm(u, 0x64646464u, 0x4342);
+  const uint32_t kBias = 0x64806480u;  // (1152, 1152) in fp16
+  asm("sub.f16x2 %0, %1, %2;" : "=r"(lo) : "r"(a), "r"(kBias));
+  asm("sub.f16x2 %0, %1, %2;" : "=r"(hi) : "r"(b), "r"(kBias));
+}
+
+template <typename T>
+struct Dequant;
+template <>
+struct Dequant<__nv_bfloat16> {
+  static __device__ __forceinline__ void run(uint32_t w, uint32_t& lo, uint32_t& hi) {
+    i8x4_to_bf16x2x2(w, lo, hi);
+  }
+};
+template <>
+struct Dequant<__half> {
+  static __device__ __forceinline__ void run(uint32_t w, uint32_t& lo, uint32_t& hi) {
+    i8x4_to_f16x2x2(w, lo, hi);
+  }
+};
+
+// ---- mma.sync m16n8k16, fp32 accumulate ---------------------------------------------
+
+template <typename T>
+struct Mma16816;
+template <>
+struct Mma16816<__nv_bfloat16> {
+  static __device__ __forceinline__ void run(float (&d)[4], const uint32_t (&a)[4], uint32_t b0, uint32_t b1) {
+    asm volatile(
+        "mma.sync.aligned.m16n8k16.row.col.f32.bf16.bf16.f32 "
+        "{%0, %1, %2, %3}, {%4, %5, %6, %7}, {%8, %9}, {%0, %1, %2, %3};"
+        : "+f"(d[0]), "+f"(d[1]), "+f"(d[2]), "+f"(d[3])
+        : "r"(a[0]), "r"(a[1]), "r"(a[2]), "r"(a[3]), "r"(b0), "r"(b1));
+  }
+};
+template <>
+struct Mma16816<__half> {
+  static __device__ __forceinline__ void run(float (&d)[4], const uint32_t (&a)[4], uint32_t b0, uint32_t b1) {
+    asm volatile(
+        "mma.sync.aligned.m16n8k16.row.col.f32.f16.f16.f32 "
+        "{%0, %1, %2, %3}, {%4, %5, %6, %7}, {%8, %9}, {%0, %1, %2, %3};"
+        : "+f"(d[0]), "+f"(d[1]), "+f"(d[2]), "+f"(d[3])
+        : "r"(a[0]), "r"(a[1]), "r"(a[2]), "r"(a[3]), "r"(b0), "r"(b1));
+  }
+};
+
+// ---- scalar conversions -----------------------------------------------------------
+
+__device__ __forceinline__ float load_as_float(const void* p, int dtype, int64_t i) {
+  switch (dtype) {
+    case QTTS_BF16:
+      return __bfloat162float(static_cast<const __nv_bfloat16*>(p)[i]);
+    case QTTS_FP16:
+      return __half2float(static_cast<const __half*>(p)[i]);
+    default:
+      return static_cast<const float*>(p)[i];
+  }
+}
+
+template <typename T>
+__device__ __forceinline__ T from_float(float v);
+template <>
+__device__ __forceinline__ __nv_bfloat16 from_float<__nv_bfloat16>(float v) {
+  return __float2bfloat16_rn(v);
+}
+template <>
+__device__ __forceinline__ __half from_float<__half>(float v) {
+  return __float2half_rn(v);
+}
+template <>
+__device__ __forceinline__ float from_float<float>(float v) {
+  return v;
+}
+
+template <typename T>
+__device__ __forceinline__ float to_float(T v);
+template <>
+__device__ __forceinline__ float to_float<__nv_bfloat16>(__nv_bfloat16 v) {
+  return __bfloat162float(v);
+}
+template <>
+__device__ __forceinline__ float to_float<__half>(__half v) {
+  return __half2float(v);
+}
+template <>
+__device__ __forceinline__ float to_float<float>(float v) {
+  return v;
+}
+
+}  // namespace qtts

@@ -1,0 +1,61 @@
+// Internal host-side interface between the C ABI (capi.cu) and the kernel
+// translation units. Not part of the public ABI.
+#pragma once
+
+#include <cuda.h>
+#include <cuda_runtime.h>
+#include <stddef.h>
+#include <stdint.h>
+
+#include "../../include/qtts_b200.h"
+
+namespace qtts {
+
+constexpr int kNumSMs = 148;                 // B200: 2 dies x 74 SMs
+constexpr size_t kMaxDynSmem = 227 * 1024;   // opt-in dynamic shared memory per CTA
+
+// ---- skinny W8A16 ------------------------------------------------------------
+struct SkinnyArgs {
+  const void* x;
+  int64_t ldx;
+  int64_t gsx;  // group stride of x (elements)
+  const void* scale;
+  int scale_dtype;
+  const void* bias;
+  void* out;
+  int64_t ldo;
+  int64_t gso;  // group stride of out (elements)
+  int M, N, K;  // N is per group
+  int G;
+  int k_per_cta;  // multiple of 128
+  int stages;
+  int x_pitch;  // elements per staged activation row
+  int m_chunks;
+  const int64_t* group_index;  // device pointer or NULL
+  uint64_t wait_ns;
+};
+
+struct SkinnyPlan {
+  int mt;        // batch n-tiles of 8 (1, 2, 4, 8)
+  int m_chunks;  // ceil(M / (8*mt))
+  int split;     // CTAs per cluster along K
+  int k_per_cta;
+  int x_pitch;
+  int stages;
+  size_t smem;
+  dim3 grid;
+};
+
+SkinnyPlan plan_skinny(int M, int N, int K, int G, int split_req);
+int launch_skinny_w8a16(const SkinnyPlan& p, const CUtensorMap& map, const SkinnyArgs& args, int x_dtype,
+                        bool pdl, cudaStream_t stream);
+
+// ---- tensor maps ---------------------------------------------------------------
+// 2-D uint8 tensor map over a row-major [rows, cols] byte matrix with row pitch
+// `pitch_bytes`, box [box_rows, box_cols] and 128-byte swizzle.
+int make_tmap_u8_2d(CUtensorMap* map, const void* base, uint64_t rows, uint64_t cols, uint64_t pitch_bytes,
+                    uint32_t box_rows, uint32_t box_cols);
+
+uint64_t current_wait_limit_ns();
+
+}  // namespace qtts

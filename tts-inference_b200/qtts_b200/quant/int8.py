@@ -1,0 +1,175 @@
+"""int8 quantization methods.
+
+:class:`Int8WeightOnlyMethod` keeps the reference's contract
+(qtts/quant/int8.py:59-117): per-output-channel symmetric int8 weights stored
+as ``int8_weight`` [N, K] and ``int8_scale`` [N] in the weight dtype,
+calibration per distinct shape (``_profitable``), the full-precision weight
+dropped after conversion, and ``apply`` computing
+``x @ (int8_weight * int8_scale).T + bias``. The GEMM is the sm_100a kernel of
+this package; calibration additionally records which kernel variant is fastest
+for the shape, per batch-row bucket, and ``apply`` passes it along.
+
+:class:`Int8Method` (W8A8 through ``torch._int_mm``, int8.py:120-155) is kept
+unchanged: it is not part of the accelerated path.
+"""
+
+from __future__ import annotations
+
+import torch
+import torch.nn.functional as F
+
+from .. import _native as nat
+from ..layers.linear import LinearBase
+from ..utils import get_logger
+from .base import QuantMethodBase
+from .calibrate import choose_variant, lookup_variant, worth_quantizing
+from .kernels import kernel_available, quantize_int8_rows, w8_gemm
+
+logger = get_logger("quant.int8")
+
+_INT8_MAX = 127.0
+#: torch._int_mm rejects fewer rows than this.
+_INT_MM_MIN_ROWS = 17
+#: Batch-row buckets the skinny kernel specializes on (8 rows per MMA tile).
+_ROW_BUCKETS = (8, 16, 32, 64)
+#: Split-K factors calibration chooses from.
+_SPLITS = (1, 2, 4, 8)
+
+
+def quantize_weight_per_channel(weight: torch.Tensor) -> tuple[torch.Tensor, torch.Tensor]:
+    """Symmetric per-output-channel int8. Returns ``(int8 weight, fp32 scale)``.
+
+    Same arithmetic as int8.py:45-56 -- fp32 absmax / 127 clamped at 1e-12,
+    round half to even, clamp to +-127 -- computed on the GPU by the library
+    (bit-exact with the reference's torch ops).
+    """
+    return quantize_int8_rows(weight)
+
+
+def row_bucket(rows: int) -> int:
+    for b in _ROW_BUCKETS:
+        if rows <= b:
+            return b
+    return _ROW_BUCKETS[-1]
+
+
+class Int8WeightOnlyMethod(QuantMethodBase):
+    """int8 weights, bf16 activations, dequantized inside the GEMM."""
+
+    name = "int8_weight_only"
+
+    def __init__(self, calibrate: bool = True, calibration_batch: int = 16) -> None:
+        available, reason = kernel_available()
+        if not available:
+            raise RuntimeError(f"int8 weight-only needs the sm_100a kernels of qtts_b200: {reason}")
+        self.calibrate = calibrate
+        self.calibration_batch = calibration_batch
+        self.quantized = 0
+        self.declined = 0
+
+    # -- calibration ---------------------------------------------------------
+
+    def _variant_key(self, n: int, k: int, bucket: int, dtype: torch.dtype) -> tuple:
+        return ("int8_wo_variant", n, k, bucket, str(dtype))
+
+    def _tune_variants(self, q: torch.Tensor, scale: torch.Tensor, dtype: torch.dtype) -> None:
+        n, k = q.shape
+        top = row_bucket(max(1, self.calibration_batch))
+        for bucket in _ROW_BUCKETS:
+            if bucket > top:
+                break
+            key = self._variant_key(n, k, bucket, dtype)
+            if lookup_variant(key) is not None:
+                continue
+            x = torch.zeros(bucket, k, device=q.device, dtype=dtype)
+            candidates = {
+                nat.variant_skinny(s): (lambda s=s: w8_gemm(x, q, scale, None, variant=nat.variant_skinny(s)))
+                for s in _SPLITS
+            }
+            choose_variant(candidates, key=key)
+
+    def _profitable(self, layer: LinearBase, q: torch.Tensor, scale: torch.Tensor) -> bool:
+        if not self.calibrate:
+            return True
+        if not torch.cuda.is_available() or layer.weight.device.type != "cuda":
+            return False
+        weight = layer.weight
+        rows = max(1, self.calibration_batch)
+        self._tune_variants(q, scale, weight.dtype)
+        x = torch.zeros(rows, layer.in_features, device=weight.device, dtype=weight.dtype)
+        variant = self.variant_for(layer.out_features, layer.in_features, rows, weight.dtype)
+        return worth_quantizing(
+            lambda: w8_gemm(x, q, scale, None, variant=variant),
+            lambda: F.linear(x, weight, None),
+            key=("int8_wo", layer.out_features, layer.in_features, rows, str(weight.dtype)),
+        )
+
+    def variant_for(self, n: int, k: int, rows: int, dtype: torch.dtype) -> int:
+        v = lookup_variant(self._variant_key(n, k, row_bucket(rows), dtype))
+        return nat.VARIANT_AUTO if v is None else v
+
+    # -- QuantMethodBase ------------------------------------------------------
+
+    def process_weights(self, layer: LinearBase) -> None:
+        q, scale = quantize_weight_per_channel(layer.weight)
+        scale = scale.to(layer.weight.dtype)
+        if not self._profitable(layer, q, scale):
+            self.declined += 1
+            # Leaving quant_method unset is what keeps the layer on F.linear.
+            layer.register_buffer("int8_weight", None, persistent=False)
+            return
+        # Buffers rather than plain attributes so they follow module.to() and
+        # are counted by the byte report of quantize_module.
+        layer.register_buffer("int8_weight", q, persistent=False)
+        layer.register_buffer("int8_scale", scale, persistent=False)
+        # Drop the full-precision weight: keeping both would report a memory
+        # saving that was not made.
+        layer.weight = torch.nn.Parameter(
+            torch.empty(0, dtype=layer.weight.dtype, device=layer.weight.device), requires_grad=False
+        )
+        self.quantized += 1
+
+    def applies_to(self, layer: LinearBase) -> bool:
+        return getattr(layer, "int8_weight", None) is not None
+
+    def apply(self, layer: LinearBase, x: torch.Tensor, bias: torch.Tensor | None) -> torch.Tensor:
+        rows = x.numel() // max(1, x.shape[-1])
+        variant = self.variant_for(layer.out_features, layer.in_features, rows, x.dtype)
+        return w8_gemm(x, layer.int8_weight, layer.int8_scale, bias, variant=variant)  # type: ignore[attr-defined]
+
+
+class Int8Method(QuantMethodBase):
+    """W8A8: per-token activation scales, per-channel weight scales, int8 GEMM (torch._int_mm)."""
+
+    name = "int8"
+
+    def process_weights(self, layer: LinearBase) -> None:
+        w = layer.weight.detach().float()
+        scale = w.abs().amax(dim=1).clamp_min(1e-12) / _INT8_MAX
+        q = (w / scale[:, None]).round().clamp_(-_INT8_MAX, _INT8_MAX).to(torch.int8)
+        # _int_mm takes B as [K, N]; the transpose is materialised once here.
+        layer.register_buffer("int8_weight", q.t().contiguous(), persistent=False)
+        layer.register_buffer("int8_scale", scale, persistent=False)
+        layer.weight = torch.nn.Parameter(
+            torch.empty(0, dtype=layer.weight.dtype, device=layer.weight.device), requires_grad=False
+        )
+
+    def applies_to(self, layer: LinearBase) -> bool:
+        return getattr(layer, "int8_weight", None) is not None
+
+    def apply(self, layer: LinearBase, x: torch.Tensor, bias: torch.Tensor | None) -> torch.Tensor:
+        shape = x.shape
+        flat = x.reshape(-1, shape[-1])
+        scale_x = flat.abs().amax(dim=1, keepdim=True).clamp_min(1e-6) / _INT8_MAX
+        q = (flat / scale_x).round().clamp_(-_INT8_MAX, _INT8_MAX).to(torch.int8)
+        rows = q.shape[0]
+        padded = rows < _INT_MM_MIN_ROWS
+        if padded:
+            q = torch.cat([q, q.new_zeros(_INT_MM_MIN_ROWS - rows, q.shape[1])], dim=0)
+        acc = torch._int_mm(q, layer.int8_weight)  # type: ignore[attr-defined]
+        if padded:
+            acc = acc[:rows]
+        out = acc.float() * scale_x.float() * layer.int8_scale.reshape(1, -1)  # type: ignore[attr-defined]
+        if bias is not None:
+            out += bias.float()
+        return out.to(x.dtype).reshape(*shape[:-1], layer.out_features)

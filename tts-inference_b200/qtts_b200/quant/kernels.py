@@ -1,0 +1,279 @@
+"""Fused dequantize-and-matmul entry points on the sm_100a library.
+
+Drop-in for ``qtts/quant/kernels.py``: ``kernel_available()`` and
+``w8_gemm(x, weight, scale, bias=None)`` keep their names, argument meaning
+and error behaviour (kernels.py:84-86, 138-177), but the work is done by the
+hand-written CUDA kernels behind the C ABI (``include/qtts_b200.h``) instead of
+Triton. Every function launches on ``torch.cuda.current_stream()`` and
+allocates only its output (from torch's caching allocator), so all of them can
+be captured in a CUDA graph.
+
+There is no CPU path. CPU tensors, or a machine without the library or a
+compute-capability 10.x GPU, raise ``RuntimeError``.
+"""
+
+from __future__ import annotations
+
+import torch
+
+from .. import _native as nat
+
+#: Launch with programmatic dependent launch unless told otherwise. Safe for
+#: every kernel of this library: weights are never written by the kernel that
+#: immediately precedes a GEMM, and everything else is read after the wait.
+USE_PDL = True
+
+
+def kernel_available() -> tuple[bool, str]:
+    """(available, reason) -- the library loaded and an sm_100 GPU is present."""
+    return nat.available()
+
+
+def _flags() -> int:
+    return nat.FLAG_PDL if USE_PDL else 0
+
+
+def _require_cuda(*tensors: torch.Tensor | None) -> torch.device:
+    device = None
+    for t in tensors:
+        if t is None:
+            continue
+        if t.device.type != "cuda":
+            raise RuntimeError(f"qtts_b200 kernels run on CUDA tensors only, got a tensor on {t.device}")
+        if device is None:
+            device = t.device
+        elif t.device != device:
+            raise RuntimeError(f"tensors on different devices: {device} and {t.device}")
+    assert device is not None
+    return device
+
+
+def _rows_view(x: torch.Tensor, k: int) -> torch.Tensor:
+    """[..., K] -> a 2-D [rows, K] view with unit stride along K (copying only if needed)."""
+    a = x.reshape(-1, k) if x.dim() != 2 else x
+    if a.stride(-1) != 1 or (a.shape[0] > 1 and a.stride(0) < k):
+        a = a.contiguous()
+    return a
+
+
+def w8_gemm(
+    x: torch.Tensor,
+    weight: torch.Tensor,
+    scale: torch.Tensor,
+    bias: torch.Tensor | None = None,
+    *,
+    variant: int = nat.VARIANT_AUTO,
+    out: torch.Tensor | None = None,
+) -> torch.Tensor:
+    """``x @ (weight * scale).T + bias``, dequantizing ``weight`` in registers.
+
+    ``x`` is ``[..., K]`` (bf16, fp16 or fp32), ``weight`` is ``[N, K]`` int8 and
+    ``scale`` is ``[N]`` (bf16, fp16 or fp32): one per output channel, applied
+    once after the fp32 K loop. The result has ``x``'s dtype and shape
+    ``[..., N]``. ``variant`` selects a kernel (see ``include/qtts_b200.h``);
+    the default lets the library choose.
+    """
+    ok, reason = nat.available()
+    if not ok:
+        raise RuntimeError(reason)
+    shape = x.shape
+    k = shape[-1]
+    if weight.dim() != 2 or weight.dtype != torch.int8:
+        raise ValueError(f"weight must be a 2-D int8 tensor, got {tuple(weight.shape)} {weight.dtype}")
+    n = weight.shape[0]
+    if weight.shape[1] != k:
+        raise ValueError(f"weight is [{n}, {weight.shape[1]}] but x has K={k}")
+    if scale.numel() != n:
+        raise ValueError(f"scale has {scale.numel()} elements, expected {n}")
+    device = _require_cuda(x, weight, scale, bias)
+    a = _rows_view(x, k)
+    rows = a.shape[0]
+    if weight.stride(1) != 1:
+        weight = weight.contiguous()
+    scale = scale.reshape(-1)
+    if scale.stride(0) != 1:
+        scale = scale.contiguous()
+    if bias is not None:
+        bias = bias.reshape(-1)
+        if bias.dtype != x.dtype or bias.stride(0) != 1:
+            bias = bias.to(x.dtype).contiguous()
+    if out is None:
+        out = torch.empty((rows, n), device=device, dtype=x.dtype)
+    elif out.shape != (rows, n) or out.dtype != x.dtype or out.stride(1) != 1:
+        raise ValueError(f"out must be [{rows}, {n}] {x.dtype} with unit column stride")
+    code = nat.lib().qtts_w8a16_gemm(
+        a.data_ptr(), a.stride(0) if rows > 1 else k, nat.dtype_code(a.dtype),
+        weight.data_ptr(), weight.stride(0),
+        scale.data_ptr(), nat.dtype_code(scale.dtype),
+        bias.data_ptr() if bias is not None else None,
+        out.data_ptr(), out.stride(0) if rows > 1 else n,
+        rows, n, k, variant, _flags(), nat.stream_ptr(device),
+    )
+    nat.check(code, "qtts_w8a16_gemm")
+    return out.reshape(*shape[:-1], n)
+
+
+def w8_grouped_gemm(
+    x: torch.Tensor,
+    weight: torch.Tensor,
+    scale: torch.Tensor,
+    bias: torch.Tensor | None = None,
+    *,
+    variant: int = nat.VARIANT_AUTO,
+) -> torch.Tensor:
+    """G independent W8A16 problems of one shape in one launch.
+
+    ``x`` is ``[G, M, K]``, ``weight`` the stacked ``[G*N, K]`` int8 matrix,
+    ``scale`` ``[G*N]``; returns ``[G, M, N]``.
+    """
+    ok, reason = nat.available()
+    if not ok:
+        raise RuntimeError(reason)
+    if x.dim() != 3:
+        raise ValueError("x must be [G, M, K]")
+    g, m, k = x.shape
+    if weight.shape[0] % g != 0 or weight.shape[1] != k:
+        raise ValueError(f"weight {tuple(weight.shape)} is not [G*N, {k}] for G={g}")
+    n = weight.shape[0] // g
+    device = _require_cuda(x, weight, scale, bias)
+    if x.stride(2) != 1:
+        x = x.contiguous()
+    if bias is not None and bias.dtype != x.dtype:
+        bias = bias.to(x.dtype)
+    out = torch.empty((g, m, n), device=device, dtype=x.dtype)
+    code = nat.lib().qtts_w8a16_grouped_gemm(
+        x.data_ptr(), x.stride(0), x.stride(1) if m > 1 else k, nat.dtype_code(x.dtype),
+        weight.data_ptr(), weight.stride(0),
+        scale.data_ptr(), nat.dtype_code(scale.dtype),
+        bias.data_ptr() if bias is not None else None,
+        out.data_ptr(), out.stride(0), n,
+        g, m, n, k, None, variant, _flags(), nat.stream_ptr(device),
+    )
+    nat.check(code, "qtts_w8a16_grouped_gemm")
+    return out
+
+
+def w8_indexed_gemm(
+    x: torch.Tensor,
+    weight: torch.Tensor,
+    scale: torch.Tensor,
+    index: torch.Tensor,
+    groups: int,
+    bias: torch.Tensor | None = None,
+    *,
+    out: torch.Tensor | None = None,
+    variant: int = nat.VARIANT_AUTO,
+) -> torch.Tensor:
+    """One group of a stacked ``[groups*N, K]`` weight, chosen by a device tensor.
+
+    ``index`` is a one-element int64 CUDA tensor read by the kernel at run
+    time, so a captured graph can pick a different codebook head per replay.
+    ``x`` is ``[M, K]``; returns ``[M, N]``.
+    """
+    ok, reason = nat.available()
+    if not ok:
+        raise RuntimeError(reason)
+    k = x.shape[-1]
+    a = _rows_view(x, k)
+    m = a.shape[0]
+    n = weight.shape[0] // groups
+    device = _require_cuda(a, weight, scale, bias, index)
+    if index.dtype != torch.int64 or index.numel() != 1:
+        raise ValueError("index must be a one-element int64 tensor")
+    if bias is not None and bias.dtype != x.dtype:
+        bias = bias.to(x.dtype)
+    if out is None:
+        out = torch.empty((m, n), device=device, dtype=x.dtype)
+    code = nat.lib().qtts_w8a16_grouped_gemm(
+        a.data_ptr(), 0, a.stride(0) if m > 1 else k, nat.dtype_code(a.dtype),
+        weight.data_ptr(), weight.stride(0),
+        scale.data_ptr(), nat.dtype_code(scale.dtype),
+        bias.data_ptr() if bias is not None else None,
+        out.data_ptr(), 0, out.stride(0) if m > 1 else n,
+        groups, m, n, k, index.data_ptr(), variant, _flags(), nat.stream_ptr(device),
+    )
+    nat.check(code, "qtts_w8a16_grouped_gemm (indexed)")
+    return out.reshape(*x.shape[:-1], n)
+
+
+def quantize_int8_rows(weight: torch.Tensor) -> tuple[torch.Tensor, torch.Tensor]:
+    """Per-output-channel int8 on the GPU; bit-exact with quantize_weight_per_channel."""
+    device = _require_cuda(weight)
+    w = weight.detach()
+    if w.stride(-1) != 1:
+        w = w.contiguous()
+    n, k = w.shape
+    q = torch.empty((n, k), device=device, dtype=torch.int8)
+    s = torch.empty((n,), device=device, dtype=torch.float32)
+    code = nat.lib().qtts_quantize_int8_rows(
+        w.data_ptr(), w.stride(0), nat.dtype_code(w.dtype), q.data_ptr(), s.data_ptr(), n, k,
+        nat.stream_ptr(device),
+    )
+    nat.check(code, "qtts_quantize_int8_rows")
+    return q, s
+
+
+def quantize_fp8_rows(weight: torch.Tensor) -> tuple[torch.Tensor, torch.Tensor]:
+    """Per-output-channel e4m3 on the GPU; bit-exact with quantize_weight_fp8."""
+    device = _require_cuda(weight)
+    w = weight.detach()
+    if w.stride(-1) != 1:
+        w = w.contiguous()
+    n, k = w.shape
+    q = torch.empty((n, k), device=device, dtype=torch.float8_e4m3fn)
+    s = torch.empty((n,), device=device, dtype=torch.float32)
+    code = nat.lib().qtts_quantize_fp8_rows(
+        w.data_ptr(), w.stride(0), nat.dtype_code(w.dtype), q.data_ptr(), s.data_ptr(), n, k,
+        nat.stream_ptr(device),
+    )
+    nat.check(code, "qtts_quantize_fp8_rows")
+    return q, s
+
+
+def fp8_quant_rows(x: torch.Tensor) -> tuple[torch.Tensor, torch.Tensor]:
+    """Per-token e4m3 activation quantization: returns (q [M, K], scale_x [M, 1] fp32)."""
+    device = _require_cuda(x)
+    k = x.shape[-1]
+    a = _rows_view(x, k)
+    m = a.shape[0]
+    q = torch.empty((m, k), device=device, dtype=torch.float8_e4m3fn)
+    s = torch.empty((m, 1), device=device, dtype=torch.float32)
+    code = nat.lib().qtts_fp8_quant_rows(
+        a.data_ptr(), a.stride(0) if m > 1 else k, nat.dtype_code(a.dtype), q.data_ptr(), s.data_ptr(), m, k,
+        _flags(), nat.stream_ptr(device),
+    )
+    nat.check(code, "qtts_fp8_quant_rows")
+    return q, s
+
+
+def fp8_scaled_mm(
+    xq: torch.Tensor,
+    scale_x: torch.Tensor,
+    wq: torch.Tensor,
+    scale_w: torch.Tensor,
+    bias: torch.Tensor | None,
+    out_dtype: torch.dtype,
+    *,
+    variant: int = nat.VARIANT_AUTO,
+) -> torch.Tensor:
+    """``(xq @ wq.T) * scale_x * scale_w + bias`` with e4m3 operands.
+
+    ``xq`` [M, K] e4m3, ``wq`` [N, K] e4m3 (row-major; pass ``fp8_weight.t()``
+    of the reference's column-major view), scales fp32 ``[M]``/``[N]``.
+    """
+    device = _require_cuda(xq, scale_x, wq, scale_w, bias)
+    m, k = xq.shape
+    n = wq.shape[0]
+    if wq.shape[1] != k or wq.stride(1) != 1 or xq.stride(1) != 1:
+        raise ValueError("xq and wq must be row-major [M, K] and [N, K]")
+    if bias is not None and bias.dtype != out_dtype:
+        bias = bias.to(out_dtype)
+    out = torch.empty((m, n), device=device, dtype=out_dtype)
+    code = nat.lib().qtts_fp8_gemm(
+        xq.data_ptr(), xq.stride(0) if m > 1 else k, scale_x.data_ptr(),
+        wq.data_ptr(), wq.stride(0), scale_w.data_ptr(),
+        bias.data_ptr() if bias is not None else None,
+        out.data_ptr(), n, nat.dtype_code(out_dtype), m, n, k, variant, _flags(), nat.stream_ptr(device),
+    )
+    nat.check(code, "qtts_fp8_gemm")
+    return out
