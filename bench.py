@@ -49,7 +49,7 @@ import torch  # noqa: E402
 SHAPES = [("qkv", 4096, 2048), ("o_proj", 2048, 2048), ("gate_up", 12288, 2048), ("down_proj", 2048, 6144)]
 ROWS = (1, 2, 4, 8, 16, 32, 64)
 CALLS_PER_GRAPH = 224  # multiple of every pool size below
-REPLAYS_PER_POINT = 9  # 9 x 224 = 2016 calls per point
+REPLAYS_PER_POINT = 9  # 9 x 224 = 2016 calls per point (--replays)
 POOL_MIN_BYTES = 256 << 20
 METRIC = "int8 W8A16 GEMM HBM GB/s (talker linear sweep, M=1..64)"
 
@@ -499,7 +499,10 @@ def main(argv=None) -> int:
     ap.add_argument("--no-bf16-compare", dest="bf16_compare", action="store_false")
     ap.add_argument("--no-cpu-baseline", action="store_true")
     ap.add_argument("--cpu-seconds", type=float, default=15.0)
+    ap.add_argument("--replays", type=int, default=REPLAYS_PER_POINT,
+                    help="graph replays per point per step (224 calls each); 9 gives the reference's 2016 calls")
     args = ap.parse_args(argv)
+    globals()["REPLAYS_PER_POINT"] = args.replays
     if args.warmup < 3:
         print("warning: fewer than 3 warm-up steps", file=sys.stderr)
     if args.impl == "reference":

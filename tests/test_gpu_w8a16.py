@@ -94,7 +94,13 @@ def test_every_variant_agrees(variant, m):
     x, q, s = seeded_case(n, k, m, seed=2)
     ref = oracle.w8a16_reference(x.float().numpy(), q, scale_values(s, torch.bfloat16))
     v = nat.VARIANT_GENERIC if variant == "generic" else nat.variant_skinny(int(variant[-1]))
-    out = qk.w8_gemm(*to_dev(x, q, s), variant=v)
+    try:
+        out = qk.w8_gemm(*to_dev(x, q, s), variant=v)
+    except RuntimeError as exc:
+        # A forced split whose activation slice cannot fit in shared memory is
+        # refused on the host (QTTS_ERR_VARIANT); the library's own choice never is.
+        assert "inapplicable kernel variant" in str(exc)
+        return
     assert_close_to_oracle(out, ref, f"{variant} M={m}")
 
 

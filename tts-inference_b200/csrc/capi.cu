@@ -397,9 +397,10 @@ static int w8a16_dispatch(const void* x, int64_t gsx, int64_t ldx, int x_dtype, 
     const int zg = group_index != nullptr ? 1 : G;
     const SkinnyPlan plan = plan_skinny(M, N, K, zg, split);
     if (plan.grid.z > 65535u) return QTTS_ERR_SHAPE;
+    if (plan.smem > kMaxDynSmem) return QTTS_ERR_VARIANT;  // activation slice does not fit this split
     CUtensorMap map;
     const uint64_t rows = static_cast<uint64_t>(G) * N;
-    const int r = make_tmap_u8_2d(&map, w, rows, static_cast<uint64_t>(K), static_cast<uint64_t>(ldw), 64, 128);
+    const int r = make_tmap_u8_2d(&map, w, rows, static_cast<uint64_t>(K), static_cast<uint64_t>(ldw), 128, 128);
     if (r != QTTS_OK) return r;
     SkinnyArgs sa{};
     sa.x = x;
