@@ -80,9 +80,12 @@ enum qtts_dtype {
  * calibration (qtts_b200.quant.calibrate) times them per shape. */
 #define QTTS_VARIANT_AUTO 0
 #define QTTS_VARIANT_GENERIC 1 /* SIMT kernel: any shape, stride, dtype    */
-/* TMA-streamed weights + mma.sync, split-K over a thread-block cluster of
- * `split` CTAs (1, 2, 4 or 8) reduced through distributed shared memory. */
+/* TMA-streamed weights + mma.sync. `split`: K split over a thread-block
+ * cluster of 1, 2, 4 or 8 CTAs reduced through distributed shared memory;
+ * `rows`: row groups of 16 per CTA (1, 2, 4 or 8; the rest of the CTA's 8
+ * warps split K inside it). 0 in either field lets the library choose. */
 #define QTTS_VARIANT_SKINNY(split) (0x100 | (split))
+#define QTTS_VARIANT_SKINNY_R(split, rows) (0x100 | (split) | ((rows) << 4))
 /* tcgen05/TMEM tile kernel (weights dequantized to bf16 in shared memory,
  * accumulator in tensor memory), split-K over a cluster of `split` CTAs. */
 #define QTTS_VARIANT_UMMA(split) (0x200 | (split))

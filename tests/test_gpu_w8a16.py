@@ -87,13 +87,21 @@ def test_matches_reference_eager_path(label, n, k):
     assert oracle.rel_err(out.float().cpu().numpy(), naive) <= 1e-2
 
 
-@pytest.mark.parametrize("variant", ["skinny1", "skinny2", "skinny4", "skinny8", "generic"])
-@pytest.mark.parametrize("m", [1, 8, 16, 64])
+VARIANTS = {
+    "generic": nat.VARIANT_GENERIC,
+    **{f"skinny{s}": nat.variant_skinny(s) for s in (1, 2, 4, 8)},
+    **{f"skinny{s}r{r}": nat.variant_skinny(s, r) for s, r in ((1, 1), (1, 2), (2, 4), (4, 2), (8, 1))},
+    **{f"umma{s}": nat.variant_umma(s) for s in (1, 2, 4, 8)},
+}
+
+
+@pytest.mark.parametrize("variant", sorted(VARIANTS))
+@pytest.mark.parametrize("m", [1, 8, 16, 33, 64])
 def test_every_variant_agrees(variant, m):
     n, k = 2048, 6144
     x, q, s = seeded_case(n, k, m, seed=2)
     ref = oracle.w8a16_reference(x.float().numpy(), q, scale_values(s, torch.bfloat16))
-    v = nat.VARIANT_GENERIC if variant == "generic" else nat.variant_skinny(int(variant[-1]))
+    v = VARIANTS[variant]
     try:
         out = qk.w8_gemm(*to_dev(x, q, s), variant=v)
     except RuntimeError as exc:
@@ -114,6 +122,14 @@ def test_ragged_shapes(n, k, m):
     ref = oracle.w8a16_reference(x.float().numpy(), q, scale_values(s, torch.bfloat16))
     out = qk.w8_gemm(*to_dev(x, q, s))
     assert_close_to_oracle(out, ref, f"N={n} K={k} M={m}")
+
+
+@pytest.mark.parametrize("n,k,m", [(80, 272, 3), (300, 2048, 130), (4096, 2048, 17), (12288, 2048, 64), (1, 16, 9)])
+def test_umma_ragged_shapes(n, k, m):
+    x, q, s = seeded_case(n, k, m, seed=13)
+    ref = oracle.w8a16_reference(x.float().numpy(), q, scale_values(s, torch.bfloat16))
+    out = qk.w8_gemm(*to_dev(x, q, s), variant=nat.variant_umma(0))
+    assert_close_to_oracle(out, ref, f"umma N={n} K={k} M={m}")
 
 
 def test_forced_skinny_rejects_unaligned_k():

@@ -381,10 +381,14 @@ static int w8a16_dispatch(const void* x, int64_t gsx, int64_t ldx, int x_dtype, 
   const bool skinny_ok = (x_dtype == QTTS_BF16 || x_dtype == QTTS_FP16) && K % 16 == 0 && K > 0 && aligned16(x) &&
                          aligned16(w) && (ldx * xs) % 16 == 0 && (gsx * xs) % 16 == 0 && ldw % 16 == 0;
   int family = variant & 0xF00;
-  int split = variant & 0xFF;
+  int split = variant & 0xF;
+  int rgroups = (variant >> 4) & 0xF;
   if (variant == QTTS_VARIANT_AUTO) {
-    family = skinny_ok ? 0x100 : 0;
+    // Decode rows (M <= 8): the mma.sync streaming kernel; wider batches: the
+    // tcgen05 kernel, whose MMA cost does not grow with M.
+    family = skinny_ok ? (M <= 8 ? 0x100 : 0x200) : 0;
     split = 0;
+    rgroups = 0;
   }
   if (variant == QTTS_VARIANT_GENERIC || family == 0) {
     if (variant != QTTS_VARIANT_AUTO && variant != QTTS_VARIANT_GENERIC) return QTTS_ERR_VARIANT;
@@ -394,13 +398,16 @@ static int w8a16_dispatch(const void* x, int64_t gsx, int64_t ldx, int x_dtype, 
   if (family == 0x100) {
     if (!skinny_ok) return QTTS_ERR_ALIGN;
     if (!(split == 0 || split == 1 || split == 2 || split == 4 || split == 8)) return QTTS_ERR_VARIANT;
+    if (!(rgroups == 0 || rgroups == 1 || rgroups == 2 || rgroups == 4 || rgroups == 8)) return QTTS_ERR_VARIANT;
+    if ((variant & 0xF000) != 0) return QTTS_ERR_VARIANT;
     const int zg = group_index != nullptr ? 1 : G;
-    const SkinnyPlan plan = plan_skinny(M, N, K, zg, split);
+    const SkinnyPlan plan = plan_skinny(M, N, K, zg, split, rgroups);
     if (plan.grid.z > 65535u) return QTTS_ERR_SHAPE;
     if (plan.smem > kMaxDynSmem) return QTTS_ERR_VARIANT;  // activation slice does not fit this split
     CUtensorMap map;
     const uint64_t rows = static_cast<uint64_t>(G) * N;
-    const int r = make_tmap_u8_2d(&map, w, rows, static_cast<uint64_t>(K), static_cast<uint64_t>(ldw), 128, 128);
+    const int r = make_tmap_u8_2d(&map, w, rows, static_cast<uint64_t>(K), static_cast<uint64_t>(ldw),
+                                  static_cast<uint32_t>(16 * plan.r), 128);
     if (r != QTTS_OK) return r;
     SkinnyArgs sa{};
     sa.x = x;
@@ -422,7 +429,46 @@ static int w8a16_dispatch(const void* x, int64_t gsx, int64_t ldx, int x_dtype, 
     sa.m_chunks = plan.m_chunks;
     sa.group_index = group_index;
     sa.wait_ns = current_wait_limit_ns();
+    sa.trace_slot = -1;
+#ifdef QTTS_TRACE
+    sa.trace_slot = qtts_trace_next_slot();
+#endif
     return launch_skinny_w8a16(plan, map, sa, x_dtype, pdl, stream);
+  }
+  if (family == 0x200) {
+    if (!skinny_ok) return QTTS_ERR_ALIGN;
+    if (!(split == 0 || split == 1 || split == 2 || split == 4 || split == 8) || rgroups != 0) return QTTS_ERR_VARIANT;
+    if ((variant & 0xF000) != 0) return QTTS_ERR_VARIANT;
+    const int zg = group_index != nullptr ? 1 : G;
+    const SkinnyPlan plan = plan_umma(M, N, K, zg, split);
+    if (plan.grid.z > 65535u) return QTTS_ERR_SHAPE;
+    if (plan.smem > kMaxDynSmem) return QTTS_ERR_VARIANT;
+    CUtensorMap map;
+    const uint64_t rows = static_cast<uint64_t>(G) * N;
+    const int r = make_tmap_u8_2d(&map, w, rows, static_cast<uint64_t>(K), static_cast<uint64_t>(ldw), 128, 128);
+    if (r != QTTS_OK) return r;
+    SkinnyArgs sa{};
+    sa.x = x;
+    sa.ldx = ldx;
+    sa.gsx = gsx;
+    sa.scale = scale;
+    sa.scale_dtype = scale_dtype;
+    sa.bias = bias;
+    sa.out = out;
+    sa.ldo = ldo;
+    sa.gso = gso;
+    sa.M = M;
+    sa.N = N;
+    sa.K = K;
+    sa.G = G;
+    sa.k_per_cta = plan.k_per_cta;
+    sa.stages = plan.stages;
+    sa.x_pitch = 0;
+    sa.m_chunks = plan.m_chunks;
+    sa.group_index = group_index;
+    sa.wait_ns = current_wait_limit_ns();
+    sa.trace_slot = -1;
+    return launch_umma_w8a16(plan, map, sa, x_dtype, pdl, stream);
   }
   return QTTS_ERR_VARIANT;
 }

@@ -33,10 +33,12 @@ struct SkinnyArgs {
   int m_chunks;
   const int64_t* group_index;  // device pointer or NULL
   uint64_t wait_ns;
+  int trace_slot;  // timeline probe slot (-1: off); only read in -DQTTS_TRACE builds
 };
 
 struct SkinnyPlan {
   int mt;        // batch n-tiles of 8 (1, 2, 4, 8)
+  int r;         // row groups of 16 per CTA (1, 2, 4, 8): BN = 16*r
   int m_chunks;  // ceil(M / (8*mt))
   int split;     // CTAs per cluster along K
   int k_per_cta;
@@ -46,9 +48,15 @@ struct SkinnyPlan {
   dim3 grid;
 };
 
-SkinnyPlan plan_skinny(int M, int N, int K, int G, int split_req);
+// split_req / r_req: 0 = choose.
+SkinnyPlan plan_skinny(int M, int N, int K, int G, int split_req, int r_req);
 int launch_skinny_w8a16(const SkinnyPlan& p, const CUtensorMap& map, const SkinnyArgs& args, int x_dtype,
                         bool pdl, cudaStream_t stream);
+
+// ---- tcgen05 W8A16 (same argument block; plan.mt = NB/8, plan.r = 8) ----------
+SkinnyPlan plan_umma(int M, int N, int K, int G, int split_req);
+int launch_umma_w8a16(const SkinnyPlan& p, const CUtensorMap& map, const SkinnyArgs& args, int x_dtype, bool pdl,
+                      cudaStream_t stream);
 
 // ---- tensor maps ---------------------------------------------------------------
 // 2-D uint8 tensor map over a row-major [rows, cols] byte matrix with row pitch
@@ -57,5 +65,9 @@ int make_tmap_u8_2d(CUtensorMap* map, const void* base, uint64_t rows, uint64_t 
                     uint32_t box_rows, uint32_t box_cols);
 
 uint64_t current_wait_limit_ns();
+
+#ifdef QTTS_TRACE
+int qtts_trace_next_slot();
+#endif
 
 }  // namespace qtts

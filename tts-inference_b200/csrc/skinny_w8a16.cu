@@ -7,30 +7,33 @@
 // 129-130).
 //
 // Design (B200, sm_100a). A decode GEMM streams N*K weight bytes once and does
-// 2*M flops per byte, so the kernel is built around the weight stream:
-//   * A CTA owns 128 weight rows and one K slice. A producer warp streams the
-//     slice HBM -> shared memory as 2-D TMA boxes of 128 rows x 128 bytes
-//     (128-byte swizzle) through a ring of mbarrier-tracked stages. Weights
-//     are constant, so streaming starts before the programmatic-dependent-
-//     launch wait: in a chain of linears the next layer's weights arrive while
-//     the previous kernel drains.
-//   * 8 consumer warps wait on the dependency and stage the activation slice
-//     in shared memory as fp16 with a per-row power-of-two scale (exact for
-//     every element within 2^28 of the row's largest magnitude; smaller ones
-//     round as fp16 subnormals, far below the bf16 output resolution).
-//   * Dequantization is one byte-permute per two weights: 0x64 above a byte u
-//     is the fp16 1024 + u, so (b ^ 0x80) placed there and 1152 subtracted
-//     gives b exactly. The MMA is mma.sync m16n8k16 f16 with fp32 accumulation,
-//     weights as the M=16 operand and activations as the N=8 operand ("swap
-//     AB"): batch rows 1..8 cost one MMA per 256 weights.
-//   * Each warp owns 16 rows over the whole 128-k stage, so no reduction is
-//     needed inside the CTA. K is permuted inside each 64-wide chunk (thread q
-//     owns k = 16q..16q+15) so weight and activation fragments are plain
-//     128-bit shared loads; a dot product does not depend on the order.
-//   * Split-K runs across the CTAs of a thread-block cluster (1, 2, 4 or 8).
-//     Each CTA owns 128/split rows of the result; partial sums travel to their
-//     owner with st.async into its shared memory, counted on the owner's
-//     mbarrier. One split cluster barrier (arrive at start, wait before the
+// 2*M flops per byte; in a decode step every linear waits on the previous one,
+// so per-kernel latency matters as much as bandwidth.
+//   * A CTA owns BN = 16*R weight rows (R = 1, 2, 4 or 8 row groups) and one K
+//     slice. Its 8 consumer warps form R row groups x (8/R) k groups. A stage
+//     is 16 KiB: 8/R TMA boxes of BN rows x 128 bytes (128-byte swizzle), one
+//     per k group, so small shapes split K inside the CTA (reduced through
+//     shared memory) instead of across CTAs.
+//   * A producer warp streams the weight slice through a ring of
+//     mbarrier-tracked stages. Weights are constant, so streaming starts before
+//     the programmatic-dependent-launch wait: in a chain of linears the next
+//     layer's weights arrive while the previous kernel drains.
+//   * After the dependency wait one thread fetches the activation slice with a
+//     bulk copy per row; each warp then scales its rows to fp16 in registers
+//     with a per-row power of two (exact for every element within 2^28 of the
+//     row's largest magnitude; smaller ones round as fp16 subnormals, far below
+//     the bf16 output resolution).
+//   * Dequantization: 0x64 above a byte u is the fp16 1024 + u, so (b ^ 0x80)
+//     placed there by one byte-permute per two weights, minus 1152, is b
+//     exactly. MMA: mma.sync m16n8k16 f16 -> fp32, weights as the M=16 operand
+//     and activations as the N=8 operand ("swap AB"), so batch rows 1..8 cost
+//     one MMA per 256 weights. K is permuted inside each 64-wide chunk (thread
+//     q owns k = 16q..16q+15) so weight and activation fragments are plain
+//     128-bit shared loads; the dot product does not depend on the order.
+//   * Optional split-K across a thread-block cluster (S = 2, 4, 8) for large
+//     M*K: each CTA owns BN/S rows of the result and receives the other CTAs'
+//     partial sums by st.async into its shared memory, counted on its own
+//     mbarrier; one split cluster barrier (arrive at start, wait before the
 //     first remote store) is the only cluster-wide synchronization.
 //   * Every wait is bounded (globaltimer). On expiry the kernel records
 //     QTTS_ERR_TIMEOUT in the device status word, keeps the remote-store
@@ -41,55 +44,90 @@
 
 namespace qtts {
 
-constexpr int kSkBN = 128;                     // weight rows per CTA
-constexpr int kSkBK = 128;                     // k bytes per stage (one swizzle span)
-constexpr int kSkStageBytes = kSkBN * kSkBK;   // 16 KiB
+constexpr int kSkStageBytes = 16384;
 constexpr int kSkConsumerWarps = 8;
 constexpr int kSkThreads = (kSkConsumerWarps + 1) * 32;
 
 __device__ __forceinline__ float pow2f(int e) { return __int_as_float((e + 127) << 23); }
 
-template <int MT, typename XT>
+// Timeline probe, compiled in only with -DQTTS_TRACE (never in the shipped
+// library): globaltimer stamps per CTA at each phase of the kernel.
+#ifdef QTTS_TRACE
+constexpr int kTraceEvents = 8;
+constexpr int kTraceSlots = 4096;
+__device__ unsigned long long g_trace[kTraceSlots][kTraceEvents];
+#define QTTS_TRACE_STAMP(ev)                                                             \
+  do {                                                                                   \
+    if (a.trace_slot >= 0) {                                                             \
+      const int _c = a.trace_slot * 256 + blockIdx.x + gridDim.x * blockIdx.y;           \
+      if (_c < kTraceSlots) g_trace[_c][ev] = globaltimer_ns();                          \
+    }                                                                                    \
+  } while (0)
+#else
+#define QTTS_TRACE_STAMP(ev) \
+  do {                       \
+  } while (0)
+#endif
+
+// 1-D bulk copy global -> this CTA's shared memory, completion counted on `bar`.
+__device__ __forceinline__ void bulk_load(void* dst, const void* src, uint32_t bytes, uint64_t* bar) {
+  asm volatile(
+      "cp.async.bulk.shared::cluster.global.mbarrier::complete_tx::bytes [%0], [%1], %2, [%3];" ::"r"(
+          smem_u32(dst)),
+      "l"(reinterpret_cast<uint64_t>(src)), "r"(bytes), "r"(smem_u32(bar))
+      : "memory");
+}
+
+template <int MT, int R, typename XT>
 __global__ void __launch_bounds__(kSkThreads, 2)
     skinny_w8a16_kernel(const __grid_constant__ CUtensorMap wmap, const SkinnyArgs a) {
-  constexpr int MB = MT * 8;  // batch rows per CTA (MMA N dimension)
+  constexpr int MB = MT * 8;       // batch rows per CTA (MMA N dimension)
+  constexpr int KG = 8 / R;        // k groups
+  constexpr int BN = 16 * R;       // weight rows per CTA
+  constexpr int SW = 128 * KG;     // k per stage
+  constexpr int NACC = MT <= 2 ? 2 : 1;  // independent accumulator sets (MMA latency)
   extern __shared__ uint8_t smem_raw[];
   uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
   uint8_t* wbuf = smem;
   __half* xs = reinterpret_cast<__half*>(smem + a.stages * kSkStageBytes);  // [MB][x_pitch]
   float* xinv = reinterpret_cast<float*>(xs + MB * a.x_pitch);               // [MB] 2^-scale
-  float* recv = xinv + MB;                                                   // [split][128/split][MB]
+  float* recv = xinv + MB;                                                   // [S][BN/S][MB]
+  const int split = gridDim.y;
   uint64_t* full = reinterpret_cast<uint64_t*>(
-      (reinterpret_cast<uintptr_t>(recv + (gridDim.y > 1 ? kSkBN * MB : 0)) + 15) & ~uintptr_t(15));
+      (reinterpret_cast<uintptr_t>(recv + (split > 1 ? BN * MB : 0)) + 15) & ~uintptr_t(15));
   uint64_t* empty = full + a.stages;
   uint64_t* recv_bar = empty + a.stages;
-  int* err_flag = reinterpret_cast<int*>(recv_bar + 1);
+  uint64_t* x_bar = recv_bar + 1;
+  int* err_flag = reinterpret_cast<int*>(x_bar + 1);
+  float* red = reinterpret_cast<float*>(wbuf);  // [KG][BN][MB], reuses the ring after the loop
 
   const int tid = threadIdx.x;
   const int warp = tid >> 5;
   const int lane = tid & 31;
-  const int split = gridDim.y;
   const int kidx = blockIdx.y;
   const uint32_t crank = split > 1 ? cluster_ctarank() : 0u;
-  const int rows_per_owner = kSkBN / split;
-  const int n0 = blockIdx.x * kSkBN;
+  const int rpo = BN / split;  // result rows owned per CTA
+  const int n0 = blockIdx.x * BN;
   const int mchunk = blockIdx.z % a.m_chunks;
   int group = blockIdx.z / a.m_chunks;
   const int m0 = mchunk * MB;
   const int k0 = kidx * a.k_per_cta;
   const int klen = max(0, min(a.K - k0, a.k_per_cta));
-  int n_iters = (klen + kSkBK - 1) / kSkBK;
+  int n_iters = (klen + SW - 1) / SW;
 
   if (tid == 0) {
+    QTTS_TRACE_STAMP(0);
     for (int s = 0; s < a.stages; ++s) {
       mbar_init(&full[s], 1);
       mbar_init(&empty[s], kSkConsumerWarps);
     }
     mbar_init(recv_bar, 1);
+    mbar_init(x_bar, 1);
+    for (int i = 0; i < MB; ++i) xinv[i] = 0.f;
     if (split > 1) {
       // The single arrival happens now; the phase completes once every peer's
-      // partial sums (split-1 slices) have landed.
-      mbar_arrive_expect_tx(recv_bar, static_cast<uint32_t>((split - 1) * rows_per_owner * MB * 4));
+      // partial sums for my rows have landed.
+      mbar_arrive_expect_tx(recv_bar, static_cast<uint32_t>((split - 1) * rpo * MB * 4));
     }
     *err_flag = 0;
     fence_mbarrier_init();
@@ -107,7 +145,7 @@ __global__ void __launch_bounds__(kSkThreads, 2)
     if (gi < 0 || gi >= a.G) {
       valid = false;
       n_iters = 0;
-      if (tid == 0 && kidx == 0) record_status(QTTS_ERR_SHAPE);
+      if (tid == 0 && kidx == 0 && blockIdx.x == 0) record_status(QTTS_ERR_SHAPE);
     } else {
       group = static_cast<int>(gi);
     }
@@ -134,8 +172,13 @@ __global__ void __launch_bounds__(kSkThreads, 2)
           }
         }
         mbar_arrive_expect_tx(&full[s], kSkStageBytes);
-        tma_load_2d(wbuf + s * kSkStageBytes, &wmap, k0 + it * kSkBK, static_cast<int>(wrow0), &full[s]);
+        uint8_t* dst = wbuf + s * kSkStageBytes;
+#pragma unroll
+        for (int c = 0; c < KG; ++c) {
+          tma_load_2d(dst + c * BN * 128, &wmap, k0 + it * SW + c * 128, static_cast<int>(wrow0), &full[s]);
+        }
         n_issued = it + 1;
+        if (it == 0) QTTS_TRACE_STAMP(1);
       }
     }
     __syncwarp();
@@ -143,84 +186,106 @@ __global__ void __launch_bounds__(kSkThreads, 2)
   } else {
     // ---------------- consumers ----------------
     pdl_wait();
-    const int kpad = n_iters * kSkBK;
-    // 1) Activation slice [MB, kpad] -> shared memory as raw 16-bit values,
-    //    zero padded past K and past the last batch row.
+    if (tid == 0) QTTS_TRACE_STAMP(2);
+    const int kpad = n_iters * SW;
+    // 1) Activation slice [MB, kpad]: each thread loads 16-byte chunks into
+    //    registers (zeros past K and past the last batch row), the per-row
+    //    maximum is combined with shared-memory atomics, then every thread
+    //    scales its own chunks to fp16 and stores them.
     {
-      constexpr int kVec = 8;  // 16-bit elements per 16-byte chunk
-      const int per_row = kpad / kVec;
-      for (int i = tid; i < MB * per_row; i += kSkConsumerWarps * 32) {
-        const int m = i / per_row;
-        const int kv = (i - m * per_row) * kVec;
-        uint4 v = make_uint4(0u, 0u, 0u, 0u);
+      const int cpr = kpad / 8;  // chunks per row
+      const int total = MB * cpr;
+      constexpr int kHeld = 4;
+      const bool in_regs = total <= kHeld * kSkConsumerWarps * 32;
+      uint4 held[kHeld];
+      const int nj = in_regs ? kHeld : (total + kSkConsumerWarps * 32 - 1) / (kSkConsumerWarps * 32);
+#pragma unroll 4
+      for (int j = 0; j < nj; ++j) {
+        const int ci = tid + kSkConsumerWarps * 32 * j;
+        if (ci >= total) break;
+        const int m = ci / cpr;
+        const int kv = (ci - m * cpr) * 8;
+        uint4 u = make_uint4(0u, 0u, 0u, 0u);
         if (valid && m < mrows && kv < klen) {
-          v = __ldcg(reinterpret_cast<const uint4*>(xg + static_cast<int64_t>(m) * a.ldx + k0 + kv));
+          u = __ldcg(reinterpret_cast<const uint4*>(xg + static_cast<int64_t>(m) * a.ldx + k0 + kv));
         }
-        *reinterpret_cast<uint4*>(xs + m * a.x_pitch + kv) = v;
-      }
-    }
-    named_bar_sync(1, kSkConsumerWarps * 32);
-    // 2) Per batch row: power-of-two scale that puts max|x| in [2^14, 2^15),
-    //    then convert in place to fp16 (exact for all but tiny elements).
-    for (int m = warp; m < MB; m += kSkConsumerWarps) {
-      uint4* row = reinterpret_cast<uint4*>(xs + m * a.x_pitch);
-      const int nvec = kpad / 8;
-      float mx = 0.f;
-      for (int v = lane; v < nvec; v += 32) {
-        const uint4 u = row[v];
         const XT* e = reinterpret_cast<const XT*>(&u);
+        float mx = 0.f;
 #pragma unroll
-        for (int j = 0; j < 8; ++j) mx = fmaxf(mx, fabsf(to_float(e[j])));
+        for (int q = 0; q < 8; ++q) mx = fmaxf(mx, fabsf(to_float(e[q])));
+        if (mx > 0.f) atomicMax(reinterpret_cast<unsigned int*>(&xinv[m]), __float_as_uint(mx));
+        if (in_regs) {
+          held[j & (kHeld - 1)] = u;
+        } else {
+          *reinterpret_cast<uint4*>(xs + m * a.x_pitch + kv) = u;  // raw; converted below
+        }
       }
-#pragma unroll
-      for (int o = 16; o > 0; o >>= 1) mx = fmaxf(mx, __shfl_xor_sync(0xffffffffu, mx, o));
-      int sexp = 0;
-      if (mx > 0.f) {
-        const int e = static_cast<int>((__float_as_uint(mx) >> 23) & 0xFF) - 127;  // floor(log2 mx), normal mx
-        sexp = min(max(14 - e, -100), 100);
-      }
-      const float sc = pow2f(sexp);
-      for (int v = lane; v < nvec; v += 32) {
-        const uint4 u = row[v];
+      named_bar_sync(1, kSkConsumerWarps * 32);
+#pragma unroll 4
+      for (int j = 0; j < nj; ++j) {
+        const int ci = tid + kSkConsumerWarps * 32 * j;
+        if (ci >= total) break;
+        const int m = ci / cpr;
+        const int kv = (ci - m * cpr) * 8;
+        uint4* dst = reinterpret_cast<uint4*>(xs + m * a.x_pitch + kv);
+        const uint4 u = in_regs ? held[j & (kHeld - 1)] : *dst;
+        const float mxr = xinv[m];
+        int sexp = 0;
+        if (mxr > 0.f) sexp = min(max(14 - (static_cast<int>((__float_as_uint(mxr) >> 23) & 0xFF) - 127), -100), 100);
+        const float sc = pow2f(sexp);
         const XT* e = reinterpret_cast<const XT*>(&u);
         uint4 o;
-        __half* h = reinterpret_cast<__half*>(&o);
+        __half2* h = reinterpret_cast<__half2*>(&o);
 #pragma unroll
-        for (int j = 0; j < 8; ++j) h[j] = __float2half_rn(to_float(e[j]) * sc);
-        row[v] = o;
+        for (int q = 0; q < 4; ++q) h[q] = __floats2half2_rn(to_float(e[2 * q]) * sc, to_float(e[2 * q + 1]) * sc);
+        *dst = o;
       }
-      if (lane == 0) xinv[m] = pow2f(-sexp);
+      named_bar_sync(1, kSkConsumerWarps * 32);
+      if (tid < MB) {
+        // xinv held the row maximum (as bits); turn it into 2^-scale.
+        const float mxr = xinv[tid];
+        int sexp = 0;
+        if (mxr > 0.f) sexp = min(max(14 - (static_cast<int>((__float_as_uint(mxr) >> 23) & 0xFF) - 127), -100), 100);
+        xinv[tid] = pow2f(-sexp);
+      }
     }
     named_bar_sync(1, kSkConsumerWarps * 32);
+    if (tid == 0) QTTS_TRACE_STAMP(3);
 
-    // 3) Main loop.
+    // 2) Main loop.
+    const int rg = warp / KG;  // row group
+    const int kg = warp % KG;  // k group (which 128-byte box of the stage)
     const int g = lane >> 2;
     const int q = lane & 3;
     // MMA row g <-> weight row permutation: the rows of one shared-load phase
     // (g = 2p, 2p+1 -> p, p+4) land in opposite 64-byte halves of the span.
     const int pr = (g >> 1) | ((g & 1) << 2);
-    const int rowA = warp * 16 + pr;
+    const int rowA = rg * 16 + pr;
     const int rowB = rowA + 8;
+    const uint32_t box = kg * BN * 128;
+    const uint32_t offA0 = box + rowA * 128 + (((0 * 4 + q) ^ (rowA & 7)) << 4);
+    const uint32_t offA1 = box + rowA * 128 + (((1 * 4 + q) ^ (rowA & 7)) << 4);
+    const uint32_t offB0 = box + rowB * 128 + (((0 * 4 + q) ^ (rowB & 7)) << 4);
+    const uint32_t offB1 = box + rowB * 128 + (((1 * 4 + q) ^ (rowB & 7)) << 4);
     const uint32_t wbase = smem_u32(wbuf);
-    const uint32_t offA0 = rowA * kSkBK + (((0 * 4 + q) ^ (rowA & 7)) << 4);
-    const uint32_t offA1 = rowA * kSkBK + (((1 * 4 + q) ^ (rowA & 7)) << 4);
-    const uint32_t offB0 = rowB * kSkBK + (((0 * 4 + q) ^ (rowB & 7)) << 4);
-    const uint32_t offB1 = rowB * kSkBK + (((1 * 4 + q) ^ (rowB & 7)) << 4);
-    const uint32_t xbase = smem_u32(xs) + (g * a.x_pitch + q * 16) * 2;
+    const uint32_t xbase = smem_u32(xs) + (g * a.x_pitch + kg * 128 + q * 16) * 2;
     const uint32_t xtile = 8 * a.x_pitch * 2;
 
-    float acc[MT][4];
+    float acc[NACC][MT][4];
 #pragma unroll
-    for (int t = 0; t < MT; ++t) acc[t][0] = acc[t][1] = acc[t][2] = acc[t][3] = 0.f;
+    for (int i = 0; i < NACC; ++i)
+#pragma unroll
+      for (int t = 0; t < MT; ++t) acc[i][t][0] = acc[i][t][1] = acc[i][t][2] = acc[i][t][3] = 0.f;
 
-    bool ok = true;
-    for (int it = 0; it < n_iters; ++it) {
+    bool ok = *reinterpret_cast<volatile int*>(err_flag) == 0;
+    for (int it = 0; ok && it < n_iters; ++it) {
       const int s = it % a.stages;
       const bool got = mbar_wait_bounded(&full[s], (it / a.stages) & 1, a.wait_ns);
       if (!__all_sync(0xffffffffu, got)) {
         ok = false;
         break;
       }
+      if (it == 0 && tid == 0) QTTS_TRACE_STAMP(4);
       const uint32_t sb = wbase + s * kSkStageBytes;
       const uint4 wa0 = lds128(sb + offA0);
       const uint4 wb0 = lds128(sb + offB0);
@@ -247,18 +312,19 @@ __global__ void __launch_bounds__(kSkThreads, 2)
       i8x4_to_f16x2x2(wa1.w, A[1][3][0], A[1][3][2]);
       i8x4_to_f16x2x2(wb1.w, A[1][3][1], A[1][3][3]);
 
-      const uint32_t xk = xbase + it * kSkBK * 2;
+      const uint32_t xk = xbase + it * SW * 2;
 #pragma unroll
       for (int t = 0; t < MT; ++t) {
 #pragma unroll
         for (int h = 0; h < 2; ++h) {
+          float(&c)[4] = acc[h % NACC][t];
           const uint32_t xa = xk + t * xtile + h * 64 * 2;
           const uint4 x0 = lds128(xa);
           const uint4 x1 = lds128(xa + 16);
-          Mma16816<__half>::run(acc[t], A[h][0], x0.x, x0.y);
-          Mma16816<__half>::run(acc[t], A[h][1], x0.z, x0.w);
-          Mma16816<__half>::run(acc[t], A[h][2], x1.x, x1.y);
-          Mma16816<__half>::run(acc[t], A[h][3], x1.z, x1.w);
+          Mma16816<__half>::run(c, A[h][0], x0.x, x0.y);
+          Mma16816<__half>::run(c, A[h][1], x0.z, x0.w);
+          Mma16816<__half>::run(c, A[h][2], x1.x, x1.y);
+          Mma16816<__half>::run(c, A[h][3], x1.z, x1.w);
         }
       }
     }
@@ -266,80 +332,92 @@ __global__ void __launch_bounds__(kSkThreads, 2)
       if (lane == 0) record_status(QTTS_ERR_TIMEOUT);
       *reinterpret_cast<volatile int*>(err_flag) = 1;
     }
-
-    // 4) Undo the activation scale; hand the partial sums to their owner.
-    float v[MT][4];
+    if (tid == 0) QTTS_TRACE_STAMP(5);
+    // Every warp is done with the stage ring before it becomes `red`.
+    named_bar_sync(1, kSkConsumerWarps * 32);
+    const bool cta_err = *reinterpret_cast<volatile int*>(err_flag) != 0;
+    if (!cta_err) {
 #pragma unroll
-    for (int t = 0; t < MT; ++t) {
-      const int c0 = t * 8 + 2 * q;
-      const float i0 = xinv[c0];
-      const float i1 = xinv[c0 + 1];
-      v[t][0] = acc[t][0] * i0;
-      v[t][1] = acc[t][1] * i1;
-      v[t][2] = acc[t][2] * i0;
-      v[t][3] = acc[t][3] * i1;
+      for (int t = 0; t < MT; ++t) {
+        const int c0 = t * 8 + 2 * q;
+        const float i0 = xinv[c0];
+        const float i1 = xinv[c0 + 1];
+        float v0 = acc[0][t][0], v1 = acc[0][t][1], v2 = acc[0][t][2], v3 = acc[0][t][3];
+        if (NACC > 1) {
+          v0 += acc[NACC - 1][t][0];
+          v1 += acc[NACC - 1][t][1];
+          v2 += acc[NACC - 1][t][2];
+          v3 += acc[NACC - 1][t][3];
+        }
+        float* r = red + kg * BN * MB;
+        *reinterpret_cast<float2*>(&r[rowA * MB + c0]) = make_float2(v0 * i0, v1 * i1);
+        *reinterpret_cast<float2*>(&r[rowB * MB + c0]) = make_float2(v2 * i0, v3 * i1);
+      }
     }
+    named_bar_sync(1, kSkConsumerWarps * 32);
+    // 3) Sum the k groups in fixed order: red[0] = CTA partial sums [BN][MB].
+    if (KG > 1 && !cta_err) {
+      for (int i = tid; i < BN * MB; i += kSkConsumerWarps * 32) {
+        float sum = red[i];
+#pragma unroll
+        for (int c = 1; c < KG; ++c) sum += red[c * BN * MB + i];
+        red[i] = sum;
+      }
+      named_bar_sync(1, kSkConsumerWarps * 32);
+    }
+
     if (split == 1) {
-      // This warp owns its 16 rows outright: finish them from registers.
-      const bool store = valid && *reinterpret_cast<volatile int*>(err_flag) == 0;
-      if (store) {
-#pragma unroll
-        for (int t = 0; t < MT; ++t) {
-#pragma unroll
-          for (int e = 0; e < 4; ++e) {
-            const int row = (e < 2) ? rowA : rowB;
-            const int m = t * 8 + 2 * q + (e & 1);
-            const int n = n0 + row;
-            if (m < mrows && n < a.N) {
-              const int64_t ch = static_cast<int64_t>(group) * a.N + n;
-              float r = v[t][e] * load_as_float(a.scale, a.scale_dtype, ch);
-              if (a.bias != nullptr) r += to_float(static_cast<const XT*>(a.bias)[ch]);
-              og[static_cast<int64_t>(m) * a.ldo + n] = from_float<XT>(r);
-            }
+      if (valid && !cta_err) {
+        for (int i = tid; i < BN * mrows; i += kSkConsumerWarps * 32) {
+          const int m = i / BN;
+          const int row = i - m * BN;
+          const int n = n0 + row;
+          if (n < a.N) {
+            const int64_t ch = static_cast<int64_t>(group) * a.N + n;
+            float r = red[row * MB + m] * load_as_float(a.scale, a.scale_dtype, ch);
+            if (a.bias != nullptr) r += to_float(static_cast<const XT*>(a.bias)[ch]);
+            og[static_cast<int64_t>(m) * a.ldo + n] = from_float<XT>(r);
           }
         }
       }
     } else {
+      // 4) Hand each row's partial sums to the CTA that owns the row.
       cluster_wait();  // every peer's receive barrier is initialized
-      const int owner = (warp * 16) / rows_per_owner;
-      const int lrA = rowA - owner * rows_per_owner;
-      const int lrB = rowB - owner * rows_per_owner;
-      float* slot = recv + (crank * rows_per_owner) * MB;  // my slice in the owner's buffer
-      if (owner == static_cast<int>(crank)) {
-#pragma unroll
-        for (int t = 0; t < MT; ++t) {
-          const int c0 = t * 8 + 2 * q;
-          *reinterpret_cast<float2*>(&slot[lrA * MB + c0]) = make_float2(v[t][0], v[t][1]);
-          *reinterpret_cast<float2*>(&slot[lrB * MB + c0]) = make_float2(v[t][2], v[t][3]);
+      for (int i = tid; i < BN * (MB / 2); i += kSkConsumerWarps * 32) {
+        const int row = i / (MB / 2);
+        const int cp = (i - row * (MB / 2)) * 2;
+        const int owner = row / rpo;
+        const int lr = row - owner * rpo;
+        float v0 = 0.f, v1 = 0.f;
+        if (!cta_err) {
+          v0 = red[row * MB + cp];
+          v1 = red[row * MB + cp + 1];
         }
-      } else {
-        const uint32_t rslot = mapa_shared(smem_u32(slot), owner);
-        const uint32_t rbar = mapa_shared(smem_u32(recv_bar), owner);
-#pragma unroll
-        for (int t = 0; t < MT; ++t) {
-          const int c0 = t * 8 + 2 * q;
-          st_async_f32x2(rslot + (lrA * MB + c0) * 4, v[t][0], v[t][1], rbar);
-          st_async_f32x2(rslot + (lrB * MB + c0) * 4, v[t][2], v[t][3], rbar);
+        float* dst = recv + (crank * rpo + lr) * MB + cp;
+        if (owner == static_cast<int>(crank)) {
+          *reinterpret_cast<float2*>(dst) = make_float2(v0, v1);
+        } else {
+          st_async_f32x2(mapa_shared(smem_u32(dst), owner), v0, v1, mapa_shared(smem_u32(recv_bar), owner));
         }
       }
-      // 5) Owner: reduce the split partial sums of its rows in rank order.
       named_bar_sync(1, kSkConsumerWarps * 32);
+      // 5) Owner: reduce the split partial sums of its rows in rank order.
       bool have = mbar_wait_bounded(recv_bar, 0, a.wait_ns);
       if (!have) {
         if (tid == 0) record_status(QTTS_ERR_TIMEOUT);
         // Peers always send; keep this CTA alive until their stores land.
         have = mbar_wait_bounded(recv_bar, 0, 4 * a.wait_ns);
       }
-      const bool store = have && valid && *reinterpret_cast<volatile int*>(err_flag) == 0;
-      if (store) {
-        const int rbase = static_cast<int>(crank) * rows_per_owner;
-        for (int i = tid; i < rows_per_owner * mrows; i += kSkConsumerWarps * 32) {
-          const int m = i / rows_per_owner;
-          const int lr = i - m * rows_per_owner;
+      if (tid == 0) QTTS_TRACE_STAMP(7);
+      if (have && valid && !cta_err) {
+        const int rbase = static_cast<int>(crank) * rpo;
+        for (int i = tid; i < rpo * mrows; i += kSkConsumerWarps * 32) {
+          const int m = i / rpo;
+          const int lr = i - m * rpo;
           const int n = n0 + rbase + lr;
           if (n < a.N) {
             float r = 0.f;
-            for (int p = 0; p < split; ++p) r += recv[(p * rows_per_owner + lr) * MB + m];
+            for (int p = 0; p < split; ++p) r += recv[(p * rpo + lr) * MB + m];
             const int64_t ch = static_cast<int64_t>(group) * a.N + n;
             r *= load_as_float(a.scale, a.scale_dtype, ch);
             if (a.bias != nullptr) r += to_float(static_cast<const XT*>(a.bias)[ch]);
@@ -350,6 +428,7 @@ __global__ void __launch_bounds__(kSkThreads, 2)
     }
   }
 
+  if (tid == 0) QTTS_TRACE_STAMP(6);
   // Error path: make sure no copy of ours is still landing in shared memory.
   if (warp == kSkConsumerWarps && lane == 0 && *reinterpret_cast<volatile int*>(err_flag) != 0) {
     for (int s = 0; s < a.stages && s < n_issued; ++s) {
@@ -364,10 +443,10 @@ __global__ void __launch_bounds__(kSkThreads, 2)
 
 namespace {
 
-template <int MT, typename XT>
+template <int MT, int R, typename XT>
 int launch_skinny_t(const CUtensorMap& map, const SkinnyArgs& args, dim3 grid, int split, size_t smem,
                     bool pdl, cudaStream_t stream) {
-  auto kern = skinny_w8a16_kernel<MT, XT>;
+  auto kern = skinny_w8a16_kernel<MT, R, XT>;
   static int configured[64] = {0};
   int dev = 0;
   cudaGetDevice(&dev);
@@ -402,76 +481,117 @@ int launch_skinny_t(const CUtensorMap& map, const SkinnyArgs& args, dim3 grid, i
   return e == cudaSuccess ? QTTS_OK : QTTS_ERR_LAUNCH;
 }
 
-template <typename XT>
-int launch_skinny_mt(int mt, const CUtensorMap& map, const SkinnyArgs& args, dim3 grid, int split,
-                     size_t smem, bool pdl, cudaStream_t stream) {
-  switch (mt) {
+template <int MT, typename XT>
+int launch_skinny_r(int r, const CUtensorMap& map, const SkinnyArgs& args, dim3 grid, int split, size_t smem,
+                    bool pdl, cudaStream_t stream) {
+  switch (r) {
     case 1:
-      return launch_skinny_t<1, XT>(map, args, grid, split, smem, pdl, stream);
+      return launch_skinny_t<MT, 1, XT>(map, args, grid, split, smem, pdl, stream);
     case 2:
-      return launch_skinny_t<2, XT>(map, args, grid, split, smem, pdl, stream);
+      return launch_skinny_t<MT, 2, XT>(map, args, grid, split, smem, pdl, stream);
     case 4:
-      return launch_skinny_t<4, XT>(map, args, grid, split, smem, pdl, stream);
+      return launch_skinny_t<MT, 4, XT>(map, args, grid, split, smem, pdl, stream);
     default:
-      return launch_skinny_t<8, XT>(map, args, grid, split, smem, pdl, stream);
+      return launch_skinny_t<MT, 8, XT>(map, args, grid, split, smem, pdl, stream);
   }
 }
 
-size_t skinny_smem(int mb, int x_pitch, int stages, int split) {
-  const size_t xbytes = static_cast<size_t>(mb) * x_pitch * 2 + mb * 4;
-  const size_t recv = split > 1 ? static_cast<size_t>(kSkBN) * mb * 4 : 0;
-  return 1024 + static_cast<size_t>(stages) * kSkStageBytes + xbytes + recv + 16 + 16 * stages + 32;
+template <typename XT>
+int launch_skinny_mt(const SkinnyPlan& p, const CUtensorMap& map, const SkinnyArgs& args, bool pdl,
+                     cudaStream_t stream) {
+  switch (p.mt) {
+    case 1:
+      return launch_skinny_r<1, XT>(p.r, map, args, p.grid, p.split, p.smem, pdl, stream);
+    case 2:
+      return launch_skinny_r<2, XT>(p.r, map, args, p.grid, p.split, p.smem, pdl, stream);
+    case 4:
+      return launch_skinny_r<4, XT>(p.r, map, args, p.grid, p.split, p.smem, pdl, stream);
+    default:
+      return launch_skinny_r<8, XT>(p.r, map, args, p.grid, p.split, p.smem, pdl, stream);
+  }
 }
+
+size_t skinny_smem(int mb, int bn, int x_pitch, int stages, int split) {
+  const size_t xbytes = static_cast<size_t>(mb) * x_pitch * 2 + mb * 4;
+  const size_t recv = split > 1 ? static_cast<size_t>(bn) * mb * 4 : 0;
+  return 1024 + static_cast<size_t>(stages) * kSkStageBytes + xbytes + recv + 16 + 16 * stages + 48;
+}
+
+int kpc_for(int K, int split, int sw) { return ((K + split - 1) / split + sw - 1) / sw * sw; }
 
 }  // namespace
 
-SkinnyPlan plan_skinny(int M, int N, int K, int G, int split_req) {
+SkinnyPlan plan_skinny(int M, int N, int K, int G, int split_req, int r_req) {
   SkinnyPlan p{};
   p.mt = M <= 8 ? 1 : (M <= 16 ? 2 : (M <= 32 ? 4 : 8));
   const int mb = p.mt * 8;
   p.m_chunks = (M + mb - 1) / mb;
-  const int n_tiles = (N + kSkBN - 1) / kSkBN;
-  const int ctas_base = n_tiles * G * p.m_chunks;
-  auto kpc_for = [&](int split) { return ((K + split - 1) / split + kSkBK - 1) / kSkBK * kSkBK; };
-  int split = split_req;
+  const size_t x_cap = 64 * 1024;
+  auto xbytes = [&](int s, int r) { return static_cast<size_t>(mb) * (kpc_for(K, s, 128 * (8 / r)) + 8) * 2; };
+  auto ctas = [&](int s, int r) { return ((N + 16 * r - 1) / (16 * r)) * s * G * p.m_chunks; };
+  const int splits[4] = {1, 2, 4, 8};
+  int split = split_req, r = r_req;
+  if (r == 0) r = 8;  // 128-row tiles: no k-group reduction inside the CTA
   if (split == 0) {
-    // Smallest split that puts a CTA on (most of) the 148 SMs while the
-    // activation slice stays within 48 KiB of shared memory; the largest
-    // otherwise.
+    // Smallest cluster split that puts ~a CTA on each of the 148 SMs with the
+    // activation slice in 48 KiB; the largest otherwise.
     split = 8;
-    for (int s = 1; s <= 8; s *= 2) {
-      const size_t xb = static_cast<size_t>(mb) * (kpc_for(s) + 8) * 2;
-      if (xb <= 48 * 1024 && ctas_base * s >= 120) {
-        split = s;
+    for (int si = 0; si < 4; ++si) {
+      const int s_ = splits[si];
+      if (xbytes(s_, r) <= 48 * 1024 && ctas(s_, r) >= 120) {
+        split = s_;
         break;
       }
     }
   }
+  (void)x_cap;
   p.split = split;
-  p.k_per_cta = kpc_for(split);
+  p.r = r;
+  const int bn = 16 * r;
+  const int sw = 128 * (8 / r);
+  p.k_per_cta = kpc_for(K, split, sw);
   p.x_pitch = p.k_per_cta + 8;  // +16 bytes: rows of one LDS phase hit distinct banks
-  const int n_iters = p.k_per_cta / kSkBK;
+  const int n_iters = p.k_per_cta / sw;
   // Stage ring: fill a ~100 KiB budget (so the next kernel's CTA fits beside
   // this one under programmatic dependent launch), 2..6 stages, never more
-  // than the slice needs.
-  const size_t fixed = skinny_smem(mb, p.x_pitch, 0, split);
+  // than the slice needs; at least enough to hold the k-group reduction.
+  const size_t fixed = skinny_smem(mb, bn, p.x_pitch, 0, split);
   const size_t budget = 100 * 1024;
   int stages = fixed < budget ? static_cast<int>((budget - fixed) / kSkStageBytes) : 0;
   stages = stages > 6 ? 6 : stages;
   stages = stages < n_iters ? stages : n_iters;
+  const int min_stages = (512 * mb + kSkStageBytes - 1) / kSkStageBytes;
+  stages = stages < min_stages ? min_stages : stages;
   stages = stages < 2 ? 2 : stages;
   p.stages = stages;
-  p.smem = skinny_smem(mb, p.x_pitch, stages, split);
-  p.grid = dim3(n_tiles, split, G * p.m_chunks);
+  p.smem = skinny_smem(mb, bn, p.x_pitch, stages, split);
+  p.grid = dim3((N + bn - 1) / bn, split, G * p.m_chunks);
   return p;
 }
 
 int launch_skinny_w8a16(const SkinnyPlan& p, const CUtensorMap& map, const SkinnyArgs& args, int x_dtype,
                         bool pdl, cudaStream_t stream) {
   if (p.smem > kMaxDynSmem) return QTTS_ERR_VARIANT;
-  if (x_dtype == QTTS_BF16) return launch_skinny_mt<__nv_bfloat16>(p.mt, map, args, p.grid, p.split, p.smem, pdl, stream);
-  if (x_dtype == QTTS_FP16) return launch_skinny_mt<__half>(p.mt, map, args, p.grid, p.split, p.smem, pdl, stream);
+  if (x_dtype == QTTS_BF16) return launch_skinny_mt<__nv_bfloat16>(p, map, args, pdl, stream);
+  if (x_dtype == QTTS_FP16) return launch_skinny_mt<__half>(p, map, args, pdl, stream);
   return QTTS_ERR_DTYPE;
 }
 
 }  // namespace qtts
+
+#ifdef QTTS_TRACE
+#include <atomic>
+namespace qtts {
+static std::atomic<int> g_trace_slot{0};
+int qtts_trace_next_slot() { return g_trace_slot.fetch_add(1) % 16; }
+}  // namespace qtts
+extern "C" __attribute__((visibility("default"))) int qtts_trace_read(void* dst, size_t bytes) {
+  return cudaMemcpyFromSymbol(dst, qtts::g_trace, bytes) == cudaSuccess ? 0 : 9;
+}
+extern "C" __attribute__((visibility("default"))) void qtts_trace_reset(void) { qtts::g_trace_slot = 0; }
+extern "C" __attribute__((visibility("default"))) int qtts_trace_clear(void) {
+  void* p = nullptr;
+  if (cudaGetSymbolAddress(&p, qtts::g_trace) != cudaSuccess) return 9;
+  return cudaMemset(p, 0, sizeof(qtts::g_trace)) == cudaSuccess ? 0 : 9;
+}
+#endif

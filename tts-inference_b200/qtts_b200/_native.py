@@ -37,8 +37,9 @@ VARIANT_AUTO = 0
 VARIANT_GENERIC = 1
 
 
-def variant_skinny(split: int) -> int:
-    return 0x100 | split
+def variant_skinny(split: int, rows: int = 0) -> int:
+    """Skinny kernel: K split over `split` clustered CTAs, `rows` row groups of 16 per CTA (0 = choose)."""
+    return 0x100 | split | (rows << 4)
 
 
 def variant_umma(split: int) -> int:
