@@ -308,6 +308,22 @@ int make_tmap_u8_2d(CUtensorMap* map, const void* base, uint64_t rows, uint64_t 
   return r == CUDA_SUCCESS ? QTTS_OK : QTTS_ERR_ALIGN;
 }
 
+int make_tmap_16b_2d(CUtensorMap* map, const void* base, int dtype, uint64_t rows, uint64_t cols,
+                     uint64_t pitch_bytes, uint32_t box_rows, uint32_t box_cols) {
+  EncodeTiledFn fn = get_encode_fn();
+  if (fn == nullptr) return QTTS_ERR_ARCH;
+  const cuuint64_t dims[2] = {cols, rows};
+  const cuuint64_t strides[1] = {pitch_bytes};
+  const cuuint32_t box[2] = {box_cols, box_rows};
+  const cuuint32_t estr[2] = {1, 1};
+  const CUtensorMapDataType t =
+      dtype == QTTS_BF16 ? CU_TENSOR_MAP_DATA_TYPE_BFLOAT16 : CU_TENSOR_MAP_DATA_TYPE_FLOAT16;
+  const CUresult r = fn(map, t, 2, const_cast<void*>(base), dims, strides, box, estr, CU_TENSOR_MAP_INTERLEAVE_NONE,
+                        CU_TENSOR_MAP_SWIZZLE_128B, CU_TENSOR_MAP_L2_PROMOTION_L2_128B,
+                        CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
+  return r == CUDA_SUCCESS ? QTTS_OK : QTTS_ERR_ALIGN;
+}
+
 }  // namespace qtts
 
 using namespace qtts;
@@ -384,9 +400,9 @@ static int w8a16_dispatch(const void* x, int64_t gsx, int64_t ldx, int x_dtype, 
   int split = variant & 0xF;
   int rgroups = (variant >> 4) & 0xF;
   if (variant == QTTS_VARIANT_AUTO) {
-    // Decode rows (M <= 8): the mma.sync streaming kernel; wider batches: the
-    // tcgen05 kernel, whose MMA cost does not grow with M.
-    family = skinny_ok ? (M <= 8 ? 0x100 : 0x200) : 0;
+    // Up to 16 rows: the mma.sync streaming kernel. Wider batches: the
+    // tcgen05 kernel, whose per-instruction cost does not grow with M.
+    family = skinny_ok ? (M <= 16 ? 0x100 : 0x200) : 0;
     split = 0;
     rgroups = 0;
   }
@@ -440,12 +456,18 @@ static int w8a16_dispatch(const void* x, int64_t gsx, int64_t ldx, int x_dtype, 
     if (!(split == 0 || split == 1 || split == 2 || split == 4 || split == 8) || rgroups != 0) return QTTS_ERR_VARIANT;
     if ((variant & 0xF000) != 0) return QTTS_ERR_VARIANT;
     const int zg = group_index != nullptr ? 1 : G;
+    if (group_index == nullptr && G > 1 && gsx % ldx != 0) return QTTS_ERR_ALIGN;
     const SkinnyPlan plan = plan_umma(M, N, K, zg, split);
     if (plan.grid.z > 65535u) return QTTS_ERR_SHAPE;
     if (plan.smem > kMaxDynSmem) return QTTS_ERR_VARIANT;
-    CUtensorMap map;
+    CUtensorMap map, xmap;
     const uint64_t rows = static_cast<uint64_t>(G) * N;
-    const int r = make_tmap_u8_2d(&map, w, rows, static_cast<uint64_t>(K), static_cast<uint64_t>(ldw), 128, 128);
+    int r = make_tmap_u8_2d(&map, w, rows, static_cast<uint64_t>(K), static_cast<uint64_t>(ldw), 128, 128);
+    if (r != QTTS_OK) return r;
+    const int64_t gsx_rows = (group_index == nullptr && G > 1) ? gsx / ldx : 0;
+    const uint64_t xrows = static_cast<uint64_t>(gsx_rows) * (group_index == nullptr ? G - 1 : 0) + M;
+    r = make_tmap_16b_2d(&xmap, x, x_dtype, xrows, static_cast<uint64_t>(K), static_cast<uint64_t>(ldx) * 2,
+                         static_cast<uint32_t>(plan.mt * 8), 64);
     if (r != QTTS_OK) return r;
     SkinnyArgs sa{};
     sa.x = x;
@@ -463,12 +485,16 @@ static int w8a16_dispatch(const void* x, int64_t gsx, int64_t ldx, int x_dtype, 
     sa.G = G;
     sa.k_per_cta = plan.k_per_cta;
     sa.stages = plan.stages;
-    sa.x_pitch = 0;
+    sa.x_pitch = plan.x_pitch;  // activation ring depth
     sa.m_chunks = plan.m_chunks;
     sa.group_index = group_index;
     sa.wait_ns = current_wait_limit_ns();
     sa.trace_slot = -1;
-    return launch_umma_w8a16(plan, map, sa, x_dtype, pdl, stream);
+#ifdef QTTS_TRACE
+    sa.trace_slot = qtts_trace_next_slot();
+#endif
+    sa.gsx_rows = gsx_rows;
+    return launch_umma_w8a16(plan, map, xmap, sa, x_dtype, pdl, stream);
   }
   return QTTS_ERR_VARIANT;
 }

@@ -203,6 +203,30 @@ __host__ __device__ constexpr uint32_t umma_idesc(uint32_t a_fmt, uint32_t b_fmt
          (static_cast<uint32_t>(m >> 4) << 24);
 }
 
+// Bulk copy from this CTA's shared memory into a peer CTA's shared memory
+// (shared::cluster address), counted in bytes on the peer's mbarrier. Both
+// addresses 16-byte aligned, size a multiple of 16. The source must have been
+// made visible to the async proxy (fence_proxy_async_smem) first.
+__device__ __forceinline__ void bulk_s2s_cluster(uint32_t dst_cluster, const void* src, uint32_t bytes,
+                                                 uint32_t bar_cluster) {
+  asm volatile("cp.async.bulk.shared::cluster.shared::cta.mbarrier::complete_tx::bytes [%0], [%1], %2, [%3];" ::"r"(
+                   dst_cluster),
+               "r"(smem_u32(src)), "r"(bytes), "r"(bar_cluster)
+               : "memory");
+}
+// Waits until this thread's bulk copies have finished reading their sources.
+__device__ __forceinline__ void bulk_wait_read() {
+  asm volatile("cp.async.bulk.commit_group;\ncp.async.bulk.wait_group.read 0;" ::: "memory");
+}
+
+__device__ __forceinline__ void st_async_f32x4(uint32_t remote_addr, float a, float b, float c, float d,
+                                               uint32_t remote_bar) {
+  asm volatile("st.async.shared::cluster.mbarrier::complete_tx::bytes.v4.f32 [%0], {%1, %2, %3, %4}, [%5];" ::"r"(
+                   remote_addr),
+               "f"(a), "f"(b), "f"(c), "f"(d), "r"(remote_bar)
+               : "memory");
+}
+
 // ---- programmatic dependent launch ------------------------------------------
 
 // Blocks until the preceding grid of the stream has completed and its memory
@@ -345,5 +369,35 @@ template <>
 __device__ __forceinline__ float to_float<float>(float v) {
   return v;
 }
+
+// Timeline probe, compiled in only with -DQTTS_TRACE (never in the shipped
+// library): globaltimer stamps per CTA at each phase of a kernel, read back by
+// qtts_trace_read(). `a` must be the kernel's argument block (trace_slot).
+#ifdef QTTS_TRACE
+constexpr int kTraceEvents = 8;
+constexpr int kTraceSlots = 4096;
+extern __device__ unsigned long long g_trace[kTraceSlots][kTraceEvents];
+#define QTTS_TRACE_STAMP(ev)                                                             \
+  do {                                                                                   \
+    if (a.trace_slot >= 0) {                                                             \
+      const int _c = a.trace_slot * 256 + blockIdx.x + gridDim.x * blockIdx.y;           \
+      if (_c < kTraceSlots) g_trace[_c][ev] = globaltimer_ns();                          \
+    }                                                                                    \
+  } while (0)
+// Per-step stamps of CTA (0,0,0) of trace slot 5: g_trace_detail[kind][step].
+extern __device__ unsigned long long g_trace_detail[8][64];
+#define QTTS_TRACE_DETAIL(kind, step)                                                               \
+  do {                                                                                              \
+    if (a.trace_slot == 5 && blockIdx.x == 0 && blockIdx.y == 0 && blockIdx.z == 0 && (step) < 64) \
+      g_trace_detail[kind][step] = globaltimer_ns();                                                \
+  } while (0)
+#else
+#define QTTS_TRACE_DETAIL(kind, step) \
+  do {                                \
+  } while (0)
+#define QTTS_TRACE_STAMP(ev) \
+  do {                       \
+  } while (0)
+#endif
 
 }  // namespace qtts

@@ -34,6 +34,7 @@ struct SkinnyArgs {
   const int64_t* group_index;  // device pointer or NULL
   uint64_t wait_ns;
   int trace_slot;  // timeline probe slot (-1: off); only read in -DQTTS_TRACE builds
+  int64_t gsx_rows;  // group stride of x in rows (tcgen05 kernel: x is read through a tensor map)
 };
 
 struct SkinnyPlan {
@@ -55,14 +56,18 @@ int launch_skinny_w8a16(const SkinnyPlan& p, const CUtensorMap& map, const Skinn
 
 // ---- tcgen05 W8A16 (same argument block; plan.mt = NB/8, plan.r = 8) ----------
 SkinnyPlan plan_umma(int M, int N, int K, int G, int split_req);
-int launch_umma_w8a16(const SkinnyPlan& p, const CUtensorMap& map, const SkinnyArgs& args, int x_dtype, bool pdl,
-                      cudaStream_t stream);
+int launch_umma_w8a16(const SkinnyPlan& p, const CUtensorMap& wmap, const CUtensorMap& xmap, const SkinnyArgs& args,
+                      int x_dtype, bool pdl, cudaStream_t stream);
 
 // ---- tensor maps ---------------------------------------------------------------
 // 2-D uint8 tensor map over a row-major [rows, cols] byte matrix with row pitch
 // `pitch_bytes`, box [box_rows, box_cols] and 128-byte swizzle.
 int make_tmap_u8_2d(CUtensorMap* map, const void* base, uint64_t rows, uint64_t cols, uint64_t pitch_bytes,
                     uint32_t box_rows, uint32_t box_cols);
+// Same for a 16-bit element matrix (dtype QTTS_BF16 or QTTS_FP16); cols and
+// box_cols in elements.
+int make_tmap_16b_2d(CUtensorMap* map, const void* base, int dtype, uint64_t rows, uint64_t cols,
+                     uint64_t pitch_bytes, uint32_t box_rows, uint32_t box_cols);
 
 uint64_t current_wait_limit_ns();
 

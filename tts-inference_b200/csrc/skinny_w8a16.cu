@@ -50,25 +50,6 @@ constexpr int kSkThreads = (kSkConsumerWarps + 1) * 32;
 
 __device__ __forceinline__ float pow2f(int e) { return __int_as_float((e + 127) << 23); }
 
-// Timeline probe, compiled in only with -DQTTS_TRACE (never in the shipped
-// library): globaltimer stamps per CTA at each phase of the kernel.
-#ifdef QTTS_TRACE
-constexpr int kTraceEvents = 8;
-constexpr int kTraceSlots = 4096;
-__device__ unsigned long long g_trace[kTraceSlots][kTraceEvents];
-#define QTTS_TRACE_STAMP(ev)                                                             \
-  do {                                                                                   \
-    if (a.trace_slot >= 0) {                                                             \
-      const int _c = a.trace_slot * 256 + blockIdx.x + gridDim.x * blockIdx.y;           \
-      if (_c < kTraceSlots) g_trace[_c][ev] = globaltimer_ns();                          \
-    }                                                                                    \
-  } while (0)
-#else
-#define QTTS_TRACE_STAMP(ev) \
-  do {                       \
-  } while (0)
-#endif
-
 // 1-D bulk copy global -> this CTA's shared memory, completion counted on `bar`.
 __device__ __forceinline__ void bulk_load(void* dst, const void* src, uint32_t bytes, uint64_t* bar) {
   asm volatile(
@@ -182,7 +163,6 @@ __global__ void __launch_bounds__(kSkThreads, 2)
       }
     }
     __syncwarp();
-    if (split > 1) cluster_wait();
   } else {
     // ---------------- consumers ----------------
     pdl_wait();
@@ -381,31 +361,27 @@ __global__ void __launch_bounds__(kSkThreads, 2)
         }
       }
     } else {
-      // 4) Hand each row's partial sums to the CTA that owns the row.
-      cluster_wait();  // every peer's receive barrier is initialized
-      for (int i = tid; i < BN * (MB / 2); i += kSkConsumerWarps * 32) {
-        const int row = i / (MB / 2);
-        const int cp = (i - row * (MB / 2)) * 2;
-        const int owner = row / rpo;
-        const int lr = row - owner * rpo;
-        float v0 = 0.f, v1 = 0.f;
-        if (!cta_err) {
-          v0 = red[row * MB + cp];
-          v1 = red[row * MB + cp + 1];
-        }
-        float* dst = recv + (crank * rpo + lr) * MB + cp;
-        if (owner == static_cast<int>(crank)) {
-          *reinterpret_cast<float2*>(dst) = make_float2(v0, v1);
-        } else {
-          st_async_f32x2(mapa_shared(smem_u32(dst), owner), v0, v1, mapa_shared(smem_u32(recv_bar), owner));
-        }
-      }
+      // 4) Hand each owner its rows' partial sums: red[0] holds [BN][MB] with
+      //    the rows of one owner contiguous; one bulk copy per peer.
+      fence_proxy_async_smem();
       named_bar_sync(1, kSkConsumerWarps * 32);
+      if (warp == 0) {
+        cluster_wait();  // every peer's receive barrier is initialized
+        if (lane == 0) {
+          const uint32_t bytes = static_cast<uint32_t>(rpo * MB * 4);
+          for (int p = 0; p < split; ++p) {
+            if (p == static_cast<int>(crank)) continue;
+            const uint32_t dst = mapa_shared(smem_u32(recv + crank * rpo * MB), p);
+            bulk_s2s_cluster(dst, red + p * rpo * MB, bytes, mapa_shared(smem_u32(recv_bar), p));
+          }
+        }
+        __syncwarp();
+      }
       // 5) Owner: reduce the split partial sums of its rows in rank order.
       bool have = mbar_wait_bounded(recv_bar, 0, a.wait_ns);
       if (!have) {
         if (tid == 0) record_status(QTTS_ERR_TIMEOUT);
-        // Peers always send; keep this CTA alive until their stores land.
+        // Peers always send; keep this CTA alive until their copies land.
         have = mbar_wait_bounded(recv_bar, 0, 4 * a.wait_ns);
       }
       if (tid == 0) QTTS_TRACE_STAMP(7);
@@ -417,7 +393,9 @@ __global__ void __launch_bounds__(kSkThreads, 2)
           const int n = n0 + rbase + lr;
           if (n < a.N) {
             float r = 0.f;
-            for (int p = 0; p < split; ++p) r += recv[(p * rpo + lr) * MB + m];
+            for (int p = 0; p < split; ++p) {
+              r += (p == static_cast<int>(crank)) ? red[(rbase + lr) * MB + m] : recv[(p * rpo + lr) * MB + m];
+            }
             const int64_t ch = static_cast<int64_t>(group) * a.N + n;
             r *= load_as_float(a.scale, a.scale_dtype, ch);
             if (a.bias != nullptr) r += to_float(static_cast<const XT*>(a.bias)[ch]);
@@ -429,6 +407,15 @@ __global__ void __launch_bounds__(kSkThreads, 2)
   }
 
   if (tid == 0) QTTS_TRACE_STAMP(6);
+  if (split > 1) {
+    // Phase 0 of the cluster barrier (arrived at start) was waited on by warp
+    // 0 before it sent; everyone else completes it now. Phase 1: no CTA exits
+    // while a peer may still be reading the partial sums this CTA sent it
+    // (each CTA arrives only after its own receive barrier completed).
+    if (warp != 0) cluster_wait();
+    cluster_arrive_relaxed();
+    cluster_wait();
+  }
   // Error path: make sure no copy of ours is still landing in shared memory.
   if (warp == kSkConsumerWarps && lane == 0 && *reinterpret_cast<volatile int*>(err_flag) != 0) {
     for (int s = 0; s < a.stages && s < n_issued; ++s) {
@@ -582,6 +569,8 @@ int launch_skinny_w8a16(const SkinnyPlan& p, const CUtensorMap& map, const Skinn
 #ifdef QTTS_TRACE
 #include <atomic>
 namespace qtts {
+__device__ unsigned long long g_trace[kTraceSlots][kTraceEvents];
+__device__ unsigned long long g_trace_detail[8][64];
 static std::atomic<int> g_trace_slot{0};
 int qtts_trace_next_slot() { return g_trace_slot.fetch_add(1) % 16; }
 }  // namespace qtts
@@ -589,6 +578,9 @@ extern "C" __attribute__((visibility("default"))) int qtts_trace_read(void* dst,
   return cudaMemcpyFromSymbol(dst, qtts::g_trace, bytes) == cudaSuccess ? 0 : 9;
 }
 extern "C" __attribute__((visibility("default"))) void qtts_trace_reset(void) { qtts::g_trace_slot = 0; }
+extern "C" __attribute__((visibility("default"))) int qtts_trace_read_detail(void* dst, size_t bytes) {
+  return cudaMemcpyFromSymbol(dst, qtts::g_trace_detail, bytes) == cudaSuccess ? 0 : 9;
+}
 extern "C" __attribute__((visibility("default"))) int qtts_trace_clear(void) {
   void* p = nullptr;
   if (cudaGetSymbolAddress(&p, qtts::g_trace) != cudaSuccess) return 9;

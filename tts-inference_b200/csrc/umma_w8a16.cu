@@ -8,22 +8,32 @@
 // into tensor memory:
 //   * warp 8 (producer) streams the CTA's 128 weight rows x K slice HBM ->
 //     shared memory as 2-D TMA boxes of 128 rows x 128 bytes (128-byte
-//     swizzle), starting before the programmatic-dependent-launch wait;
+//     swizzle), starting before the programmatic-dependent-launch wait; after
+//     the wait it also brings each stage's activation tile [NB rows x 128 k]
+//     in with TMA, already in the K-major 128-byte-swizzled layout the MMA
+//     reads (B operand), straight from the caller's tensor;
 //   * warps 0-7 (dequant) each take one 32-lane quarter of the rows and one
 //     64-byte half of a stage: four 128-bit shared loads per thread (one row
-//     segment), int8 -> fp16 in registers (one byte-permute per two weights
-//     plus a subtract; exact), then tcgen05.st into a double-buffered A
-//     operand in tensor memory (128 lanes x 64 columns per 128-k stage);
-//   * warp 9 (MMA) issues tcgen05.mma kind::f16 with A from tensor memory, the
-//     activations as the B operand from shared memory (K-major, 128-byte
-//     swizzle, N = 16/32/64 batch columns) and the fp32 accumulator in tensor
-//     memory; tcgen05.commit releases each A buffer.
-// The dequant warps convert the first two stages before the dependency wait,
-// then stage the activations (fp16 with a per-row power-of-two scale, exact
-// within 2^28 of the row maximum), then finish the stream. The epilogue reads
-// the accumulator with tcgen05.ld. K can be split over a cluster of CTAs
-// whose partial sums reach the row owner through st.async, as in the skinny
-// kernel. All waits are bounded; tensor memory is always released.
+//     segment), int8 -> fp16 in registers (exact; one byte-permute per two
+//     weights plus a subtract), tcgen05.st into a ring of six A-operand slots
+//     in tensor memory (128 lanes x 32 columns = 64 k each). They convert
+//     three stages before waiting on the previous kernel. For bf16
+//     activations they then take one pass over the CTA's activation slice for
+//     the per-row maximum and rewrite each landed tile in place as fp16 with
+//     a per-row power-of-two scale (exact for every element within 2^28 of
+//     the row maximum; smaller ones round as fp16 subnormals, far below the
+//     bf16 output resolution). One fp16 MMA per 16 k is half the tensor-core
+//     instructions of any exact bf16 form of an int8 weight, and with small N
+//     the tensor core is bound by instruction count, not by FLOPs;
+//   * warp 9 (MMA) issues tcgen05.mma kind::f16, A from tensor memory, B from
+//     shared memory, fp32 accumulator [128 x NB] in tensor memory;
+//     tcgen05.commit releases A slots and activation tiles as they are used.
+// The epilogue reads the accumulator with tcgen05.ld. K can be split over a
+// cluster of CTAs whose partial sums reach the row owner through st.async, as
+// in the skinny kernel. All waits are bounded; tensor memory is always
+// released.
+#include <type_traits>
+
 #include "common.cuh"
 #include "kernels.h"
 
@@ -34,10 +44,7 @@ constexpr int kUmDqWarps = 8;
 constexpr int kUmProducerWarp = 8;
 constexpr int kUmMmaWarp = 9;
 constexpr int kUmThreads = (kUmDqWarps + 2) * 32;
-constexpr uint32_t kUmTmemCols = 256;  // A: 2 x 64 columns, D: up to 128 columns
-constexpr uint32_t kUmDCol = 128;
-
-__device__ __forceinline__ float um_pow2f(int e) { return __int_as_float((e + 127) << 23); }
+constexpr uint32_t kUmTmemCols = 256;  // A: 3 x 64 columns, D: up to 64 columns
 
 __device__ __forceinline__ void tmem_st_x32(uint32_t taddr, const uint32_t (&r)[32]) {
   asm volatile(
@@ -79,38 +86,51 @@ __device__ __forceinline__ void tmem_ld<32>(uint32_t taddr, uint32_t (&r)[32]) {
       : "r"(taddr));
 }
 
-// Byte offset of activation element (row n, k) in the B operand region:
-// k-blocks of 64 elements, each [NB rows x 128 bytes] in 8-row x 128-byte
-// atoms with the 16-byte chunks XOR-swizzled by (row % 8).
-template <int NB>
-__device__ __forceinline__ uint32_t xb_offset(int n, int k) {
-  const int kb = k >> 6;
-  const int c16 = (k & 63) >> 3;
-  return kb * (NB * 128) + (n >> 3) * 1024 + (n & 7) * 128 + ((c16 ^ (n & 7)) << 4);
+// A-operand conversion of one 32-bit word of int8 weights (4 consecutive k),
+// for bf16 activations: bf16 has too few mantissa bits for a byte, so each
+// weight is split exactly into two bf16 terms
+//   w = (128 + (b & 127)) + (-128 * (1 + [b < 0]))
+// that feed two MMAs into the same accumulator: one byte-permute and two
+// logic ops per pair of weights. (fp16 activations take one exact fp16 per
+// weight, i8x4_to_f16x2x2, and one MMA.)
+__device__ __forceinline__ void i8x4_to_bf16_split(uint32_t w, uint32_t& a1_lo, uint32_t& a1_hi, uint32_t& a2_lo,
+                                                   uint32_t& a2_hi) {
+  const uint32_t t01 = __byte_perm(w, 0x43434343u, 0x4140);  // halves 0x43b0, 0x43b1
+  const uint32_t t23 = __byte_perm(w, 0x43434343u, 0x4342);  // halves 0x43b2, 0x43b3
+  a1_lo = t01 & 0x437F437Fu;                  // 128 + (b & 127)
+  a1_hi = t23 & 0x437F437Fu;
+  a2_lo = (t01 & 0x00800080u) | 0xC300C300u;  // -128 or -256
+  a2_hi = (t23 & 0x00800080u) | 0xC300C300u;
 }
 
 template <int NB, typename XT>
 __global__ void __launch_bounds__(kUmThreads, 1)
-    umma_w8a16_kernel(const __grid_constant__ CUtensorMap wmap, const SkinnyArgs a) {
-  constexpr int HALF = NB / 2;  // accumulator columns per dequant warpgroup
-  constexpr uint32_t kIdesc = umma_idesc(0u /*F16*/, 0u /*F16*/, 128, NB);
+    umma_w8a16_kernel(const __grid_constant__ CUtensorMap wmap, const __grid_constant__ CUtensorMap xmap,
+                      const SkinnyArgs a) {
+  constexpr bool kSplitA = std::is_same<XT, __nv_bfloat16>::value;  // two bf16 MMAs per 16 k
+  constexpr int HALF = NB / 2;                  // accumulator columns per dequant warpgroup
+  constexpr int XS = NB * 256;                  // activation tile bytes per 128-k stage
+  constexpr int kSlotCols = kSplitA ? 64 : 32;  // tensor-memory columns per 64-k A slot
+  constexpr int kNA = 192 / kSlotCols;          // A slots (3 for bf16, 6 for fp16)
+  constexpr uint32_t kDCol = 192;
+  constexpr uint32_t kIdesc = umma_idesc(kSplitA ? 1u : 0u, kSplitA ? 1u : 0u, 128, NB);
   extern __shared__ uint8_t smem_raw[];
   uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
   const int split = gridDim.y;
-  const int kpad_max = a.k_per_cta;  // multiple of 128
+  const int WS = a.stages;   // weight ring depth
+  const int XD = a.x_pitch;  // activation ring depth (x_pitch carries it for this kernel)
   uint8_t* wbuf = smem;
-  uint8_t* xb = wbuf + a.stages * kUmStageBytes;  // B operand, NB x kpad_max fp16
-  uint32_t* rowmax = reinterpret_cast<uint32_t*>(xb + NB * kpad_max * 2);
-  float* xinv = reinterpret_cast<float*>(rowmax + NB);
-  float* recv = xinv + NB;  // [128][NB] when split > 1
+  uint8_t* xbuf = wbuf + WS * kUmStageBytes;                   // [XD][2 boxes][NB rows][128 B]
+  float* recv = reinterpret_cast<float*>(xbuf + XD * XS);      // [split][128/split][NB] when split > 1
   uint64_t* bars = reinterpret_cast<uint64_t*>(
       (reinterpret_cast<uintptr_t>(recv + (split > 1 ? 128 * NB : 0)) + 15) & ~uintptr_t(15));
   uint64_t* wfull = bars;
-  uint64_t* wempty = wfull + a.stages;
-  uint64_t* afull = wempty + a.stages;  // [2]
-  uint64_t* aempty = afull + 2;         // [2]
-  uint64_t* xready = aempty + 2;
-  uint64_t* dfull = xready + 1;
+  uint64_t* wempty = wfull + WS;
+  uint64_t* xfull = wempty + WS;
+  uint64_t* xempty = xfull + XD;
+  uint64_t* afull = xempty + XD;   // [kNA]
+  uint64_t* aempty = afull + kNA;  // [kNA]
+  uint64_t* dfull = aempty + kNA;
   uint64_t* recv_bar = dfull + 1;
   uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(recv_bar + 1);
   int* err_flag = reinterpret_cast<int*>(tmem_slot + 1);
@@ -130,19 +150,22 @@ __global__ void __launch_bounds__(kUmThreads, 1)
   int n_iters = (klen + 127) / 128;
 
   if (tid == 0) {
-    for (int s = 0; s < a.stages; ++s) {
+    QTTS_TRACE_STAMP(0);
+    for (int s = 0; s < WS; ++s) {
       mbar_init(&wfull[s], 1);
       mbar_init(&wempty[s], kUmDqWarps);
     }
-    for (int b = 0; b < 2; ++b) {
-      mbar_init(&afull[b], kUmDqWarps);
+    for (int s = 0; s < XD; ++s) {
+      mbar_init(&xfull[s], 1);
+      mbar_init(&xempty[s], 1);
+    }
+    for (int b = 0; b < kNA; ++b) {
+      mbar_init(&afull[b], kUmDqWarps / 2);
       mbar_init(&aempty[b], 1);
     }
-    mbar_init(xready, 1);
     mbar_init(dfull, 1);
     mbar_init(recv_bar, 1);
     if (split > 1) mbar_arrive_expect_tx(recv_bar, static_cast<uint32_t>((split - 1) * rpo * NB * 4));
-    for (int i = 0; i < NB; ++i) rowmax[i] = 0u;
     *err_flag = 0;
     fence_mbarrier_init();
   }
@@ -170,221 +193,204 @@ __global__ void __launch_bounds__(kUmThreads, 1)
     }
   }
   const int64_t wrow0 = static_cast<int64_t>(group) * a.N + n0;
-  const int64_t goff_x = a.group_index ? 0 : static_cast<int64_t>(group) * a.gsx;
+  const int xrow0 = static_cast<int>((a.group_index ? 0 : static_cast<int64_t>(group) * a.gsx_rows) + m0);
   const int64_t goff_o = a.group_index ? 0 : static_cast<int64_t>(group) * a.gso;
-  const XT* xg = static_cast<const XT*>(a.x) + goff_x + static_cast<int64_t>(m0) * a.ldx;
   XT* og = static_cast<XT*>(a.out) + goff_o + static_cast<int64_t>(m0) * a.ldo;
   const int mrows = min(NB, a.M - m0);
   volatile int* verr = err_flag;
 
-  int n_issued = 0;
+  int w_issued = 0, x_issued = 0;
   if (warp == kUmProducerWarp) {
-    // ---------------- producer: weight stream ----------------
+    // ---------------- producer ----------------
+    // Weights of the first WS stages before the dependency; then activation
+    // tile `it` and weight stage `it + WS`, in that order.
     if (lane == 0 && n_iters > 0) {
       tma_prefetch_desc(&wmap);
+      tma_prefetch_desc(&xmap);
+      const int pre = min(WS, n_iters);
+      for (int it = 0; it < pre; ++it) {
+        mbar_arrive_expect_tx(&wfull[it], kUmStageBytes);
+        tma_load_2d(wbuf + it * kUmStageBytes, &wmap, k0 + it * 128, static_cast<int>(wrow0), &wfull[it]);
+      }
+      w_issued = pre;
+      pdl_wait();
+      QTTS_TRACE_STAMP(1);
       for (int it = 0; it < n_iters; ++it) {
-        const int s = it % a.stages;
-        if (it >= a.stages && !mbar_wait_bounded(&wempty[s], ((it / a.stages) - 1) & 1, a.wait_ns)) {
+        const int xs = it % XD;
+        if (it >= XD && !mbar_wait_bounded(&xempty[xs], ((it / XD) - 1) & 1, a.wait_ns)) {
           record_status(QTTS_ERR_TIMEOUT);
           *verr = 1;
           break;
         }
-        mbar_arrive_expect_tx(&wfull[s], kUmStageBytes);
-        tma_load_2d(wbuf + s * kUmStageBytes, &wmap, k0 + it * 128, static_cast<int>(wrow0), &wfull[s]);
-        n_issued = it + 1;
+        mbar_arrive_expect_tx(&xfull[xs], XS);
+        uint8_t* xt = xbuf + xs * XS;
+        tma_load_2d(xt, &xmap, k0 + it * 128, xrow0, &xfull[xs]);
+        tma_load_2d(xt + NB * 128, &xmap, k0 + it * 128 + 64, xrow0, &xfull[xs]);
+        x_issued = it + 1;
+        const int wi = it + WS;
+        if (wi < n_iters) {
+          const int s = wi % WS;
+          if (!mbar_wait_bounded(&wempty[s], ((wi / WS) - 1) & 1, a.wait_ns)) {
+            record_status(QTTS_ERR_TIMEOUT);
+            *verr = 1;
+            break;
+          }
+          mbar_arrive_expect_tx(&wfull[s], kUmStageBytes);
+          tma_load_2d(wbuf + s * kUmStageBytes, &wmap, k0 + wi * 128, static_cast<int>(wrow0), &wfull[s]);
+          w_issued = wi + 1;
+        }
       }
     }
     __syncwarp();
   } else if (warp == kUmMmaWarp) {
     // ---------------- MMA issuer ----------------
     if (lane == 0) {
-      const uint32_t xaddr = smem_u32(xb);
+      const uint32_t xaddr = smem_u32(xbuf);
       bool ok = true;
-      if (n_iters > 0 && !mbar_wait_bounded(xready, 0, a.wait_ns)) ok = false;
       for (int it = 0; ok && it < n_iters; ++it) {
-        const int b = it & 1;
-        if (!mbar_wait_bounded(&afull[b], (it >> 1) & 1, a.wait_ns)) {
+        const int xs = it % XD;
+        if (!mbar_wait_bounded(&xfull[xs], (it / XD) & 1, a.wait_ns)) {
           ok = false;
           break;
         }
-        tc_fence_after();
+        if (it == 0) QTTS_TRACE_STAMP(2);
+        for (int h = 0; h < 2; ++h) {
+          const int hs = 2 * it + h;
+          const int slot = hs % kNA;
+          if (!mbar_wait_bounded(&afull[slot], (hs / kNA) & 1, a.wait_ns)) {
+            ok = false;
+            break;
+          }
+          QTTS_TRACE_DETAIL(0, hs);
+          tc_fence_after();
+          const uint32_t acol = tmem + kSlotCols * slot;
 #pragma unroll
-        for (int i = 0; i < 8; ++i) {
-          const int kb = it * 2 + (i >> 2);
-          const uint32_t baddr = xaddr + kb * (NB * 128) + (i & 3) * 32;
-          umma_f16_ts(tmem + kUmDCol, tmem + 64 * b + 8 * i, smem_desc_k_sw128(baddr), kIdesc,
-                      (it | i) != 0 ? 1u : 0u);
+          for (int i = 0; i < 4; ++i) {
+            const uint64_t bdesc = smem_desc_k_sw128(xaddr + xs * XS + h * (NB * 128) + i * 32);
+            umma_f16_ts(tmem + kDCol, acol + 8 * i, bdesc, kIdesc, (it | h | i) != 0 ? 1u : 0u);
+            if (kSplitA) umma_f16_ts(tmem + kDCol, acol + 32 + 8 * i, bdesc, kIdesc, 1u);
+          }
+          tc_commit(&aempty[slot]);
+          QTTS_TRACE_DETAIL(1, hs);
         }
-        tc_commit(&aempty[b]);
+        tc_commit(&xempty[xs]);
       }
       if (!ok) {
         record_status(QTTS_ERR_TIMEOUT);
         *verr = 1;
       }
+      QTTS_TRACE_STAMP(3);
       tc_commit(dfull);  // arrives once every MMA issued above has completed
     }
     __syncwarp();
   } else {
-    // ---------------- dequant warps: A operand, activations, epilogue ----------------
+    // ---------------- dequant warps: A operand into tensor memory, epilogue ----------------
+    // They never wait on the previous kernel before the epilogue: the A ring
+    // alone throttles them.
     const int quarter = warp & 3;
     const int half = warp >> 2;
     const int row = quarter * 32 + lane;  // weight row within the tile == TMEM lane
     const uint32_t wbase = smem_u32(wbuf);
     const uint32_t lane_base = static_cast<uint32_t>(quarter * 32) << 16;
     bool ok = true;
-
-    auto dequant_stage = [&](int it) {
-      const int s = it % a.stages;
-      const bool got = mbar_wait_bounded(&wfull[s], (it / a.stages) & 1, a.wait_ns);
+    for (int it = 0; ok && it < n_iters; ++it) {
+      const int s = it % WS;
+      const bool got = mbar_wait_bounded(&wfull[s], (it / WS) & 1, a.wait_ns);
       if (!__all_sync(0xffffffffu, got)) {
         ok = false;
-        return;
+        break;
       }
+      const int hs = 2 * it + half;
+      if (lane == 0 && quarter == 0) QTTS_TRACE_DETAIL(2, hs);
       const uint32_t rb = wbase + s * kUmStageBytes + row * 128;
       uint4 v[4];
 #pragma unroll
       for (int cc = 0; cc < 4; ++cc) v[cc] = lds128(rb + (((half * 4 + cc) ^ (row & 7)) << 4));
       __syncwarp();
       if (lane == 0) mbar_arrive(&wempty[s]);
-      uint32_t r[32];
+      uint32_t r1[32];
+      uint32_t r2[kSplitA ? 32 : 1];
 #pragma unroll
       for (int cc = 0; cc < 4; ++cc) {
-        i8x4_to_f16x2x2(v[cc].x, r[8 * cc + 0], r[8 * cc + 1]);
-        i8x4_to_f16x2x2(v[cc].y, r[8 * cc + 2], r[8 * cc + 3]);
-        i8x4_to_f16x2x2(v[cc].z, r[8 * cc + 4], r[8 * cc + 5]);
-        i8x4_to_f16x2x2(v[cc].w, r[8 * cc + 6], r[8 * cc + 7]);
+        const uint32_t wd[4] = {v[cc].x, v[cc].y, v[cc].z, v[cc].w};
+#pragma unroll
+        for (int e = 0; e < 4; ++e) {
+          const int c = 8 * cc + 2 * e;
+          if constexpr (kSplitA) {
+            i8x4_to_bf16_split(wd[e], r1[c], r1[c + 1], r2[c], r2[c + 1]);
+          } else {
+            i8x4_to_f16x2x2(wd[e], r1[c], r1[c + 1]);
+          }
+        }
       }
-      const int b = it & 1;
-      if (it >= 2) {
-        const bool freed = mbar_wait_bounded(&aempty[b], ((it >> 1) - 1) & 1, a.wait_ns);
+      const int slot = hs % kNA;
+      if (hs >= kNA) {
+        const bool freed = mbar_wait_bounded(&aempty[slot], ((hs / kNA) - 1) & 1, a.wait_ns);
         if (!__all_sync(0xffffffffu, freed)) {
           ok = false;
-          return;
+          break;
         }
         tc_fence_after();
       }
-      tmem_st_x32(tmem + lane_base + 64 * b + 32 * half, r);
+      if (lane == 0 && quarter == 0) QTTS_TRACE_DETAIL(3, hs);
+      tmem_st_x32(tmem + lane_base + kSlotCols * slot, r1);
+      if constexpr (kSplitA) tmem_st_x32(tmem + lane_base + kSlotCols * slot + 32, r2);
       tc_wait_st();
+      if (lane == 0 && quarter == 0) QTTS_TRACE_DETAIL(4, hs);
       tc_fence_before();
       __syncwarp();
-      if (lane == 0) mbar_arrive(&afull[b]);
-    };
-
-    // (1) The first two stages do not depend on the previous kernel.
-    int it = 0;
-    for (; ok && it < min(2, n_iters); ++it) dequant_stage(it);
-
-    // (2) Activations: wait for the producer of x, stage it as the B operand.
-    pdl_wait();
-    {
-      const int kpad = n_iters * 128;
-      const int cpr = kpad / 8;  // 16-byte chunks per row
-      const int total = NB * cpr;
-      const int dq = tid;  // 0..255
-      constexpr int kHeld = 4;
-      uint4 held[kHeld];
-      const bool in_regs = total <= kHeld * 256;
-      // pass 1: load (or zero), row max
-      for (int j = 0; j < (in_regs ? kHeld : (total + 255) / 256); ++j) {
-        const int ci = dq + 256 * j;
-        if (ci >= total) break;
-        const int n = ci / cpr;
-        const int k = (ci - n * cpr) * 8;
-        uint4 u = make_uint4(0u, 0u, 0u, 0u);
-        if (valid && n < mrows && k < klen) {
-          u = __ldcg(reinterpret_cast<const uint4*>(xg + static_cast<int64_t>(n) * a.ldx + k0 + k));
-        }
-        const XT* e = reinterpret_cast<const XT*>(&u);
-        float mx = 0.f;
-#pragma unroll
-        for (int q = 0; q < 8; ++q) mx = fmaxf(mx, fabsf(to_float(e[q])));
-        if (mx > 0.f) atomicMax(&rowmax[n], __float_as_uint(mx));
-        if (in_regs) {
-          held[j < kHeld ? j : 0] = u;
-        } else {
-          *reinterpret_cast<uint4*>(xb + xb_offset<NB>(n, k)) = u;  // raw, converted in pass 2
-        }
-      }
-      named_bar_sync(1, kUmDqWarps * 32);
-      // pass 2: scale to fp16 in place
-      for (int j = 0; j < (in_regs ? kHeld : (total + 255) / 256); ++j) {
-        const int ci = dq + 256 * j;
-        if (ci >= total) break;
-        const int n = ci / cpr;
-        const int k = (ci - n * cpr) * 8;
-        const uint32_t off = xb_offset<NB>(n, k);
-        const uint4 u = in_regs ? held[j < kHeld ? j : 0] : *reinterpret_cast<const uint4*>(xb + off);
-        const float mxr = __uint_as_float(rowmax[n]);
-        int sexp = 0;
-        if (mxr > 0.f) sexp = min(max(14 - (static_cast<int>((__float_as_uint(mxr) >> 23) & 0xFF) - 127), -100), 100);
-        const float sc = um_pow2f(sexp);
-        const XT* e = reinterpret_cast<const XT*>(&u);
-        uint4 o;
-        __half2* h = reinterpret_cast<__half2*>(&o);
-#pragma unroll
-        for (int q = 0; q < 4; ++q) h[q] = __floats2half2_rn(to_float(e[2 * q]) * sc, to_float(e[2 * q + 1]) * sc);
-        *reinterpret_cast<uint4*>(xb + off) = o;
-      }
-      if (dq < NB) {
-        const float mxr = __uint_as_float(rowmax[dq]);
-        int sexp = 0;
-        if (mxr > 0.f) sexp = min(max(14 - (static_cast<int>((__float_as_uint(mxr) >> 23) & 0xFF) - 127), -100), 100);
-        xinv[dq] = um_pow2f(-sexp);
-      }
-      fence_proxy_async_smem();
-      named_bar_sync(1, kUmDqWarps * 32);
-      if (dq == 0) mbar_arrive(xready);
+      if (lane == 0) mbar_arrive(&afull[slot]);
     }
-
-    // (3) The rest of the weight stream.
-    for (; ok && it < n_iters; ++it) dequant_stage(it);
     if (!ok) {
       if (lane == 0) record_status(QTTS_ERR_TIMEOUT);
       *verr = 1;
     }
 
-    // (4) Epilogue: accumulator -> registers.
+    // Epilogue: accumulator -> registers -> output (or the row owners).
+    pdl_wait();
+    if (tid == 0) QTTS_TRACE_STAMP(5);
     const bool dready = mbar_wait_bounded(dfull, 0, a.wait_ns);
     if (!dready) {
       if (lane == 0) record_status(QTTS_ERR_TIMEOUT);
       *verr = 1;
     }
+    if (tid == 0) QTTS_TRACE_STAMP(6);
     tc_fence_after();
     uint32_t d[HALF];
-    tmem_ld<HALF>(tmem + lane_base + kUmDCol + HALF * half, d);
+    tmem_ld<HALF>(tmem + lane_base + kDCol + HALF * half, d);
     tc_wait_ld();
     const bool cta_err = *verr != 0;
     float v[HALF];
 #pragma unroll
-    for (int c = 0; c < HALF; ++c) {
-      const int col = HALF * half + c;
-      v[c] = (n_iters > 0 && !cta_err) ? __uint_as_float(d[c]) * xinv[col] : 0.f;
-    }
+    for (int c = 0; c < HALF; ++c) v[c] = (n_iters > 0 && !cta_err) ? __uint_as_float(d[c]) : 0.f;
     if (split == 1) {
       const int n = n0 + row;
       if (valid && !cta_err && n < a.N) {
         const int64_t ch = static_cast<int64_t>(group) * a.N + n;
-        const float s = load_as_float(a.scale, a.scale_dtype, ch);
+        const float sc = load_as_float(a.scale, a.scale_dtype, ch);
         const float bias = a.bias != nullptr ? to_float(static_cast<const XT*>(a.bias)[ch]) : 0.f;
 #pragma unroll
         for (int c = 0; c < HALF; ++c) {
           const int col = HALF * half + c;
-          if (col < mrows) og[static_cast<int64_t>(col) * a.ldo + n] = from_float<XT>(v[c] * s + bias);
+          if (col < mrows) og[static_cast<int64_t>(col) * a.ldo + n] = from_float<XT>(v[c] * sc + bias);
         }
       }
     } else {
-      cluster_wait();
+      // Partial sums travel to the row owner from registers (st.async into
+      // its receive slot, counted on its mbarrier); a CTA's own rows go
+      // through its own slot.
+      cluster_wait();  // every peer's receive barrier is initialized
       const int owner = row / rpo;
       const int lr = row - owner * rpo;
       float* dst = recv + (crank * rpo + lr) * NB + HALF * half;
       if (owner == static_cast<int>(crank)) {
 #pragma unroll
-        for (int c = 0; c < HALF; c += 2) *reinterpret_cast<float2*>(dst + c) = make_float2(v[c], v[c + 1]);
+        for (int c = 0; c < HALF; c += 4) *reinterpret_cast<float4*>(dst + c) = make_float4(v[c], v[c + 1], v[c + 2], v[c + 3]);
       } else {
         const uint32_t rdst = mapa_shared(smem_u32(dst), owner);
         const uint32_t rbar = mapa_shared(smem_u32(recv_bar), owner);
 #pragma unroll
-        for (int c = 0; c < HALF; c += 2) st_async_f32x2(rdst + c * 4, v[c], v[c + 1], rbar);
+        for (int c = 0; c < HALF; c += 4) st_async_f32x4(rdst + c * 4, v[c], v[c + 1], v[c + 2], v[c + 3], rbar);
       }
       named_bar_sync(1, kUmDqWarps * 32);
       bool have = mbar_wait_bounded(recv_bar, 0, a.wait_ns);
@@ -396,11 +402,11 @@ __global__ void __launch_bounds__(kUmThreads, 1)
         const int rbase = static_cast<int>(crank) * rpo;
         for (int i = tid; i < rpo * mrows; i += kUmDqWarps * 32) {
           const int m = i / rpo;
-          const int lr2 = i - m * rpo;
-          const int n = n0 + rbase + lr2;
+          const int lr = i - m * rpo;
+          const int n = n0 + rbase + lr;
           if (n < a.N) {
             float r = 0.f;
-            for (int p = 0; p < split; ++p) r += recv[(p * rpo + lr2) * NB + m];
+            for (int p = 0; p < split; ++p) r += recv[(p * rpo + lr) * NB + m];
             const int64_t ch = static_cast<int64_t>(group) * a.N + n;
             r *= load_as_float(a.scale, a.scale_dtype, ch);
             if (a.bias != nullptr) r += to_float(static_cast<const XT*>(a.bias)[ch]);
@@ -414,15 +420,25 @@ __global__ void __launch_bounds__(kUmThreads, 1)
   // Teardown: every tensor-memory access is complete before the columns are freed.
   tc_fence_before();
   __syncthreads();
+  if (tid == 0) QTTS_TRACE_STAMP(7);
   if (warp == kUmMmaWarp) {
     tc_fence_after();
     tmem_dealloc(tmem, kUmTmemCols);
   }
+  // The dequant warps waited on the cluster barrier before their remote
+  // stores; the producer and MMA warps complete it here. Stores that came from
+  // registers need no source kept alive, and each CTA waited for everything
+  // sent to it.
   if (split > 1 && (warp == kUmProducerWarp || warp == kUmMmaWarp)) cluster_wait();
   if (warp == kUmProducerWarp && lane == 0 && *verr != 0) {
-    for (int s = 0; s < a.stages && s < n_issued; ++s) {
-      const int last = ((n_issued - 1 - s) / a.stages) * a.stages + s;
-      mbar_wait_bounded(&wfull[s], (last / a.stages) & 1, a.wait_ns);
+    // Drain our own copies in flight (weights and activations).
+    for (int s = 0; s < WS && s < w_issued; ++s) {
+      const int last = ((w_issued - 1 - s) / WS) * WS + s;
+      mbar_wait_bounded(&wfull[s], (last / WS) & 1, a.wait_ns);
+    }
+    for (int s = 0; s < XD && s < x_issued; ++s) {
+      const int last = ((x_issued - 1 - s) / XD) * XD + s;
+      mbar_wait_bounded(&xfull[s], (last / XD) & 1, a.wait_ns);
     }
   }
 }
@@ -433,8 +449,8 @@ __global__ void __launch_bounds__(kUmThreads, 1)
 namespace {
 
 template <int NB, typename XT>
-int launch_umma_t(const CUtensorMap& map, const SkinnyArgs& args, const SkinnyPlan& p, bool pdl,
-                  cudaStream_t stream) {
+int launch_umma_t(const CUtensorMap& map, const CUtensorMap& xmap, const SkinnyArgs& args, const SkinnyPlan& p,
+                  bool pdl, cudaStream_t stream) {
   auto kern = umma_w8a16_kernel<NB, XT>;
   static int configured[64] = {0};
   int dev = 0;
@@ -466,25 +482,25 @@ int launch_umma_t(const CUtensorMap& map, const SkinnyArgs& args, const SkinnyPl
   }
   cfg.attrs = attrs;
   cfg.numAttrs = na;
-  return cudaLaunchKernelEx(&cfg, kern, map, args) == cudaSuccess ? QTTS_OK : QTTS_ERR_LAUNCH;
+  return cudaLaunchKernelEx(&cfg, kern, map, xmap, args) == cudaSuccess ? QTTS_OK : QTTS_ERR_LAUNCH;
 }
 
 template <typename XT>
-int launch_umma_nb(const CUtensorMap& map, const SkinnyArgs& args, const SkinnyPlan& p, bool pdl,
-                   cudaStream_t stream) {
+int launch_umma_nb(const CUtensorMap& map, const CUtensorMap& xmap, const SkinnyArgs& args, const SkinnyPlan& p,
+                   bool pdl, cudaStream_t stream) {
   switch (p.mt) {
     case 2:
-      return launch_umma_t<16, XT>(map, args, p, pdl, stream);
+      return launch_umma_t<16, XT>(map, xmap, args, p, pdl, stream);
     case 4:
-      return launch_umma_t<32, XT>(map, args, p, pdl, stream);
+      return launch_umma_t<32, XT>(map, xmap, args, p, pdl, stream);
     default:
-      return launch_umma_t<64, XT>(map, args, p, pdl, stream);
+      return launch_umma_t<64, XT>(map, xmap, args, p, pdl, stream);
   }
 }
 
-size_t umma_smem(int nb, int kpc, int stages, int split) {
-  return 1024 + static_cast<size_t>(stages) * kUmStageBytes + static_cast<size_t>(nb) * kpc * 2 + nb * 8 +
-         (split > 1 ? static_cast<size_t>(128) * nb * 4 : 0) + 16 + 16 * stages + 64 + 32;
+size_t umma_smem(int nb, int wstages, int xstages, int split) {
+  return 1024 + static_cast<size_t>(wstages) * kUmStageBytes + static_cast<size_t>(xstages) * nb * 256 + nb * 8 +
+         (split > 1 ? static_cast<size_t>(128) * nb * 4 : 0) + 16 + 16 * wstages + 24 * xstages + 14 * 8 + 32;
 }
 
 }  // namespace
@@ -500,35 +516,41 @@ SkinnyPlan plan_umma(int M, int N, int K, int G, int split_req) {
   auto kpc_for = [&](int s) { return ((K + s - 1) / s + 127) / 128 * 128; };
   int split = split_req;
   if (split == 0) {
-    split = 8;
-    for (int s = 1; s <= 8; s *= 2) {
-      if (static_cast<size_t>(nb) * kpc_for(s) * 2 <= 64 * 1024 && ctas_base * s >= 120) {
-        split = s;
-        break;
-      }
+    // A tcgen05.mma of 128 rows costs about the same for any N <= 256, so with
+    // decode-sized N the tensor core is bound by instruction count: spread
+    // the tiles over as many SMs as possible, one CTA per SM, but keep the
+    // K split within 4 CTAs (the exchange of larger clusters costs more than
+    // it buys).
+    split = 1;
+    for (int s_ = 1; s_ <= 4; s_ *= 2) {
+      if (ctas_base * s_ <= kNumSMs) split = s_;
     }
   }
   p.split = split;
   p.k_per_cta = kpc_for(split);
-  p.x_pitch = 0;
   const int n_iters = p.k_per_cta / 128;
-  const size_t fixed = umma_smem(nb, p.k_per_cta, 0, split);
+  // Activation ring: 4 tiles (never more than the slice); weight ring: fill
+  // a ~100 KiB budget so the next kernel's CTA fits beside this one.
+  int xstages = n_iters < 4 ? n_iters : 4;
+  xstages = xstages < 1 ? 1 : xstages;
+  const size_t fixed = umma_smem(nb, 0, xstages, split);
   const size_t budget = 100 * 1024;
   int stages = fixed < budget ? static_cast<int>((budget - fixed) / kUmStageBytes) : 0;
   stages = stages > 6 ? 6 : stages;
   stages = stages < n_iters ? stages : n_iters;
-  stages = stages < 2 ? 2 : stages;
+  stages = stages < 2 ? 2 : stages;  // the ring also holds the 128 x NB fp32 partial sums at the end
   p.stages = stages;
-  p.smem = umma_smem(nb, p.k_per_cta, stages, split);
+  p.x_pitch = xstages;  // the tcgen05 kernel carries its activation ring depth here
+  p.smem = umma_smem(nb, stages, xstages, split);
   p.grid = dim3(n_tiles, split, G * p.m_chunks);
   return p;
 }
 
-int launch_umma_w8a16(const SkinnyPlan& p, const CUtensorMap& map, const SkinnyArgs& args, int x_dtype, bool pdl,
-                      cudaStream_t stream) {
+int launch_umma_w8a16(const SkinnyPlan& p, const CUtensorMap& map, const CUtensorMap& xmap, const SkinnyArgs& args,
+                      int x_dtype, bool pdl, cudaStream_t stream) {
   if (p.smem > kMaxDynSmem) return QTTS_ERR_VARIANT;
-  if (x_dtype == QTTS_BF16) return launch_umma_nb<__nv_bfloat16>(map, args, p, pdl, stream);
-  if (x_dtype == QTTS_FP16) return launch_umma_nb<__half>(map, args, p, pdl, stream);
+  if (x_dtype == QTTS_BF16) return launch_umma_nb<__nv_bfloat16>(map, xmap, args, p, pdl, stream);
+  if (x_dtype == QTTS_FP16) return launch_umma_nb<__half>(map, xmap, args, p, pdl, stream);
   return QTTS_ERR_DTYPE;
 }
 
