@@ -52,6 +52,10 @@ CALLS_PER_GRAPH = 224  # multiple of every pool size below
 REPLAYS_PER_POINT = 9  # 9 x 224 = 2016 calls per point (--replays)
 POOL_MIN_BYTES = 256 << 20
 METRIC = "int8 W8A16 GEMM HBM GB/s (talker linear sweep, M=1..64)"
+# DRAM bytes per launch of the dominant kernel (skinny_w8a16_kernel, gate_up
+# M=1) from one `ncu --set full` capture (profiles/skinny_w8a16_gate_up_m1.md):
+# dram__bytes_read.sum + dram__bytes_write.sum, against its algorithmic bytes.
+NCU_TRAFFIC = {"case": "gate_up 12288x2048, M=1", "bytes_per_launch": 25235200, "algorithmic_bytes": 25243652}
 
 
 def algo_bytes(n: int, k: int, m: int) -> int:
@@ -465,7 +469,8 @@ def run_gpu_arm(args) -> None:
                 "unit": "GB/s",
                 "frac": round(value / world / pk["hbm_gbs"], 4),
                 "peak_source": pk["source"],
-                "traffic": None,
+                "traffic": NCU_TRAFFIC["bytes_per_launch"],
+                "traffic_case": NCU_TRAFFIC,
             },
             "cpu_baseline": cpu,
             "e2e": {
@@ -488,6 +493,30 @@ def run_gpu_arm(args) -> None:
         dist.destroy_process_group()
 
 
+def run_single(spec: str, calls: int = 3) -> None:
+    """One (shape, M) point, `calls` launches with an L2 flush before each:
+    a small case for `ncu` captures. spec = "<shape>:<M>[:<variant>]"."""
+    from qtts_b200.quant import kernels as qk
+
+    parts = spec.split(":")
+    label, m = parts[0], int(parts[1])
+    variant = int(parts[2], 0) if len(parts) > 2 else 0
+    n, k = {lab: (n_, k_) for lab, n_, k_ in SHAPES}[label]
+    torch.cuda.set_device(0)
+    gen = torch.Generator(device="cuda")
+    gen.manual_seed(0)
+    w = torch.randn((n, k), generator=gen, device="cuda") * 0.02
+    q, s = qk.quantize_int8_rows(w)
+    s = s.to(torch.bfloat16)
+    x = torch.randn((m, k), generator=gen, device="cuda").to(torch.bfloat16)
+    flush = torch.empty(256 << 20, dtype=torch.uint8, device="cuda")
+    for _ in range(calls):
+        flush.zero_()
+        qk.w8_gemm(x, q, s, variant=variant)
+    torch.cuda.synchronize()
+    print(json.dumps({"single": spec, "ok": True}))
+
+
 def main(argv=None) -> int:
     ap = argparse.ArgumentParser(description=__doc__, formatter_class=argparse.RawDescriptionHelpFormatter)
     ap.add_argument("--gpus", type=int, default=1)
@@ -501,8 +530,13 @@ def main(argv=None) -> int:
     ap.add_argument("--cpu-seconds", type=float, default=15.0)
     ap.add_argument("--replays", type=int, default=REPLAYS_PER_POINT,
                     help="graph replays per point per step (224 calls each); 9 gives the reference's 2016 calls")
+    ap.add_argument("--single", default=None,
+                    help="profile case: run one point '<shape>:<M>[:<variant>]' 3 times and exit")
     args = ap.parse_args(argv)
     globals()["REPLAYS_PER_POINT"] = args.replays
+    if args.single:
+        run_single(args.single)
+        return 0
     if args.warmup < 3:
         print("warning: fewer than 3 warm-up steps", file=sys.stderr)
     if args.impl == "reference":
