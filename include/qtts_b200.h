@@ -150,9 +150,14 @@ QTTS_API int qtts_w8a16_grouped_gemm(const void* x, int64_t group_stride_x, int6
                             int variant, unsigned flags, void* stream);
 
 /* ---- load-time weight quantizers ------------------------------------------
+ * Division by a constant (`amax / 127`, `/ 448`) follows torch on a CUDA
+ * tensor, where `tensor / number` is evaluated as `tensor * fl32(1 / number)`:
+ * the quantizers reproduce the reference as it runs on the GPU (on the CPU,
+ * torch divides, and about half of the scales differ in the last bit).
+ *
  * Symmetric per-output-channel int8, bit-exact with
- * quantize_weight_per_channel (qtts/quant/int8.py:45-56):
- *   scale[n] = max(max_k |float(w[n,k])|, 1e-12f) / 127
+ * quantize_weight_per_channel (qtts/quant/int8.py:45-56) on a CUDA tensor:
+ *   scale[n] = max(max_k |float(w[n,k])|, 1e-12f) * fl32(1 / 127)
  *   q[n,k]   = clamp(round_half_even(float(w[n,k]) / scale[n]), -127, 127)
  * w: [N, K] of w_dtype (BF16, FP16, FP32); q: [N, K] int8 (ld = K);
  * scale: [N] fp32. */
@@ -160,8 +165,8 @@ QTTS_API int qtts_quantize_int8_rows(const void* w, int64_t ldw, int w_dtype,
                             int8_t* q, float* scale, int N, int K, void* stream);
 
 /* Symmetric per-output-channel e4m3, bit-exact with quantize_weight_fp8
- * (qtts/quant/fp8.py:45-49):
- *   scale[n] = max(max_k |float(w[n,k])|, 1e-12f) / 448
+ * (qtts/quant/fp8.py:45-49) on a CUDA tensor:
+ *   scale[n] = max(max_k |float(w[n,k])|, 1e-12f) * fl32(1 / 448)
  *   q[n,k]   = e4m3_rne(float(w[n,k]) / scale[n])
  * q: [N, K] e4m3 bytes (ld = K); scale: [N] fp32. */
 QTTS_API int qtts_quantize_fp8_rows(const void* w, int64_t ldw, int w_dtype,
@@ -169,9 +174,9 @@ QTTS_API int qtts_quantize_fp8_rows(const void* w, int64_t ldw, int w_dtype,
 
 /* ---- fp8 e4m3 W8A8 ---------------------------------------------------------
  * Per-token dynamic activation quantization, bit-exact with
- * Fp8Method.apply (qtts/quant/fp8.py:77-78):
+ * Fp8Method.apply (qtts/quant/fp8.py:77-78) on a CUDA tensor:
  *   amax_m     = max_k |x[m,k]|                (in x_dtype, exact)
- *   scale_x[m] = float(max(amax_m, x_dtype(1e-6))) / 448
+ *   scale_x[m] = float(max(amax_m, x_dtype(1e-6))) * fl32(1 / 448)
  *   q[m,k]     = e4m3_rne(float(x[m,k]) / scale_x[m])
  * x: [M, K] (BF16/FP16/FP32, ld ldx); q: [M, K] e4m3 (ld = K); scale_x: [M]. */
 QTTS_API int qtts_fp8_quant_rows(const void* x, int64_t ldx, int x_dtype,

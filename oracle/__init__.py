@@ -8,11 +8,15 @@ it. Nothing under ``tts-inference_b200/`` imports it.
 
 Parity pin: the restatement is checked against golden vectors produced by
 running the reference's own Python code (``tests/golden/make_golden.py``
-imports ``qtts`` from the reference checkout and records its outputs).
+imports ``qtts`` from the reference checkout and records its outputs) on the
+CPU; the quantizers also model torch's CUDA evaluation of ``tensor / number``
+(``device="cuda"``, the default), pinned by the GPU tests against torch's own
+GPU ops.
 """
 
 from .qtts_ref import (  # noqa: F401
     bf16_round,
+    div_by_number,
     e4m3_decode,
     e4m3_encode,
     fp16_round,

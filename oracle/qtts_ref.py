@@ -88,9 +88,31 @@ def e4m3_encode(v) -> np.ndarray:
 
 # ----------------------------------------------------------------------------
 # Weight quantizers
+#
+# The reference divides a tensor by a Python number in three places (``amax /
+# 127``, ``amax / 448``, ``scale / 448``). torch evaluates that differently by
+# device: on the CPU it is an IEEE fp32 division; on a CUDA tensor the
+# divisor is a CPU scalar, and torch multiplies by its reciprocal instead,
+# ``a * fl32(1 / c)`` in the op's math type (fp32 for fp32/bf16/fp16 inputs),
+# which differs from the division in the last bit for some inputs. The
+# reference quantizes where its weights live -- on the GPU in a served
+# engine -- so ``device="cuda"`` (the default) is the deployed behaviour and
+# the one the library follows; ``device="cpu"`` is what the golden vectors
+# record, as they were made by running the reference on the CPU. Tensor by
+# tensor divisions (``w / scale[:, None]``) are IEEE on both devices.
 
 
-def quantize_weight_per_channel(weight) -> tuple[np.ndarray, np.ndarray]:
+def div_by_number(a, c: float, device: str) -> np.ndarray:
+    """``tensor / python_number`` as torch computes it on ``device`` (fp32 math)."""
+    a = np.asarray(a, dtype=np.float32)
+    if device == "cpu":
+        return (a / _F32(c)).astype(np.float32)
+    if device == "cuda":
+        return (a * (_F32(1.0) / _F32(c))).astype(np.float32)
+    raise ValueError(f"device must be 'cpu' or 'cuda', got {device!r}")
+
+
+def quantize_weight_per_channel(weight, device: str = "cuda") -> tuple[np.ndarray, np.ndarray]:
     """qtts/quant/int8.py:45-56 -- symmetric per-output-channel int8.
 
     fp32 throughout: scale = max(rowabsmax, 1e-12) / 127, q = clamp(round(w /
@@ -98,31 +120,31 @@ def quantize_weight_per_channel(weight) -> tuple[np.ndarray, np.ndarray]:
     """
     w = np.asarray(weight, dtype=np.float32)
     amax = np.abs(w).max(axis=1)
-    scale = (np.maximum(amax, _F32(1e-12)) / _F32(127.0)).astype(np.float32)
+    scale = div_by_number(np.maximum(amax, _F32(1e-12)), 127.0, device)
     q = np.clip(np.rint(w / scale[:, None]), -127, 127).astype(np.int8)
     return q, scale
 
 
-def tune_quantize(weight_bf16) -> tuple[np.ndarray, np.ndarray]:
+def tune_quantize(weight_bf16, device: str = "cuda") -> tuple[np.ndarray, np.ndarray]:
     """examples/kernels/tune_w8_gemm.py:82-85 -- the tuning script's quantizer.
 
     scale = bf16(amax / 127) (no 1e-12 floor), packed = round(w / float(scale)).
     """
     w = np.asarray(weight_bf16, dtype=np.float32)
-    scale = bf16_round(np.abs(w).max(axis=1) / _F32(127.0))
+    scale = bf16_round(div_by_number(np.abs(w).max(axis=1), 127.0, device))
     q = np.clip(np.rint(w / scale[:, None]), -127, 127).astype(np.int8)
     return q, scale
 
 
-def quantize_weight_fp8(weight) -> tuple[np.ndarray, np.ndarray]:
+def quantize_weight_fp8(weight, device: str = "cuda") -> tuple[np.ndarray, np.ndarray]:
     """qtts/quant/fp8.py:45-49 -- per-output-channel e4m3, scale = max(amax, 1e-12) / 448."""
     w = np.asarray(weight, dtype=np.float32)
     amax = np.abs(w).max(axis=1)
-    scale = (np.maximum(amax, _F32(1e-12)) / _F32(448.0)).astype(np.float32)
+    scale = div_by_number(np.maximum(amax, _F32(1e-12)), 448.0, device)
     return e4m3_encode(w / scale[:, None]), scale
 
 
-def quantize_act_fp8(x, dtype: str = "bf16") -> tuple[np.ndarray, np.ndarray]:
+def quantize_act_fp8(x, dtype: str = "bf16", device: str = "cuda") -> tuple[np.ndarray, np.ndarray]:
     """qtts/quant/fp8.py:77-78 -- per-token dynamic activation quantization.
 
     amax in the activation dtype (exact), clamp_min(1e-6) in that dtype (the
@@ -132,7 +154,7 @@ def quantize_act_fp8(x, dtype: str = "bf16") -> tuple[np.ndarray, np.ndarray]:
     xv = np.asarray(x, dtype=np.float32)
     amax = np.abs(xv).max(axis=1)
     floor = round_to(np.array([1e-6], dtype=np.float32), dtype)[0]
-    scale = (np.maximum(amax, floor) / _F32(448.0)).astype(np.float32)
+    scale = div_by_number(np.maximum(amax, floor), 448.0, device)
     return e4m3_encode(xv / scale[:, None]), scale
 
 

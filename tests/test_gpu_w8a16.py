@@ -314,8 +314,29 @@ def test_int8_weight_quantizer_bit_exact(golden, src):
     if src == "bf16":
         w = w.to(torch.bfloat16)
     q, s = qk.quantize_int8_rows(w.cuda())
-    np.testing.assert_array_equal(q.cpu().numpy(), golden[f"int8_q_{src}"])
-    np.testing.assert_array_equal(s.cpu().numpy().view(np.uint32), golden[f"int8_scale_{src}"].view(np.uint32))
+    qo, so = oracle.quantize_weight_per_channel(golden[f"w_{src}"], device="cuda")
+    np.testing.assert_array_equal(q.cpu().numpy(), qo)
+    np.testing.assert_array_equal(s.cpu().numpy().view(np.uint32), so.view(np.uint32))
+    # Where torch's CPU and CUDA forms give the same scale, the CPU-made golden codes hold too.
+    same = so == golden[f"int8_scale_{src}"]
+    np.testing.assert_array_equal(q.cpu().numpy()[same], golden[f"int8_q_{src}"][same])
+
+
+@pytest.mark.parametrize("dtype", [torch.float32, torch.bfloat16])
+def test_int8_quantizer_matches_reference_ops_on_gpu(dtype):
+    """The reference's own op sequence (qtts/quant/int8.py:53-56), run by torch on the GPU."""
+    g = torch.Generator().manual_seed(51)
+    w = (torch.randn(4096, 2048, generator=g) * 0.02).to(dtype).cuda()
+    wf = w.detach().float()
+    ref_s = wf.abs().amax(dim=1).clamp_min(1e-12) / 127.0
+    ref_q = (wf / ref_s[:, None]).round().clamp_(-127.0, 127.0).to(torch.int8)
+    q, s = qk.quantize_int8_rows(w)
+    assert torch.equal(s, ref_s)
+    assert torch.equal(q, ref_q)
+    # ...and it is the oracle's CUDA form, bit for bit.
+    qo, so = oracle.quantize_weight_per_channel(wf.cpu().numpy(), device="cuda")
+    np.testing.assert_array_equal(ref_s.cpu().numpy(), so)
+    np.testing.assert_array_equal(ref_q.cpu().numpy(), qo)
 
 
 def test_int8_weight_quantizer_full_size():

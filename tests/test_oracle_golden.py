@@ -1,7 +1,8 @@
 """Pin the CPU oracle to the reference: golden vectors made by the reference's own code.
 
 The vectors come from tests/golden/make_golden.py, which runs the reference's
-``qtts.quant`` functions and tuning script. Integer and e4m3 outputs and fp32
+``qtts.quant`` functions and tuning script on the CPU, so the quantizers are
+checked here in their ``device="cpu"`` form (IEEE ``tensor / number``). Integer and e4m3 outputs and fp32
 scales must match bit for bit; the eager bf16 GEMM within one bf16 rounding
 step (its fp32 summation order is the BLAS library's).
 """
@@ -16,20 +17,20 @@ import oracle
 
 @pytest.mark.parametrize("src", ["f32", "bf16"])
 def test_int8_quantizer_bit_exact(golden, src):
-    q, s = oracle.quantize_weight_per_channel(golden[f"w_{src}"])
+    q, s = oracle.quantize_weight_per_channel(golden[f"w_{src}"], device="cpu")
     np.testing.assert_array_equal(q, golden[f"int8_q_{src}"])
     np.testing.assert_array_equal(s.view(np.uint32), golden[f"int8_scale_{src}"].view(np.uint32))
 
 
 def test_int8_quantizer_zero_row_floor(golden):
-    q, s = oracle.quantize_weight_per_channel(golden["w_f32"])
+    q, s = oracle.quantize_weight_per_channel(golden["w_f32"], device="cpu")
     assert s[7] == np.float32(1e-12) / np.float32(127.0)
     assert not q[7].any()
 
 
 @pytest.mark.parametrize("src", ["f32", "bf16"])
 def test_fp8_weight_quantizer_bit_exact(golden, src):
-    q, s = oracle.quantize_weight_fp8(golden[f"w_{src}"])
+    q, s = oracle.quantize_weight_fp8(golden[f"w_{src}"], device="cpu")
     np.testing.assert_array_equal(q, golden[f"fp8_q_{src}"])
     np.testing.assert_array_equal(s.view(np.uint32), golden[f"fp8_scale_{src}"].view(np.uint32))
 
@@ -37,13 +38,13 @@ def test_fp8_weight_quantizer_bit_exact(golden, src):
 @pytest.mark.parametrize("dtype", ["bf16", "fp16", "f32"])
 def test_fp8_activation_quantizer_bit_exact(golden, dtype):
     x = golden[f"act_x_{dtype}"]
-    q, s = oracle.quantize_act_fp8(x, "fp32" if dtype == "f32" else dtype)
+    q, s = oracle.quantize_act_fp8(x, "fp32" if dtype == "f32" else dtype, device="cpu")
     np.testing.assert_array_equal(s.view(np.uint32), golden[f"act_scale_{dtype}"].view(np.uint32))
     np.testing.assert_array_equal(q, golden[f"act_q_{dtype}"])
 
 
 def test_tune_quantizer_bit_exact(golden):
-    q, s = oracle.tune_quantize(golden["tune_w"])
+    q, s = oracle.tune_quantize(golden["tune_w"], device="cpu")
     np.testing.assert_array_equal(q, golden["tune_q"])
     np.testing.assert_array_equal(s.view(np.uint32), golden["tune_scale"].view(np.uint32))
 
@@ -98,3 +99,29 @@ def test_bf16_round_matches_torch():
 def test_rel_err_metric():
     assert oracle.rel_err(np.array([1.0, 2.0]), np.array([1.0, 2.0])) == 0.0
     assert oracle.rel_err(np.array([1.0, 2.5]), np.array([1.0, 2.0])) == pytest.approx(0.25)
+
+
+def test_cuda_scalar_division_rule():
+    """``device="cuda"`` differs from the CPU form only through ``a * fl32(1/c)``."""
+    a = np.random.default_rng(7).random(100000, dtype=np.float32) * 4
+    cpu = oracle.div_by_number(a, 448.0, "cpu")
+    cuda = oracle.div_by_number(a, 448.0, "cuda")
+    np.testing.assert_array_equal(cpu, a / np.float32(448))
+    np.testing.assert_array_equal(cuda, a * (np.float32(1) / np.float32(448)))
+    differ = (cpu != cuda).mean()
+    assert 0 < differ < 1  # last-bit differences, on part of the inputs
+    assert np.abs(cpu.view(np.int32) - cuda.view(np.int32)).max() == 1
+    with pytest.raises(ValueError):
+        oracle.div_by_number(a, 2.0, "mps")
+
+
+@pytest.mark.parametrize("src", ["f32", "bf16"])
+def test_quantizers_cuda_form_consistent(golden, src):
+    """The CUDA-form quantizers agree with the CPU form wherever the scales agree."""
+    w = golden[f"w_{src}"]
+    for fn in (oracle.quantize_weight_per_channel, oracle.quantize_weight_fp8):
+        qc, sc = fn(w, device="cpu")
+        qg, sg = fn(w, device="cuda")
+        same = sc == sg
+        np.testing.assert_array_equal(qc[same], qg[same])
+        assert np.all(np.abs(sc.view(np.int32) - sg.view(np.int32)) <= 1)

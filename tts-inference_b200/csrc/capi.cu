@@ -251,7 +251,9 @@ __global__ void __launch_bounds__(256) quantize_rows_kernel(const void* w, int64
   float amax = 0.f;
   for (int k = threadIdx.x; k < K; k += 256) amax = fmaxf(amax, fabsf(ld_elem<T>(w, row + k)));
   amax = block_max_256(amax, sh);
-  const float s = fmaxf(amax, 1e-12f) / (mode == 0 ? 127.0f : 448.0f);
+  // ``amax / 127`` (``/ 448``) is a tensor divided by a Python number, which
+  // torch evaluates on a CUDA tensor as a product with the fp32 reciprocal.
+  const float s = fmaxf(amax, 1e-12f) * (mode == 0 ? 1.0f / 127.0f : 1.0f / 448.0f);
   if (threadIdx.x == 0) scale[n] = s;
   const int64_t qrow = static_cast<int64_t>(n) * K;
   for (int k = threadIdx.x; k < K; k += 256) {
@@ -281,7 +283,8 @@ __global__ void __launch_bounds__(256) fp8_quant_rows_kernel(const void* x, int6
   amax = block_max_256(amax, sh);
   // clamp_min(1e-6) in the activation dtype: the bound is 1e-6 rounded to T.
   const float floor_t = to_float(from_float<T>(1e-6f));
-  const float s = fmaxf(amax, floor_t) / 448.0f;
+  // ``.float() / 448`` on a CUDA tensor: a product with the fp32 reciprocal.
+  const float s = fmaxf(amax, floor_t) * (1.0f / 448.0f);
   if (threadIdx.x == 0) scale_x[m] = s;
   const int64_t qrow = static_cast<int64_t>(m) * K;
   for (int k = threadIdx.x; k < K; k += 256) {
@@ -602,6 +605,35 @@ int qtts_fp8_gemm(const uint8_t* xq, int64_t ldxq, const float* scale_x, const u
   if (dev_ok != QTTS_OK) return dev_ok;
   cudaStream_t s = static_cast<cudaStream_t>(stream);
   const bool pdl = (flags & QTTS_FLAG_PDL) != 0;
+  const bool tc_ok = K % 16 == 0 && aligned16(xq) && aligned16(wq) && ldxq % 16 == 0 && ldw % 16 == 0;
+  const int family = variant == QTTS_VARIANT_AUTO ? (tc_ok ? 0x200 : 0) : (variant & 0xF00);
+  if (family == 0x200) {
+    if (!tc_ok) return QTTS_ERR_ALIGN;
+    const int split = variant == QTTS_VARIANT_AUTO ? 0 : (variant & 0xF);
+    if (!(split == 0 || split == 1 || split == 2 || split == 4) || (variant & 0xF0F0) != 0) return QTTS_ERR_VARIANT;
+    const Fp8Plan plan = plan_fp8(M, N, K, split);
+    if (plan.grid.z > 65535u) return QTTS_ERR_SHAPE;
+    CUtensorMap wmap, xmap;
+    int r = make_tmap_u8_2d(&wmap, wq, static_cast<uint64_t>(N), static_cast<uint64_t>(K), static_cast<uint64_t>(ldw),
+                            128, 128);
+    if (r != QTTS_OK) return r;
+    r = make_tmap_u8_2d(&xmap, xq, static_cast<uint64_t>(M), static_cast<uint64_t>(K), static_cast<uint64_t>(ldxq),
+                        static_cast<uint32_t>(plan.nb), 128);
+    if (r != QTTS_OK) return r;
+    Fp8Args fa{};
+    fa.scale_x = scale_x;
+    fa.scale_w = scale_w;
+    fa.bias = bias;
+    fa.out = out;
+    fa.ldo = ldo;
+    fa.M = M;
+    fa.N = N;
+    fa.K = K;
+    fa.k_per_cta = plan.k_per_cta;
+    fa.stages = plan.stages;
+    fa.wait_ns = current_wait_limit_ns();
+    return launch_fp8_gemm(plan, wmap, xmap, fa, out_dtype, pdl, s);
+  }
   if (variant != QTTS_VARIANT_AUTO && variant != QTTS_VARIANT_GENERIC) return QTTS_ERR_VARIANT;
   GenericFp8Args ga{xq, ldxq, scale_x, wq, ldw, scale_w, bias, out, ldo, M, N, K};
   const dim3 grid((N + 7) / 8, (M + 7) / 8);

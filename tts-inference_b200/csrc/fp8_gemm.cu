@@ -1,0 +1,363 @@
+// fp8-e4m3 W8A8 GEMM on the 5th-generation tensor cores.
+//
+// Replaces torch._scaled_mm in Fp8Method.apply (qtts/quant/fp8.py:79-88):
+//   out[m, n] = cast( (sum_k xq[m,k] * wq[n,k]) * scale_x[m] * scale_w[n] + bias[n] )
+// with e4m3 operands, fp32 accumulation, and the row/column scales (and the
+// bias the reference adds afterwards) applied once in the epilogue.
+//
+// Both operands are e4m3 in memory, so nothing is converted on the way: the
+// producer warp streams 128 weight rows x 128 k (16 KiB) per stage and the
+// matching activation tile [NB rows x 128 k] with 2-D TMA (128-byte swizzle)
+// straight into the K-major shared-memory layout tcgen05 reads. The weight
+// stream starts before the programmatic-dependent-launch wait (weights are
+// constant); the activation tiles -- written by the quantization kernel that
+// precedes this one -- after it. One thread issues tcgen05.mma kind::f8f6f4
+// (M = 128 weight rows, N = NB batch columns, K = 32 per instruction; 4096
+// weights per instruction), accumulating fp32 in tensor memory, and releases
+// each stage with tcgen05.commit. Four epilogue warps read the accumulator with
+// tcgen05.ld (one row per thread). K can be split over a cluster of up to 4
+// CTAs whose partial sums reach the row owner by st.async. All waits are
+// bounded; tensor memory is always freed.
+#include "common.cuh"
+#include "kernels.h"
+
+namespace qtts {
+
+constexpr int kF8StageW = 16384;  // 128 rows x 128 k e4m3
+constexpr int kF8EpiWarps = 4;
+constexpr int kF8ProducerWarp = 4;
+constexpr int kF8MmaWarp = 5;
+constexpr int kF8Threads = 6 * 32;
+
+template <int N>
+__device__ __forceinline__ void f8_tmem_ld(uint32_t taddr, uint32_t (&r)[N]);
+template <>
+__device__ __forceinline__ void f8_tmem_ld<16>(uint32_t taddr, uint32_t (&r)[16]) {
+  asm volatile(
+      "tcgen05.ld.sync.aligned.32x32b.x16.b32 {%0, %1, %2, %3, %4, %5, %6, %7, %8, %9, %10, %11, %12, %13, %14, "
+      "%15}, [%16];"
+      : "=r"(r[0]), "=r"(r[1]), "=r"(r[2]), "=r"(r[3]), "=r"(r[4]), "=r"(r[5]), "=r"(r[6]), "=r"(r[7]),
+        "=r"(r[8]), "=r"(r[9]), "=r"(r[10]), "=r"(r[11]), "=r"(r[12]), "=r"(r[13]), "=r"(r[14]), "=r"(r[15])
+      : "r"(taddr));
+}
+
+template <int NB, typename OT>
+__global__ void __launch_bounds__(kF8Threads, 1)
+    fp8_gemm_kernel(const __grid_constant__ CUtensorMap wmap, const __grid_constant__ CUtensorMap xmap,
+                    const Fp8Args a) {
+  constexpr int XS = NB * 128;  // activation tile bytes per 128-k stage
+  constexpr uint32_t kCols = NB < 32 ? 32 : NB;  // TMEM allocation: power of two >= 32
+  constexpr uint32_t kIdesc = umma_idesc(0u /*E4M3*/, 0u /*E4M3*/, 128, NB);
+  extern __shared__ uint8_t smem_raw[];
+  uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
+  const int split = gridDim.y;
+  const int S = a.stages;
+  uint8_t* wbuf = smem;
+  uint8_t* xbuf = wbuf + S * kF8StageW;
+  float* recv = reinterpret_cast<float*>(xbuf + S * XS);  // [split][128/split][NB] when split > 1
+  uint64_t* bars = reinterpret_cast<uint64_t*>(
+      (reinterpret_cast<uintptr_t>(recv + (split > 1 ? 128 * NB : 0)) + 15) & ~uintptr_t(15));
+  uint64_t* wfull = bars;
+  uint64_t* xfull = wfull + S;
+  uint64_t* sempty = xfull + S;
+  uint64_t* dfull = sempty + S;
+  uint64_t* recv_bar = dfull + 1;
+  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(recv_bar + 1);
+  int* err_flag = reinterpret_cast<int*>(tmem_slot + 1);
+
+  const int tid = threadIdx.x;
+  const int warp = tid >> 5;
+  const int lane = tid & 31;
+  const int kidx = blockIdx.y;
+  const uint32_t crank = split > 1 ? cluster_ctarank() : 0u;
+  const int rpo = 128 / split;
+  const int n0 = blockIdx.x * 128;
+  const int m0 = blockIdx.z * NB;
+  const int k0 = kidx * a.k_per_cta;
+  const int klen = max(0, min(a.K - k0, a.k_per_cta));
+  const int n_iters = (klen + 127) / 128;
+  const int mrows = min(NB, a.M - m0);
+
+  if (tid == 0) {
+    for (int s = 0; s < S; ++s) {
+      mbar_init(&wfull[s], 1);
+      mbar_init(&xfull[s], 1);
+      mbar_init(&sempty[s], 1);
+    }
+    mbar_init(dfull, 1);
+    mbar_init(recv_bar, 1);
+    if (split > 1) mbar_arrive_expect_tx(recv_bar, static_cast<uint32_t>((split - 1) * rpo * NB * 4));
+    *err_flag = 0;
+    fence_mbarrier_init();
+  }
+  if (warp == kF8MmaWarp) {
+    tmem_alloc(tmem_slot, kCols);
+    tmem_relinquish();
+  }
+  tc_fence_before();
+  __syncthreads();
+  tc_fence_after();
+  const uint32_t tmem = *reinterpret_cast<volatile uint32_t*>(tmem_slot);
+  if (split > 1) cluster_arrive_relaxed();
+  pdl_launch_dependents();
+  volatile int* verr = err_flag;
+
+  int w_issued = 0, x_issued = 0;
+  if (warp == kF8ProducerWarp) {
+    if (lane == 0 && n_iters > 0) {
+      tma_prefetch_desc(&wmap);
+      tma_prefetch_desc(&xmap);
+      const int pre = min(S, n_iters);
+      for (int it = 0; it < pre; ++it) {
+        mbar_arrive_expect_tx(&wfull[it], kF8StageW);
+        tma_load_2d(wbuf + it * kF8StageW, &wmap, k0 + it * 128, n0, &wfull[it]);
+      }
+      w_issued = pre;
+      pdl_wait();
+      for (int it = 0; it < n_iters; ++it) {
+        const int s = it % S;
+        if (it >= S) {
+          if (!mbar_wait_bounded(&sempty[s], ((it / S) - 1) & 1, a.wait_ns)) {
+            record_status(QTTS_ERR_TIMEOUT);
+            *verr = 1;
+            break;
+          }
+          mbar_arrive_expect_tx(&wfull[s], kF8StageW);
+          tma_load_2d(wbuf + s * kF8StageW, &wmap, k0 + it * 128, n0, &wfull[s]);
+          w_issued = it + 1;
+        }
+        mbar_arrive_expect_tx(&xfull[s], XS);
+        tma_load_2d(xbuf + s * XS, &xmap, k0 + it * 128, m0, &xfull[s]);
+        x_issued = it + 1;
+      }
+    }
+    __syncwarp();
+  } else if (warp == kF8MmaWarp) {
+    if (lane == 0) {
+      const uint32_t waddr = smem_u32(wbuf);
+      const uint32_t xaddr = smem_u32(xbuf);
+      bool ok = true;
+      for (int it = 0; ok && it < n_iters; ++it) {
+        const int s = it % S;
+        const uint32_t ph = (it / S) & 1;
+        if (!mbar_wait_bounded(&wfull[s], ph, a.wait_ns) || !mbar_wait_bounded(&xfull[s], ph, a.wait_ns)) {
+          ok = false;
+          break;
+        }
+        tc_fence_after();
+#pragma unroll
+        for (int i = 0; i < 4; ++i) {
+          const uint64_t adesc = smem_desc_k_sw128(waddr + s * kF8StageW + i * 32);
+          const uint64_t bdesc = smem_desc_k_sw128(xaddr + s * XS + i * 32);
+          umma_f8_ss(tmem, adesc, bdesc, kIdesc, (it | i) != 0 ? 1u : 0u);
+        }
+        tc_commit(&sempty[s]);
+      }
+      if (!ok) {
+        record_status(QTTS_ERR_TIMEOUT);
+        *verr = 1;
+      }
+      tc_commit(dfull);
+    }
+    __syncwarp();
+  } else {
+    // ---------------- epilogue warps 0..3: one accumulator row per thread ----------------
+    pdl_wait();
+    const int row = warp * 32 + lane;
+    const uint32_t lane_base = static_cast<uint32_t>(warp * 32) << 16;
+    const bool dready = mbar_wait_bounded(dfull, 0, a.wait_ns);
+    if (!dready) {
+      if (lane == 0) record_status(QTTS_ERR_TIMEOUT);
+      *verr = 1;
+    }
+    tc_fence_after();
+    const bool cta_err = *verr != 0;
+    const int n = n0 + row;
+    float sw = 0.f, bias = 0.f;
+    if (split == 1 && n < a.N) {
+      sw = a.scale_w[n];
+      if (a.bias != nullptr) bias = to_float(static_cast<const OT*>(a.bias)[n]);
+    }
+    OT* og = static_cast<OT*>(a.out) + static_cast<int64_t>(m0) * a.ldo;
+#pragma unroll
+    for (int c0 = 0; c0 < NB; c0 += 16) {
+      uint32_t d[16];
+      f8_tmem_ld<16>(tmem + lane_base + c0, d);
+      tc_wait_ld();
+      float v[16];
+#pragma unroll
+      for (int c = 0; c < 16; ++c) v[c] = (n_iters > 0 && !cta_err) ? __uint_as_float(d[c]) : 0.f;
+      if (split == 1) {
+        if (!cta_err && n < a.N) {
+#pragma unroll
+          for (int c = 0; c < 16; ++c) {
+            const int col = c0 + c;
+            if (col < mrows) {
+              og[static_cast<int64_t>(col) * a.ldo + n] = from_float<OT>(v[c] * a.scale_x[m0 + col] * sw + bias);
+            }
+          }
+        }
+      } else {
+        if (c0 == 0) cluster_wait();
+        const int owner = row / rpo;
+        const int lr = row - owner * rpo;
+        float* dst = recv + (crank * rpo + lr) * NB + c0;
+        if (owner == static_cast<int>(crank)) {
+#pragma unroll
+          for (int c = 0; c < 16; c += 4) *reinterpret_cast<float4*>(dst + c) = make_float4(v[c], v[c + 1], v[c + 2], v[c + 3]);
+        } else {
+          const uint32_t rdst = mapa_shared(smem_u32(dst), owner);
+          const uint32_t rbar = mapa_shared(smem_u32(recv_bar), owner);
+#pragma unroll
+          for (int c = 0; c < 16; c += 4) st_async_f32x4(rdst + c * 4, v[c], v[c + 1], v[c + 2], v[c + 3], rbar);
+        }
+      }
+    }
+    if (split > 1) {
+      named_bar_sync(1, kF8EpiWarps * 32);
+      bool have = mbar_wait_bounded(recv_bar, 0, a.wait_ns);
+      if (!have) {
+        if (tid == 0) record_status(QTTS_ERR_TIMEOUT);
+        have = mbar_wait_bounded(recv_bar, 0, 4 * a.wait_ns);  // peers always send
+      }
+      if (have && !cta_err) {
+        const int rbase = static_cast<int>(crank) * rpo;
+        for (int i = tid; i < rpo * mrows; i += kF8EpiWarps * 32) {
+          const int m = i / rpo;
+          const int lr = i - m * rpo;
+          const int nn = n0 + rbase + lr;
+          if (nn < a.N) {
+            float r = 0.f;
+            for (int p = 0; p < split; ++p) r += recv[(p * rpo + lr) * NB + m];
+            r = r * a.scale_x[m0 + m] * a.scale_w[nn];
+            if (a.bias != nullptr) r += to_float(static_cast<const OT*>(a.bias)[nn]);
+            og[static_cast<int64_t>(m) * a.ldo + nn] = from_float<OT>(r);
+          }
+        }
+      }
+    }
+  }
+
+  tc_fence_before();
+  __syncthreads();
+  if (warp == kF8MmaWarp) {
+    tc_fence_after();
+    tmem_dealloc(tmem, kCols);
+  }
+  if (split > 1 && (warp == kF8ProducerWarp || warp == kF8MmaWarp)) cluster_wait();
+  if (warp == kF8ProducerWarp && lane == 0 && *verr != 0) {
+    for (int s = 0; s < S && s < w_issued; ++s) {
+      const int last = ((w_issued - 1 - s) / S) * S + s;
+      mbar_wait_bounded(&wfull[s], (last / S) & 1, a.wait_ns);
+    }
+    for (int s = 0; s < S && s < x_issued; ++s) {
+      const int last = ((x_issued - 1 - s) / S) * S + s;
+      mbar_wait_bounded(&xfull[s], (last / S) & 1, a.wait_ns);
+    }
+  }
+}
+
+namespace {
+
+template <int NB, typename OT>
+int launch_fp8_t(const CUtensorMap& wmap, const CUtensorMap& xmap, const Fp8Args& args, const Fp8Plan& p,
+                 bool pdl, cudaStream_t stream) {
+  auto kern = fp8_gemm_kernel<NB, OT>;
+  static int configured[64] = {0};
+  int dev = 0;
+  cudaGetDevice(&dev);
+  if (dev >= 0 && dev < 64 && !configured[dev]) {
+    if (cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, kMaxDynSmem) != cudaSuccess) {
+      return QTTS_ERR_CUDA;
+    }
+    configured[dev] = 1;
+  }
+  cudaLaunchConfig_t cfg = {};
+  cfg.gridDim = p.grid;
+  cfg.blockDim = dim3(kF8Threads, 1, 1);
+  cfg.dynamicSmemBytes = p.smem;
+  cfg.stream = stream;
+  cudaLaunchAttribute attrs[2];
+  int na = 0;
+  if (p.split > 1) {
+    attrs[na].id = cudaLaunchAttributeClusterDimension;
+    attrs[na].val.clusterDim.x = 1;
+    attrs[na].val.clusterDim.y = p.split;
+    attrs[na].val.clusterDim.z = 1;
+    ++na;
+  }
+  if (pdl) {
+    attrs[na].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+    attrs[na].val.programmaticStreamSerializationAllowed = 1;
+    ++na;
+  }
+  cfg.attrs = attrs;
+  cfg.numAttrs = na;
+  return cudaLaunchKernelEx(&cfg, kern, wmap, xmap, args) == cudaSuccess ? QTTS_OK : QTTS_ERR_LAUNCH;
+}
+
+template <typename OT>
+int launch_fp8_nb(const CUtensorMap& wmap, const CUtensorMap& xmap, const Fp8Args& args, const Fp8Plan& p, bool pdl,
+                  cudaStream_t stream) {
+  switch (p.nb) {
+    case 16:
+      return launch_fp8_t<16, OT>(wmap, xmap, args, p, pdl, stream);
+    case 32:
+      return launch_fp8_t<32, OT>(wmap, xmap, args, p, pdl, stream);
+    case 64:
+      return launch_fp8_t<64, OT>(wmap, xmap, args, p, pdl, stream);
+    default:
+      return launch_fp8_t<128, OT>(wmap, xmap, args, p, pdl, stream);
+  }
+}
+
+size_t fp8_smem(int nb, int stages, int split) {
+  return 1024 + static_cast<size_t>(stages) * (kF8StageW + static_cast<size_t>(nb) * 128) +
+         (split > 1 ? static_cast<size_t>(128) * nb * 4 : 0) + 16 + 24 * stages + 16 + 32;
+}
+
+}  // namespace
+
+Fp8Plan plan_fp8(int M, int N, int K, int split_req) {
+  Fp8Plan p{};
+  p.nb = M <= 16 ? 16 : (M <= 32 ? 32 : (M <= 64 ? 64 : 128));
+  const int m_chunks = (M + p.nb - 1) / p.nb;
+  const int n_tiles = (N + 127) / 128;
+  int split = split_req;
+  if (split == 0) {
+    // One CTA per SM at most (each MMA instruction is the unit of tensor
+    // work), K split within 4 CTAs.
+    split = 1;
+    for (int s = 1; s <= 4; s *= 2) {
+      if (n_tiles * m_chunks * s <= kNumSMs) split = s;
+    }
+  }
+  p.split = split;
+  p.k_per_cta = ((K + split - 1) / split + 127) / 128 * 128;
+  const int n_iters = p.k_per_cta / 128;
+  const size_t fixed = fp8_smem(p.nb, 0, split);
+  const size_t budget = 100 * 1024;
+  int stages = fixed < budget ? static_cast<int>((budget - fixed) / (kF8StageW + p.nb * 128)) : 0;
+  stages = stages > 6 ? 6 : stages;
+  stages = stages < n_iters ? stages : n_iters;
+  stages = stages < 2 ? 2 : stages;
+  p.stages = stages;
+  p.smem = fp8_smem(p.nb, stages, split);
+  p.grid = dim3(n_tiles, split, m_chunks);
+  return p;
+}
+
+int launch_fp8_gemm(const Fp8Plan& p, const CUtensorMap& wmap, const CUtensorMap& xmap, const Fp8Args& args,
+                    int out_dtype, bool pdl, cudaStream_t stream) {
+  if (p.smem > kMaxDynSmem) return QTTS_ERR_VARIANT;
+  switch (out_dtype) {
+    case QTTS_BF16:
+      return launch_fp8_nb<__nv_bfloat16>(wmap, xmap, args, p, pdl, stream);
+    case QTTS_FP16:
+      return launch_fp8_nb<__half>(wmap, xmap, args, p, pdl, stream);
+    default:
+      return launch_fp8_nb<float>(wmap, xmap, args, p, pdl, stream);
+  }
+}
+
+}  // namespace qtts

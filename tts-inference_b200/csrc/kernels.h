@@ -59,6 +59,32 @@ SkinnyPlan plan_umma(int M, int N, int K, int G, int split_req);
 int launch_umma_w8a16(const SkinnyPlan& p, const CUtensorMap& wmap, const CUtensorMap& xmap, const SkinnyArgs& args,
                       int x_dtype, bool pdl, cudaStream_t stream);
 
+// ---- fp8 e4m3 W8A8 (tcgen05) ------------------------------------------------------
+struct Fp8Args {
+  const float* scale_x;
+  const float* scale_w;
+  const void* bias;
+  void* out;
+  int64_t ldo;
+  int M, N, K;
+  int k_per_cta;
+  int stages;
+  uint64_t wait_ns;
+};
+
+struct Fp8Plan {
+  int nb;     // batch columns per CTA (MMA N): 16, 32, 64, 128
+  int split;  // CTAs per cluster along K
+  int k_per_cta;
+  int stages;
+  size_t smem;
+  dim3 grid;
+};
+
+Fp8Plan plan_fp8(int M, int N, int K, int split_req);
+int launch_fp8_gemm(const Fp8Plan& p, const CUtensorMap& wmap, const CUtensorMap& xmap, const Fp8Args& args,
+                    int out_dtype, bool pdl, cudaStream_t stream);
+
 // ---- tensor maps ---------------------------------------------------------------
 // 2-D uint8 tensor map over a row-major [rows, cols] byte matrix with row pitch
 // `pitch_bytes`, box [box_rows, box_cols] and 128-byte swizzle.
