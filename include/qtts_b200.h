@@ -195,6 +195,28 @@ QTTS_API int qtts_fp8_gemm(const uint8_t* xq, int64_t ldxq, const float* scale_x
                   const void* bias, void* out, int64_t ldo, int out_dtype,
                   int M, int N, int K, int variant, unsigned flags, void* stream);
 
+/* ---- fp8 linear without caller-provided scratch ----------------------------
+ * No counterpart in the reference. qtts_fp8_quant_rows followed by
+ * qtts_fp8_gemm (variant AUTO) -- the whole of Fp8Method.apply -- with the
+ * intermediate e4m3 codes and row scales kept in one fixed device array of the
+ * library instead of memory the caller allocates, for callers with no device
+ * allocator of their own. Nothing is allocated by the call.
+ *   out[m,n] = same value as the two-step sequence on the same inputs.
+ * x: [M, K] (BF16/FP16/FP32, ld ldx); wq: [N, K] e4m3 (ld ldw); scale_w: [N]
+ * fp32; bias [N] of out_dtype or NULL; out: [M, N] of out_dtype (ld ldo).
+ * Limits: M <= QTTS_NOALLOC_MAX_ROWS and M * K <= QTTS_NOALLOC_MAX_CODES, else
+ * QTTS_ERR_SHAPE and nothing is launched. The array is shared by every call on
+ * a device: calls that may run at the same time on one device (different
+ * streams) race on it; calls ordered on one stream are safe. Nothing in it
+ * needs to start at zero. The first call on each device looks its address up
+ * (with that device current), so make one call before recording a graph. */
+#define QTTS_NOALLOC_MAX_ROWS 1024
+#define QTTS_NOALLOC_MAX_CODES (1 << 20)
+QTTS_API int qtts_fp8_linear_noalloc(const void* x, int64_t ldx, int x_dtype,
+                            const uint8_t* wq, int64_t ldw, const float* scale_w,
+                            const void* bias, void* out, int64_t ldo, int out_dtype,
+                            int M, int N, int K, unsigned flags, void* stream);
+
 #ifdef __cplusplus
 }
 #endif

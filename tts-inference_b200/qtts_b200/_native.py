@@ -74,6 +74,11 @@ SIGNATURES: dict[str, tuple[object, list[object]]] = {
         [_c_vp, _c_i64, _c_vp, _c_vp, _c_i64, _c_vp, _c_vp, _c_vp, _c_i64, _c_int, _c_int, _c_int, _c_int,
          _c_int, _c_uint, _c_vp],
     ),
+    "qtts_fp8_linear_noalloc": (
+        _c_int,
+        [_c_vp, _c_i64, _c_int, _c_vp, _c_i64, _c_vp, _c_vp, _c_vp, _c_i64, _c_int, _c_int, _c_int, _c_int,
+         _c_uint, _c_vp],
+    ),
 }
 
 _lib: ctypes.CDLL | None = None
