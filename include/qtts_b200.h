@@ -89,6 +89,12 @@ enum qtts_dtype {
 /* tcgen05/TMEM tile kernel (weights dequantized to bf16 in shared memory,
  * accumulator in tensor memory), split-K over a cluster of `split` CTAs. */
 #define QTTS_VARIANT_UMMA(split) (0x200 | (split))
+/* Whole-K streaming kernel for M <= 16: each CTA owns 16*`rows` output rows
+ * (rows = 1, 2, 3, 4 or 6; 0 lets the library choose) over the whole of K, no
+ * cross-CTA reduction; weights dequantized with one byte-permute per two and
+ * the bias removed once per output. Refused (QTTS_ERR_VARIANT) when the
+ * activation rows do not fit in shared memory. */
+#define QTTS_VARIANT_STREAM(rows) (0x300 | ((rows) << 4))
 
 /* ---- library information ------------------------------------------------ */
 QTTS_API int qtts_abi_version(void);

@@ -92,6 +92,7 @@ VARIANTS = {
     **{f"skinny{s}": nat.variant_skinny(s) for s in (1, 2, 4, 8)},
     **{f"skinny{s}r{r}": nat.variant_skinny(s, r) for s, r in ((1, 1), (1, 2), (2, 4), (4, 2), (8, 1))},
     **{f"umma{s}": nat.variant_umma(s) for s in (1, 2, 4, 8)},
+    **{f"stream_r{r}": nat.variant_stream(r) for r in (0, 1, 2, 3, 4, 6)},
 }
 
 
@@ -106,8 +107,12 @@ def test_every_variant_agrees(variant, m):
         out = qk.w8_gemm(*to_dev(x, q, s), variant=v)
     except RuntimeError as exc:
         # A forced split whose activation slice cannot fit in shared memory is
-        # refused on the host (QTTS_ERR_VARIANT); the library's own choice never is.
+        # refused on the host (QTTS_ERR_VARIANT), as is the streaming kernel past
+        # 16 rows or with a 16-row x 6144 activation block; the library's own
+        # choice never is.
         assert "inapplicable kernel variant" in str(exc)
+        assert not (variant.startswith("stream") and m <= 8), "the streaming kernel must take M <= 8"
+        assert variant not in ("generic", "umma1"), f"{variant} must take every shape"
         return
     assert_close_to_oracle(out, ref, f"{variant} M={m}")
 
@@ -130,6 +135,40 @@ def test_umma_ragged_shapes(n, k, m):
     ref = oracle.w8a16_reference(x.float().numpy(), q, scale_values(s, torch.bfloat16))
     out = qk.w8_gemm(*to_dev(x, q, s), variant=nat.variant_umma(0))
     assert_close_to_oracle(out, ref, f"umma N={n} K={k} M={m}")
+
+
+@pytest.mark.parametrize("rows", [0, 1, 2, 3, 4, 6])
+@pytest.mark.parametrize(
+    "n,k,m",
+    [(80, 272, 3), (64, 128, 1), (65, 144, 7), (1000, 3072, 12), (7, 48, 2), (1, 16, 1), (4096, 2048, 16),
+     (2048, 6144, 9), (12288, 2048, 5), (1024, 3072, 16), (6144, 1024, 8)],
+)
+def test_stream_ragged_shapes(n, k, m, rows):
+    x, q, s = seeded_case(n, k, m, seed=14)
+    ref = oracle.w8a16_reference(x.float().numpy(), q, scale_values(s, torch.bfloat16))
+    out = qk.w8_gemm(*to_dev(x, q, s), variant=nat.variant_stream(rows))
+    assert_close_to_oracle(out, ref, f"stream rows={rows} N={n} K={k} M={m}")
+
+
+@pytest.mark.parametrize("variant", ["auto", "stream"])
+def test_activation_dynamic_range(variant):
+    # Rows spanning 1e-6..1e3 in magnitude, a zero row and a single-spike row:
+    # the per-row fp16 scaling and the bias correction must hold across them.
+    n, k, m = 2048, 2048, 12
+    g = torch.Generator().manual_seed(15)
+    w = torch.randn(n, k, generator=g) * 0.02
+    q, s = oracle.quantize_weight_per_channel(w.numpy())
+    x = torch.randn(m, k, generator=g) * torch.logspace(-6, 3, m)[:, None]
+    x[4] = 0
+    x[7] = 0
+    x[7, 100] = 300.0
+    x[9, ::3] *= 1e-4
+    x = x.to(torch.bfloat16)
+    ref = oracle.w8a16_reference(x.float().numpy(), q, scale_values(s, torch.bfloat16))
+    v = nat.VARIANT_AUTO if variant == "auto" else nat.variant_stream(0)
+    out = qk.w8_gemm(*to_dev(x, q, s), variant=v).float().cpu().numpy()
+    for r in range(m):  # each row against its own magnitude
+        assert_close_to_oracle(torch.from_numpy(out[r : r + 1]), ref[r : r + 1], f"row {r}")
 
 
 def test_forced_skinny_rejects_unaligned_k():

@@ -403,8 +403,9 @@ static int w8a16_dispatch(const void* x, int64_t gsx, int64_t ldx, int x_dtype, 
   int split = variant & 0xF;
   int rgroups = (variant >> 4) & 0xF;
   if (variant == QTTS_VARIANT_AUTO) {
-    // Up to 16 rows: the mma.sync streaming kernel. Wider batches: the
-    // tcgen05 kernel, whose per-instruction cost does not grow with M.
+    // Up to 16 rows: the split-K streaming kernel. Wider batches: the
+    // tcgen05 kernel, whose per-instruction cost does not grow with M. (The
+    // whole-K streaming kernel, 0x300, is a calibration candidate.)
     family = skinny_ok ? (M <= 16 ? 0x100 : 0x200) : 0;
     split = 0;
     rgroups = 0;
@@ -413,6 +414,46 @@ static int w8a16_dispatch(const void* x, int64_t gsx, int64_t ldx, int x_dtype, 
     if (variant != QTTS_VARIANT_AUTO && variant != QTTS_VARIANT_GENERIC) return QTTS_ERR_VARIANT;
     GenericArgs ga{x, ldx, gsx, w, ldw, scale, scale_dtype, bias, out, ldo, gso, M, N, K, G, group_index};
     return launch_generic_w8a16(ga, x_dtype, pdl, stream);
+  }
+  if (family == 0x300) {
+    if (!skinny_ok) return QTTS_ERR_ALIGN;
+    if (M > 16) return QTTS_ERR_VARIANT;
+    if (!(rgroups == 0 || stream_rows_ok(rgroups))) return QTTS_ERR_VARIANT;
+    if ((variant & 0xF00F) != 0) return QTTS_ERR_VARIANT;
+    const int zg = group_index != nullptr ? 1 : G;
+    const SkinnyPlan plan = plan_stream(M, N, K, zg, rgroups);
+    if (plan.grid.z > 65535u || plan.grid.x > 2147483647u) return QTTS_ERR_SHAPE;
+    if (plan.smem > kMaxDynSmem) return QTTS_ERR_VARIANT;
+    CUtensorMap map;
+    const uint64_t rows = static_cast<uint64_t>(G) * N;
+    const int r = make_tmap_u8_2d(&map, w, rows, static_cast<uint64_t>(K), static_cast<uint64_t>(ldw),
+                                  static_cast<uint32_t>(16 * plan.r), 128);
+    if (r != QTTS_OK) return r;
+    SkinnyArgs sa{};
+    sa.x = x;
+    sa.ldx = ldx;
+    sa.gsx = gsx;
+    sa.scale = scale;
+    sa.scale_dtype = scale_dtype;
+    sa.bias = bias;
+    sa.out = out;
+    sa.ldo = ldo;
+    sa.gso = gso;
+    sa.M = M;
+    sa.N = N;
+    sa.K = K;
+    sa.G = G;
+    sa.k_per_cta = plan.k_per_cta;
+    sa.stages = plan.stages;
+    sa.x_pitch = plan.x_pitch;
+    sa.m_chunks = plan.m_chunks;
+    sa.group_index = group_index;
+    sa.wait_ns = current_wait_limit_ns();
+    sa.trace_slot = -1;
+#ifdef QTTS_TRACE
+    sa.trace_slot = qtts_trace_next_slot();
+#endif
+    return launch_stream_w8a16(plan, map, sa, x_dtype, pdl, stream);
   }
   if (family == 0x100) {
     if (!skinny_ok) return QTTS_ERR_ALIGN;

@@ -326,10 +326,15 @@ Fp8Plan plan_fp8(int M, int N, int K, int split_req) {
   int split = split_req;
   if (split == 0) {
     // One CTA per SM at most (each MMA instruction is the unit of tensor
-    // work), K split within 4 CTAs.
+    // work), K split within 4 CTAs. The partial sums a split exchanges grow
+    // with the batch tile, so past 16 rows a CTA keeps >= 1536 of K
+    // (measured on B200: splitting K = 2048 at 32+ rows costs more than the
+    // extra CTAs gain; K = 6144 gains from a split of 4 at every M).
     split = 1;
     for (int s = 1; s <= 4; s *= 2) {
-      if (n_tiles * m_chunks * s <= kNumSMs) split = s;
+      if (n_tiles * m_chunks * s > kNumSMs) break;
+      if (p.nb > 16 && s > 1 && K / s < 1536) break;
+      split = s;
     }
   }
   p.split = split;

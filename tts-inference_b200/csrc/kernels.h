@@ -54,6 +54,12 @@ SkinnyPlan plan_skinny(int M, int N, int K, int G, int split_req, int r_req);
 int launch_skinny_w8a16(const SkinnyPlan& p, const CUtensorMap& map, const SkinnyArgs& args, int x_dtype,
                         bool pdl, cudaStream_t stream);
 
+// ---- weight-streaming W8A16 for M <= 16 (same argument block; plan.split = 1) ---
+bool stream_rows_ok(int r);
+SkinnyPlan plan_stream(int M, int N, int K, int G, int r_req);
+int launch_stream_w8a16(const SkinnyPlan& p, const CUtensorMap& map, const SkinnyArgs& args, int x_dtype, bool pdl,
+                        cudaStream_t stream);
+
 // ---- tcgen05 W8A16 (same argument block; plan.mt = NB/8, plan.r = 8) ----------
 SkinnyPlan plan_umma(int M, int N, int K, int G, int split_req);
 int launch_umma_w8a16(const SkinnyPlan& p, const CUtensorMap& wmap, const CUtensorMap& xmap, const SkinnyArgs& args,

@@ -167,6 +167,13 @@ __global__ void __launch_bounds__(kSkThreads, 2)
     // ---------------- consumers ----------------
     pdl_wait();
     if (tid == 0) QTTS_TRACE_STAMP(2);
+#ifdef QTTS_TRACE
+    if (tid == 0 && a.trace_slot == 5 && blockIdx.x == 0 && blockIdx.y == 0 && blockIdx.z == 0) {
+      g_trace_detail[3][0] = globaltimer_ns();
+      for (int s = 0; s < a.stages && s < n_iters && s < 63; ++s)
+        g_trace_detail[1][s] = mbar_try_wait(&full[s], 0) ? 1ull : 0ull;
+    }
+#endif
     const int kpad = n_iters * SW;
     // 1) Activation slice [MB, kpad]: each thread loads 16-byte chunks into
     //    registers (zeros past K and past the last batch row), the per-row
@@ -200,7 +207,9 @@ __global__ void __launch_bounds__(kSkThreads, 2)
           *reinterpret_cast<uint4*>(xs + m * a.x_pitch + kv) = u;  // raw; converted below
         }
       }
+      if (tid == 0) QTTS_TRACE_DETAIL(2, 0);
       named_bar_sync(1, kSkConsumerWarps * 32);
+      if (tid == 0) QTTS_TRACE_DETAIL(2, 1);
 #pragma unroll 4
       for (int j = 0; j < nj; ++j) {
         const int ci = tid + kSkConsumerWarps * 32 * j;
@@ -266,6 +275,7 @@ __global__ void __launch_bounds__(kSkThreads, 2)
         break;
       }
       if (it == 0 && tid == 0) QTTS_TRACE_STAMP(4);
+      if (tid == 0) QTTS_TRACE_DETAIL(0, it);
       const uint32_t sb = wbase + s * kSkStageBytes;
       const uint4 wa0 = lds128(sb + offA0);
       const uint4 wb0 = lds128(sb + offB0);
@@ -313,6 +323,8 @@ __global__ void __launch_bounds__(kSkThreads, 2)
       *reinterpret_cast<volatile int*>(err_flag) = 1;
     }
     if (tid == 0) QTTS_TRACE_STAMP(5);
+    if (tid == 32) QTTS_TRACE_DETAIL(4, 0);
+    if (tid == 224) QTTS_TRACE_DETAIL(4, 1);
     // Every warp is done with the stage ring before it becomes `red`.
     named_bar_sync(1, kSkConsumerWarps * 32);
     const bool cta_err = *reinterpret_cast<volatile int*>(err_flag) != 0;

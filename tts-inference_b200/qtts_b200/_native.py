@@ -46,6 +46,11 @@ def variant_umma(split: int) -> int:
     return 0x200 | split
 
 
+def variant_stream(rows: int = 0) -> int:
+    """Weight-streaming kernel (M <= 16): 16*`rows` output rows per CTA (0 = choose)."""
+    return 0x300 | (rows << 4)
+
+
 # Every symbol the header declares, with its ctypes signature.
 _c_i64 = ctypes.c_int64
 _c_int = ctypes.c_int

@@ -30,10 +30,23 @@ logger = get_logger("quant.int8")
 _INT8_MAX = 127.0
 #: torch._int_mm rejects fewer rows than this.
 _INT_MM_MIN_ROWS = 17
-#: Batch-row buckets the skinny kernel specializes on (8 rows per MMA tile).
-_ROW_BUCKETS = (8, 16, 32, 64)
-#: Split-K factors calibration chooses from.
+#: Batch-row buckets calibration times separately (the kernels' costs change
+#: with the rows of an 8-wide MMA tile that are real, and between tiles).
+_ROW_BUCKETS = (1, 2, 4, 8, 16, 32, 64)
+#: Split-K factors of the split-K streaming kernel calibration chooses from.
 _SPLITS = (1, 2, 4, 8)
+#: Split-K factors of the tcgen05 kernel (M > 16).
+_UMMA_SPLITS = (1, 2, 4)
+
+
+def variant_candidates(bucket: int) -> list[int]:
+    """Kernel variants worth timing for up to ``bucket`` activation rows."""
+    out = [nat.VARIANT_AUTO]
+    if bucket <= 16:
+        out += [nat.variant_skinny(s) for s in _SPLITS] + [nat.variant_stream(0)]
+    if bucket >= 16:
+        out += [nat.variant_umma(s) for s in _UMMA_SPLITS]
+    return out
 
 
 def quantize_weight_per_channel(weight: torch.Tensor) -> tuple[torch.Tensor, torch.Tensor]:
@@ -83,8 +96,7 @@ class Int8WeightOnlyMethod(QuantMethodBase):
                 continue
             x = torch.zeros(bucket, k, device=q.device, dtype=dtype)
             candidates = {
-                nat.variant_skinny(s): (lambda s=s: w8_gemm(x, q, scale, None, variant=nat.variant_skinny(s)))
-                for s in _SPLITS
+                v: (lambda v=v: w8_gemm(x, q, scale, None, variant=v)) for v in variant_candidates(bucket)
             }
             choose_variant(candidates, key=key)
 
