@@ -291,6 +291,186 @@ def capture(fn):
     return g
 
 
+FP8_ROWS = (16, 32, 64, 128)
+
+
+def fp8_algo_bytes(n: int, k: int, m: int) -> int:
+    """Config-3 bytes of one fp8 linear: e4m3 W + fp32 scale, bf16 x in, e4m3 x + fp32 scale
+    out and back in (the separate quantization step), bf16 out."""
+    return n * k + 4 * n + 2 * m * k + 2 * (m * k + 4 * m) + 2 * m * n
+
+
+def fp8_sweep(device, seed: int) -> dict:
+    """Config 3: the fp8 W8A8 path (per-token activation quantization + tcgen05 scaled GEMM,
+    as Fp8Method.apply runs it) on the four talker shapes at M in {16, 32, 64, 128}, beside
+    the reference's own op sequence on the same GPU (torch amax/clamp/div/cast +
+    torch._scaled_mm). Weight copies rotate through >= 256 MB per shape, as in config 2."""
+    from qtts_b200.quant import kernels as qk
+
+    gen = torch.Generator(device=device)
+    gen.manual_seed(seed + 7)
+    out: dict = {}
+    stream = torch.cuda.current_stream()
+
+    def timed(fn, reps=3):
+        g = capture(fn)
+        e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        g.replay()
+        e0.record(stream)
+        for _ in range(reps):
+            g.replay()
+        e1.record(stream)
+        torch.cuda.synchronize()
+        del g
+        return e0.elapsed_time(e1) * 1e3 / (reps * CALLS_PER_GRAPH)
+
+    tot_bytes = tot_us = tot_ref_us = 0.0
+    for label, n, k in SHAPES:
+        p = pool_size(n, k)
+        wq = torch.empty((p, n, k), dtype=torch.float8_e4m3fn, device=device)
+        ws = torch.empty((p, n), dtype=torch.float32, device=device)
+        for i in range(p):
+            w = torch.randn((n, k), generator=gen, device=device) * 0.02
+            q, s = qk.quantize_fp8_rows(w)
+            wq[i].copy_(q)
+            ws[i].copy_(s)
+            del w, q, s
+        wt = [wq[i].t() for i in range(p)]  # the reference's column-major fp8_weight views
+        for m in FP8_ROWS:
+            x = torch.randn((m, k), generator=gen, device=device).to(torch.bfloat16)
+
+            def ours(x=x):
+                for c in range(CALLS_PER_GRAPH):
+                    xq, sx = qk.fp8_quant_rows(x)
+                    qk.fp8_scaled_mm(xq, sx, wq[c % p], ws[c % p], None, torch.bfloat16)
+
+            def reference(x=x):
+                for c in range(CALLS_PER_GRAPH):
+                    sx = x.abs().amax(dim=1, keepdim=True).clamp_min(1e-6).float() / 448.0
+                    xq = (x.float() / sx).to(torch.float8_e4m3fn)
+                    torch._scaled_mm(xq, wt[c % p], scale_a=sx, scale_b=ws[c % p].reshape(1, -1),
+                                     bias=None, out_dtype=torch.bfloat16)
+
+            us = timed(ours)
+            try:
+                ref_us = timed(reference)
+            except Exception as exc:  # _scaled_mm unavailable for this layout/build
+                ref_us = None
+                print(f"torch._scaled_mm reference failed: {exc}", file=sys.stderr)
+            b = fp8_algo_bytes(n, k, m)
+            out.setdefault(label, {})[str(m)] = {
+                "us": round(us, 3),
+                "gbs": round(b / (us * 1e-6) / 1e9, 1),
+                "tflops": round(2 * m * n * k / (us * 1e-6) / 1e12, 1),
+                "torch_us": round(ref_us, 3) if ref_us else None,
+                "speedup_vs_torch": round(ref_us / us, 3) if ref_us else None,
+            }
+            tot_bytes += b
+            tot_us += us
+            tot_ref_us += ref_us or 0.0
+        del wq, ws, wt
+        torch.cuda.empty_cache()
+    return {
+        "workload": "config 3: fp8 e4m3 W8A8 (act quant + tcgen05 scaled GEMM, 2 launches per linear) on the "
+        "4 talker shapes at M in {16,32,64,128}; weights rotate through >= 256 MB per shape",
+        "gbs": round(tot_bytes / (tot_us * 1e-6) / 1e9, 1),
+        "torch_gbs": round(tot_bytes / (tot_ref_us * 1e-6) / 1e9, 1) if tot_ref_us else None,
+        "per_point": out,
+    }
+
+
+SHARD_POINTS = [(k, n, m) for k in (2048, 6144) for n in (12288, 49152) for m in (1, 8, 64)]
+SHARD_CALLS = 32
+
+
+def sharded_sweep(world: int, rank: int, device, seed: int) -> dict:
+    """Config 5: one int8 weight-only GEMM split along N over the ranks (each rank holds
+    ceil(N / world) rows of W and scale), outputs all-gathered over NCCL. The local GEMM is
+    timed in a CUDA graph, the all-gather of its [M, ceil(N/g)] block in an eager loop (no
+    collective is captured into a graph), each as the max over ranks of CUDA-event time;
+    GEMM + all-gather is their sum."""
+    from qtts_b200.sharded import ShardedW8Linear, shard_rows
+
+    gen = torch.Generator(device=device)
+    gen.manual_seed(seed + 11)
+    stream = torch.cuda.current_stream()
+    pk = peaks()
+    res: dict = {}
+
+    def time_graph(fn, reps=3):
+        g = capture(fn)
+        barrier(world)
+        e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        g.replay()
+        e0.record(stream)
+        for _ in range(reps):
+            g.replay()
+        e1.record(stream)
+        torch.cuda.synchronize()
+        ms = e0.elapsed_time(e1) / reps
+        del g
+        return max_over_ranks(world, ms) * 1e3 / SHARD_CALLS
+
+    def time_eager(fn, reps=3):
+        fn()
+        torch.cuda.synchronize()
+        barrier(world)
+        e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        e0.record(stream)
+        for _ in range(reps):
+            fn()
+        e1.record(stream)
+        torch.cuda.synchronize()
+        return max_over_ranks(world, e0.elapsed_time(e1) / reps) * 1e3 / SHARD_CALLS
+
+    for k, n, m in SHARD_POINTS:
+        start, stop = shard_rows(n, world, rank)
+        rows = stop - start
+        copies = max(1, min(8, -(-POOL_MIN_BYTES // max(1, rows * k))))
+        ws = [torch.randint(-127, 128, (rows, k), dtype=torch.int8, device=device, generator=gen)
+              for _ in range(copies)]
+        ss = [(torch.rand(rows, device=device, generator=gen) * 1e-3).to(torch.bfloat16) for _ in range(copies)]
+        lins = [ShardedW8Linear(ws[i], ss[i], n) for i in range(copies)]
+        x = torch.randn((m, k), generator=gen, device=device).to(torch.bfloat16)
+        block = torch.zeros((m, lins[0].shard), dtype=torch.bfloat16, device=device)
+        gathered = torch.empty((world, m, lins[0].shard), dtype=torch.bfloat16, device=device)
+
+        def gemm_only():
+            for c in range(SHARD_CALLS):
+                lins[c % copies].local(x, block)
+
+        def gather_only():
+            for _ in range(SHARD_CALLS):
+                lins[0].gather(block, gathered)
+
+        gemm_us = time_graph(gemm_only)
+        gather_us = time_eager(gather_only) if world > 1 else 0.0  # one GPU: the block is the output
+        total_us = gemm_us + gather_us
+        res[f"K{k}_N{n}_M{m}"] = {
+            "gemm_us": round(gemm_us, 3),
+            "allgather_us": round(gather_us, 3),
+            "gemm_allgather_us": round(total_us, 3),
+            "agg_weight_gbs": round(n * k / (total_us * 1e-6) / 1e9, 1),
+            "agg_weight_gbs_gemm_only": round(n * k / (gemm_us * 1e-6) / 1e9, 1),
+            "per_gpu_frac_of_hbm": round(rows * k / (gemm_us * 1e-6) / 1e9 / pk["hbm_gbs"], 4),
+        }
+        del ws, ss, lins, x, block, gathered
+        torch.cuda.empty_cache()
+    return {
+        "workload": "config 5: int8 W8A16 GEMM sharded along N over the ranks (ceil(N/g) rows each), bf16 "
+        "outputs all-gathered over NCCL; K in {2048,6144}, N in {12288,49152}, M in {1,8,64}",
+        "scaling": "strong",
+        "n_gpus": world,
+        "allgather_timed": "eager loop, CUDA events" if world > 1 else "single GPU: no exchange",
+        "per_point": res,
+    }
+
+
+def auto_kernel(m: int) -> str:
+    """The kernel the library's automatic choice launches for M activation rows (capi.cu)."""
+    return "skinny_w8a16_kernel" if m <= 16 else "umma_w8a16_kernel"
+
+
 def run_gpu_arm(args) -> None:
     from qtts_b200 import _native as nat
     from qtts_b200.quant import kernels as qk
@@ -369,6 +549,17 @@ def run_gpu_arm(args) -> None:
 
     value = bytes_per_step * args.steps * world / (elapsed_ms_max * 1e-3) / 1e9
     pk = peaks()
+    # Roofline of the dominant kernel: its algorithmic bytes per launch over
+    # its average launch duration, from the per-point events of the timed
+    # region (every call of a point launches the same kernel).
+    by_kernel: dict = {}
+    for pt, ms in zip(points, per_point_ms):
+        kname = auto_kernel(pt.m) if args.variant is None else f"variant {args.variant}"
+        kb, kt = by_kernel.get(kname, (0.0, 0.0))
+        by_kernel[kname] = (kb + pt.bytes * CALLS_PER_GRAPH * REPLAYS_PER_POINT, kt + ms)
+    dom_kernel = max(by_kernel, key=lambda kk: by_kernel[kk][1])
+    dom_bytes, dom_ms = by_kernel[dom_kernel]
+    dom_gbs = dom_bytes / (dom_ms * 1e-3) / 1e9
     calls_per_point = CALLS_PER_GRAPH * REPLAYS_PER_POINT
     per_point = {}
     for pt, ms in zip(points, per_point_ms):
@@ -408,6 +599,11 @@ def run_gpu_arm(args) -> None:
             del g
         del bf16_pools
         torch.cuda.empty_cache()
+
+    # ---- config 3 (fp8) and config 5 (N-sharded GEMM + all-gather), outside the timed region
+    fp8 = fp8_sweep(device, args.seed) if args.fp8 and rank == 0 else None
+    barrier(world)
+    sharded = sharded_sweep(world, rank, device, args.seed) if args.sharded else None
 
     # ---- end to end: host buffers in, results out, through the public API
     h2d = sum(pt.m * pt.k * 2 for pt in points)
@@ -463,14 +659,16 @@ def run_gpu_arm(args) -> None:
             },
             "roofline": {
                 "bound": "hbm",
-                "kernel": "skinny_w8a16_kernel",
-                "achieved": round(value / world, 1),
+                "kernel": dom_kernel,
+                "achieved": round(dom_gbs, 1),
                 "peak": pk["hbm_gbs"],
                 "unit": "GB/s",
-                "frac": round(value / world / pk["hbm_gbs"], 4),
+                "frac": round(dom_gbs / pk["hbm_gbs"], 4),
                 "peak_source": pk["source"],
+                "share_of_step": round(dom_ms / sum(per_point_ms), 3),
                 "traffic": NCU_TRAFFIC["bytes_per_launch"],
                 "traffic_case": NCU_TRAFFIC,
+                "by_kernel_gbs": {kk: round(b / (t * 1e-3) / 1e9, 1) for kk, (b, t) in by_kernel.items()},
             },
             "cpu_baseline": cpu,
             "e2e": {
@@ -483,6 +681,8 @@ def run_gpu_arm(args) -> None:
             "gpu_launches": launches_per_step * args.steps,
             "device_status": status,
             "per_point": per_point,
+            "fp8": fp8,
+            "sharded": sharded,
         }
         print(json.dumps(line), flush=True)
     if world > 1:
@@ -526,6 +726,9 @@ def main(argv=None) -> int:
     ap.add_argument("--seed", type=int, default=0)
     ap.add_argument("--variant", default=None, help="force a kernel variant (e.g. 0x104); default: library choice")
     ap.add_argument("--no-bf16-compare", dest="bf16_compare", action="store_false")
+    ap.add_argument("--no-fp8", dest="fp8", action="store_false", help="skip the config-3 fp8 sweep")
+    ap.add_argument("--no-sharded", dest="sharded", action="store_false",
+                    help="skip the config-5 N-sharded GEMM + all-gather sweep")
     ap.add_argument("--no-cpu-baseline", action="store_true")
     ap.add_argument("--cpu-seconds", type=float, default=15.0)
     ap.add_argument("--replays", type=int, default=REPLAYS_PER_POINT,
