@@ -14,17 +14,15 @@
 //     reads (B operand), straight from the caller's tensor;
 //   * warps 0-7 (dequant) each take one 32-lane quarter of the rows and one
 //     64-byte half of a stage: four 128-bit shared loads per thread (one row
-//     segment), int8 -> fp16 in registers (exact; one byte-permute per two
-//     weights plus a subtract), tcgen05.st into a ring of six A-operand slots
-//     in tensor memory (128 lanes x 32 columns = 64 k each). They convert
-//     three stages before waiting on the previous kernel. For bf16
-//     activations they then take one pass over the CTA's activation slice for
-//     the per-row maximum and rewrite each landed tile in place as fp16 with
-//     a per-row power-of-two scale (exact for every element within 2^28 of
-//     the row maximum; smaller ones round as fp16 subnormals, far below the
-//     bf16 output resolution). One fp16 MMA per 16 k is half the tensor-core
-//     instructions of any exact bf16 form of an int8 weight, and with small N
-//     the tensor core is bound by instruction count, not by FLOPs;
+//     segment), int8 -> the activations' 16-bit type in registers, exactly
+//     (every int8 value has at most 8 significant bits: fp16 through the
+//     0x64uu = 1024 + u pattern and one subtract per pair, bf16 through the
+//     fp32 2^23 + u pattern, one subtract per weight and a truncating repack),
+//     tcgen05.st into a ring of six A-operand slots in tensor memory (128
+//     lanes x 32 columns = 64 k each). They run ahead of the previous
+//     kernel's completion; only the epilogue waits for it. One MMA per 16 k
+//     for either type: at decode N the tensor core is bound by instruction
+//     count (~150 cycles per 128-row MMA whatever N is), not by FLOPs;
 //   * warp 9 (MMA) issues tcgen05.mma kind::f16, A from tensor memory, B from
 //     shared memory, fp32 accumulator [128 x NB] in tensor memory;
 //     tcgen05.commit releases A slots and activation tiles as they are used.
@@ -86,34 +84,19 @@ __device__ __forceinline__ void tmem_ld<32>(uint32_t taddr, uint32_t (&r)[32]) {
       : "r"(taddr));
 }
 
-// A-operand conversion of one 32-bit word of int8 weights (4 consecutive k),
-// for bf16 activations: bf16 has too few mantissa bits for a byte, so each
-// weight is split exactly into two bf16 terms
-//   w = (128 + (b & 127)) + (-128 * (1 + [b < 0]))
-// that feed two MMAs into the same accumulator: one byte-permute and two
-// logic ops per pair of weights. (fp16 activations take one exact fp16 per
-// weight, i8x4_to_f16x2x2, and one MMA.)
-__device__ __forceinline__ void i8x4_to_bf16_split(uint32_t w, uint32_t& a1_lo, uint32_t& a1_hi, uint32_t& a2_lo,
-                                                   uint32_t& a2_hi) {
-  const uint32_t t01 = __byte_perm(w, 0x43434343u, 0x4140);  // halves 0x43b0, 0x43b1
-  const uint32_t t23 = __byte_perm(w, 0x43434343u, 0x4342);  // halves 0x43b2, 0x43b3
-  a1_lo = t01 & 0x437F437Fu;                  // 128 + (b & 127)
-  a1_hi = t23 & 0x437F437Fu;
-  a2_lo = (t01 & 0x00800080u) | 0xC300C300u;  // -128 or -256
-  a2_hi = (t23 & 0x00800080u) | 0xC300C300u;
-}
-
 template <int NB, typename XT>
 __global__ void __launch_bounds__(kUmThreads, 1)
     umma_w8a16_kernel(const __grid_constant__ CUtensorMap wmap, const __grid_constant__ CUtensorMap xmap,
                       const SkinnyArgs a) {
-  constexpr bool kSplitA = std::is_same<XT, __nv_bfloat16>::value;  // two bf16 MMAs per 16 k
-  constexpr int HALF = NB / 2;                  // accumulator columns per dequant warpgroup
-  constexpr int XS = NB * 256;                  // activation tile bytes per 128-k stage
-  constexpr int kSlotCols = kSplitA ? 64 : 32;  // tensor-memory columns per 64-k A slot
-  constexpr int kNA = 192 / kSlotCols;          // A slots (3 for bf16, 6 for fp16)
+  // Weights and activations share one 16-bit type per MMA: every int8 value is
+  // exact in bf16 (8 significant bits) and in fp16, so one MMA per 16 k.
+  constexpr uint32_t kFmt = std::is_same<XT, __nv_bfloat16>::value ? 1u : 0u;
+  constexpr int HALF = NB / 2;      // accumulator columns per dequant warpgroup
+  constexpr int XS = NB * 256;      // activation tile bytes per 128-k stage
+  constexpr int kSlotCols = 32;     // tensor-memory columns per 64-k A slot
+  constexpr int kNA = 192 / kSlotCols;  // A slots
   constexpr uint32_t kDCol = 192;
-  constexpr uint32_t kIdesc = umma_idesc(kSplitA ? 1u : 0u, kSplitA ? 1u : 0u, 128, NB);
+  constexpr uint32_t kIdesc = umma_idesc(kFmt, kFmt, 128, NB);
   extern __shared__ uint8_t smem_raw[];
   uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
   const int split = gridDim.y;
@@ -268,7 +251,6 @@ __global__ void __launch_bounds__(kUmThreads, 1)
           for (int i = 0; i < 4; ++i) {
             const uint64_t bdesc = smem_desc_k_sw128(xaddr + xs * XS + h * (NB * 128) + i * 32);
             umma_f16_ts(tmem + kDCol, acol + 8 * i, bdesc, kIdesc, (it | h | i) != 0 ? 1u : 0u);
-            if (kSplitA) umma_f16_ts(tmem + kDCol, acol + 32 + 8 * i, bdesc, kIdesc, 1u);
           }
           tc_commit(&aempty[slot]);
           QTTS_TRACE_DETAIL(1, hs);
@@ -309,19 +291,11 @@ __global__ void __launch_bounds__(kUmThreads, 1)
       __syncwarp();
       if (lane == 0) mbar_arrive(&wempty[s]);
       uint32_t r1[32];
-      uint32_t r2[kSplitA ? 32 : 1];
 #pragma unroll
       for (int cc = 0; cc < 4; ++cc) {
         const uint32_t wd[4] = {v[cc].x, v[cc].y, v[cc].z, v[cc].w};
 #pragma unroll
-        for (int e = 0; e < 4; ++e) {
-          const int c = 8 * cc + 2 * e;
-          if constexpr (kSplitA) {
-            i8x4_to_bf16_split(wd[e], r1[c], r1[c + 1], r2[c], r2[c + 1]);
-          } else {
-            i8x4_to_f16x2x2(wd[e], r1[c], r1[c + 1]);
-          }
-        }
+        for (int e = 0; e < 4; ++e) Dequant<XT>::run(wd[e], r1[8 * cc + 2 * e], r1[8 * cc + 2 * e + 1]);
       }
       const int slot = hs % kNA;
       if (hs >= kNA) {
@@ -334,7 +308,6 @@ __global__ void __launch_bounds__(kUmThreads, 1)
       }
       if (lane == 0 && quarter == 0) QTTS_TRACE_DETAIL(3, hs);
       tmem_st_x32(tmem + lane_base + kSlotCols * slot, r1);
-      if constexpr (kSplitA) tmem_st_x32(tmem + lane_base + kSlotCols * slot + 32, r2);
       tc_wait_st();
       if (lane == 0 && quarter == 0) QTTS_TRACE_DETAIL(4, hs);
       tc_fence_before();
