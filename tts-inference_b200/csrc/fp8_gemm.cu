@@ -340,10 +340,13 @@ Fp8Plan plan_fp8(int M, int N, int K, int split_req) {
   p.split = split;
   p.k_per_cta = ((K + split - 1) / split + 127) / 128 * 128;
   const int n_iters = p.k_per_cta / 128;
+  // Stage ring as deep as shared memory allows: after the dependency wait a
+  // CTA streams at (bytes in flight) / (memory latency), and the grid is at
+  // most one CTA per SM.
   const size_t fixed = fp8_smem(p.nb, 0, split);
-  const size_t budget = 100 * 1024;
+  const size_t budget = 200 * 1024;
   int stages = fixed < budget ? static_cast<int>((budget - fixed) / (kF8StageW + p.nb * 128)) : 0;
-  stages = stages > 6 ? 6 : stages;
+  stages = stages > 12 ? 12 : stages;
   stages = stages < n_iters ? stages : n_iters;
   stages = stages < 2 ? 2 : stages;
   p.stages = stages;

@@ -503,7 +503,10 @@ SkinnyPlan plan_umma(int M, int N, int K, int G, int split_req) {
   p.k_per_cta = kpc_for(split);
   const int n_iters = p.k_per_cta / 128;
   // Activation ring: 4 tiles (never more than the slice); weight ring: fill
-  // a ~100 KiB budget so the next kernel's CTA fits beside this one.
+  // a ~100 KiB budget so the next kernel's CTA fits beside this one. (A
+  // deeper ring does not help: the dequant warps run at most three stages
+  // ahead of the MMAs, which are bound by the ~115-cycle cost of each
+  // 128-row tcgen05.mma.)
   int xstages = n_iters < 4 ? n_iters : 4;
   xstages = xstages < 1 ? 1 : xstages;
   const size_t fixed = umma_smem(nb, 0, xstages, split);
