@@ -466,6 +466,85 @@ def sharded_sweep(world: int, rank: int, device, seed: int) -> dict:
     }
 
 
+class FusedMathFp32:
+    """The math of the reference's int8 kernel (qtts/quant/kernels.py:114-135) in torch fp32:
+    x times the exact int8 weight, fp32 accumulation, the per-channel scale after the K loop,
+    then the cast. The parity check of config 4 (TF32 off)."""
+
+    name = "fused_math_fp32"
+
+    def apply(self, layer, x, bias):
+        acc = torch.nn.functional.linear(x.float(), layer.int8_weight.float()) * layer.int8_scale.float()
+        if bias is not None:
+            acc = acc + bias.float()
+        return acc.to(x.dtype)
+
+
+def talker_frames(seed: int, batch: int = 8) -> dict:
+    """Config 4: frames/s of the random-init talker decode step + code predictor at batch 8 in
+    one CUDA graph: all linears bf16 (cuBLAS), all linears int8 weight-only (this library),
+    and int8 where calibration measures it faster (the reference's default); plus the codes
+    of the all-int8 frame against the reference kernel's math in fp32 on the same weights."""
+    from qtts_b200.config import QuantConfig
+    from qtts_b200.decode_step import Frame, timed_frames_per_s
+    from qtts_b200.layers.linear import iter_linears
+    from qtts_b200.quant import build_method, quantize_module
+
+    frame = Frame(batch, seed=seed)
+    fps_bf16, ms_bf16 = timed_frames_per_s(frame)
+    bytes_bf16 = frame.frame_weight_bytes()
+    frame.graph = None
+    cfg = QuantConfig(method="int8_weight_only", targets=("talker", "code_predictor"), exclude_substrings=(),
+                      calibrate=False)
+    method = build_method(cfg)
+    rep_t = quantize_module(frame.talker, method, cfg, "talker")
+    rep_p = quantize_module(frame.predictor, method, cfg, "code_predictor")
+    torch.cuda.empty_cache()
+    fps_int8, ms_int8 = timed_frames_per_s(frame)
+    codes = frame.codes.clone()
+    # Same int8 weights through the reference kernel's math in fp32.
+    layers = [layer for _, layer in iter_linears(frame.talker)] + [layer for _, layer in iter_linears(frame.predictor)]
+    tf32 = torch.backends.cuda.matmul.allow_tf32
+    torch.backends.cuda.matmul.allow_tf32 = False
+    ref_method = FusedMathFp32()
+    for layer in layers:
+        layer.quant_method = ref_method
+    ref = frame.run().clone()
+    torch.backends.cuda.matmul.allow_tf32 = tf32
+    for layer in layers:
+        layer.quant_method = method
+    bytes_int8 = frame.frame_weight_bytes()
+    del frame
+    torch.cuda.empty_cache()
+    # int8 only where calibration measures it faster than bf16 (--quant-calibrate, the default).
+    frame = Frame(batch, seed=seed)
+    cal = QuantConfig(method="int8_weight_only", targets=("talker", "code_predictor"), exclude_substrings=())
+    cal_method = build_method(cal, calibration_batch=batch)
+    cal_t = quantize_module(frame.talker, cal_method, cal, "talker")
+    cal_p = quantize_module(frame.predictor, cal_method, cal, "code_predictor")
+    torch.cuda.empty_cache()
+    fps_cal, ms_cal = timed_frames_per_s(frame)
+    del frame
+    torch.cuda.empty_cache()
+    return {
+        "workload": "config 4: random-init talker decode step (28 layers, 512-token KV cache, masked codec head) "
+        "+ code predictor (5 layers, 15 sequential codebook steps, 15 heads) at batch 8, one CUDA graph per frame",
+        "frames_per_s_int8": round(fps_int8, 1),
+        "frames_per_s_bf16": round(fps_bf16, 1),
+        "speedup_vs_bf16": round(fps_int8 / fps_bf16, 3),
+        "ms_per_step_int8": round(ms_int8, 3),
+        "ms_per_step_bf16": round(ms_bf16, 3),
+        "linear_weight_bytes_per_step": {"int8": bytes_int8, "bf16": bytes_bf16},
+        "weight_gbs_int8": round(bytes_int8 / (ms_int8 * 1e-3) / 1e9, 1),
+        "layers_int8": {"talker": rep_t.get("converted"), "code_predictor": rep_p.get("converted")},
+        "frames_per_s_int8_calibrated": round(fps_cal, 1),
+        "layers_int8_calibrated": {"talker": cal_t.get("converted"), "code_predictor": cal_p.get("converted"),
+                                   "declined": (cal_t.get("declined") or 0) + (cal_p.get("declined") or 0)},
+        "code0_match_vs_fused_math_fp32": float((codes[:, 0] == ref[:, 0]).float().mean().item()),
+        "all_codes_match_vs_fused_math_fp32": float((codes == ref).float().mean().item()),
+    }
+
+
 def auto_kernel(m: int) -> str:
     """The kernel the library's automatic choice launches for M activation rows (capi.cu)."""
     return "skinny_w8a16_kernel" if m <= 16 else "umma_w8a16_kernel"
@@ -604,6 +683,8 @@ def run_gpu_arm(args) -> None:
     fp8 = fp8_sweep(device, args.seed) if args.fp8 and rank == 0 else None
     barrier(world)
     sharded = sharded_sweep(world, rank, device, args.seed) if args.sharded else None
+    talker = talker_frames(args.seed) if args.talker and rank == 0 else None
+    barrier(world)
 
     # ---- end to end: host buffers in, results out, through the public API
     h2d = sum(pt.m * pt.k * 2 for pt in points)
@@ -683,6 +764,7 @@ def run_gpu_arm(args) -> None:
             "per_point": per_point,
             "fp8": fp8,
             "sharded": sharded,
+            "talker": talker,
         }
         print(json.dumps(line), flush=True)
     if world > 1:
@@ -727,6 +809,8 @@ def main(argv=None) -> int:
     ap.add_argument("--variant", default=None, help="force a kernel variant (e.g. 0x104); default: library choice")
     ap.add_argument("--no-bf16-compare", dest="bf16_compare", action="store_false")
     ap.add_argument("--no-fp8", dest="fp8", action="store_false", help="skip the config-3 fp8 sweep")
+    ap.add_argument("--no-talker", dest="talker", action="store_false",
+                    help="skip the config-4 talker + code predictor frames/s measurement")
     ap.add_argument("--no-sharded", dest="sharded", action="store_false",
                     help="skip the config-5 N-sharded GEMM + all-gather sweep")
     ap.add_argument("--no-cpu-baseline", action="store_true")

@@ -1,0 +1,72 @@
+"""The decode-step workload (talker step + code predictor) with int8 weight-only linears.
+
+North-star parity for the model: the greedy codebook-0 ids of the random-init
+talker step with the library's kernels equal those of the reference int8
+kernel's math (exact int8 weight, fp32 accumulation, scale after the K loop,
+qtts/quant/kernels.py:114-135) run in torch fp32 on the same int8 weights; and
+the CUDA graph of a frame replays the eager frame exactly.
+"""
+
+from __future__ import annotations
+
+import pytest
+import torch
+
+from conftest import require_b200
+from qtts_b200.config import QuantConfig
+from qtts_b200.decode_step import Frame
+from qtts_b200.layers.linear import iter_linears
+from qtts_b200.quant import build_method, quantize_module
+
+pytestmark = pytest.mark.gpu
+
+
+class FusedMathFp32:
+    name = "fused_math_fp32"
+
+    def apply(self, layer, x, bias):
+        acc = torch.nn.functional.linear(x.float(), layer.int8_weight.float()) * layer.int8_scale.float()
+        if bias is not None:
+            acc = acc + bias.float()
+        return acc.to(x.dtype)
+
+
+@pytest.fixture(scope="module")
+def frame():
+    require_b200()
+    f = Frame(8, talker_layers=28, predictor_layers=2, codebooks=4, seed=5)
+    cfg = QuantConfig(method="int8_weight_only", targets=("talker", "code_predictor"), exclude_substrings=(),
+                      calibrate=False)
+    method = build_method(cfg)
+    rep = quantize_module(f.talker, method, cfg, "talker")
+    assert rep["converted"] == 28 * 4 + 1
+    quantize_module(f.predictor, method, cfg, "code_predictor")
+    f.method = method
+    return f
+
+
+def test_code0_matches_reference_math(frame):
+    ours = frame.run().clone()
+    layers = [l for _, l in iter_linears(frame.talker)] + [l for _, l in iter_linears(frame.predictor)]
+    tf32 = torch.backends.cuda.matmul.allow_tf32
+    torch.backends.cuda.matmul.allow_tf32 = False
+    for layer in layers:
+        layer.quant_method = FusedMathFp32()
+    try:
+        ref = frame.run().clone()
+    finally:
+        torch.backends.cuda.matmul.allow_tf32 = tf32
+        for layer in layers:
+            layer.quant_method = frame.method
+    assert torch.equal(ours[:, 0], ref[:, 0]), f"code 0: {ours[:, 0].tolist()} vs {ref[:, 0].tolist()}"
+    assert (ours == ref).float().mean().item() >= 0.9
+
+
+def test_graph_replay_equals_eager(frame):
+    eager = frame.run().clone()
+    frame.capture()
+    frame.codes.zero_()
+    frame.graph.replay()
+    torch.cuda.synchronize()
+    assert torch.equal(frame.codes, eager)
+    frame.graph = None
