@@ -116,7 +116,8 @@ class Block(nn.Module):
 
 
 class Talker(nn.Module):
-    def __init__(self, batch: int, dtype=torch.bfloat16, device="cuda", layers: int = TALKER.layers) -> None:
+    def __init__(self, batch: int, dtype=torch.bfloat16, device="cuda", layers: int = TALKER.layers,
+                 seed: int = 0) -> None:
         super().__init__()
         d = Dims(layers=layers, hidden=TALKER.hidden, inter=TALKER.inter)
         self.d = d
@@ -125,8 +126,10 @@ class Talker(nn.Module):
         self.codec_head = LinearBase(d.hidden, CODEC_VOCAB, dtype=dtype, device=device)
         slots = 768  # key length 513 bucketed, as the reference's graphs do
         shape = (layers, batch, d.kv_heads, slots, d.head_dim)
-        self.cache_k = torch.randn(shape, dtype=dtype, device=device)
-        self.cache_v = torch.randn(shape, dtype=dtype, device=device)
+        gen = torch.Generator(device=device)
+        gen.manual_seed(seed)
+        self.cache_k = torch.randn(shape, generator=gen, device=device).to(dtype)
+        self.cache_v = torch.randn(shape, generator=gen, device=device).to(dtype)
         mask = torch.full((CODEC_VOCAB,), float("-inf"), device=device)
         mask[1:2048] = 0.0
         mask[2150] = 0.0
@@ -146,7 +149,7 @@ class Talker(nn.Module):
 
 class CodePredictor(nn.Module):
     def __init__(self, dtype=torch.bfloat16, device="cuda", layers: int = PREDICTOR.layers,
-                 codebooks: int = CODEBOOKS - 1) -> None:
+                 codebooks: int = CODEBOOKS - 1, seed: int = 0) -> None:
         super().__init__()
         d = Dims(layers=layers, hidden=PREDICTOR.hidden, inter=PREDICTOR.inter)
         self.d = d
@@ -157,9 +160,12 @@ class CodePredictor(nn.Module):
         self.lm_head = nn.ModuleList([LinearBase(d.hidden, CODE_VOCAB, dtype=dtype, device=device)
                                       for _ in range(codebooks)])
         # Embeddings of code 0 (from the talker's codec vocabulary) and of codes 1..15.
+        gen = torch.Generator(device=device)
+        gen.manual_seed(seed)
         self.embed = nn.ParameterList(
-            [nn.Parameter(torch.randn(CODEC_VOCAB if i == 0 else CODE_VOCAB, d.hidden, dtype=dtype,
-                                      device=device) * 0.02, requires_grad=False) for i in range(codebooks)])
+            [nn.Parameter((torch.randn(CODEC_VOCAB if i == 0 else CODE_VOCAB, d.hidden, generator=gen,
+                                       device=device) * 0.02).to(dtype), requires_grad=False)
+             for i in range(codebooks)])
         self.cos, self.sin = rope_tables(torch.arange(codebooks + 1, device=device), d.head_dim)
 
     def run(self, talker_hidden: torch.Tensor, code0: torch.Tensor) -> torch.Tensor:
@@ -197,8 +203,8 @@ class Frame:
     def __init__(self, batch: int = 8, *, device="cuda", talker_layers: int = TALKER.layers,
                  predictor_layers: int = PREDICTOR.layers, codebooks: int = CODEBOOKS - 1, seed: int = 0) -> None:
         self.batch = batch
-        self.talker = Talker(batch, device=device, layers=talker_layers)
-        self.predictor = CodePredictor(device=device, layers=predictor_layers, codebooks=codebooks)
+        self.talker = Talker(batch, device=device, layers=talker_layers, seed=seed + 3)
+        self.predictor = CodePredictor(device=device, layers=predictor_layers, codebooks=codebooks, seed=seed + 4)
         random_init_(self.talker, seed)
         random_init_(self.predictor, seed + 1)
         gen = torch.Generator(device=device)
