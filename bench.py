@@ -777,10 +777,28 @@ def run_gpu_arm(args) -> None:
 
 def run_single(spec: str, calls: int = 3) -> None:
     """One (shape, M) point, `calls` launches with an L2 flush before each:
-    a small case for `ncu` captures. spec = "<shape>:<M>[:<variant>]"."""
+    a small case for `ncu` captures. spec = "<shape>:<M>[:<variant>]" (W8A16) or
+    "fp8:<shape>:<M>" (activation quantization + fp8 GEMM)."""
     from qtts_b200.quant import kernels as qk
 
     parts = spec.split(":")
+    if parts[0] == "fp8":
+        label, m = parts[1], int(parts[2])
+        n, k = {lab: (n_, k_) for lab, n_, k_ in SHAPES}[label]
+        torch.cuda.set_device(0)
+        gen = torch.Generator(device="cuda")
+        gen.manual_seed(0)
+        w = torch.randn((n, k), generator=gen, device="cuda") * 0.02
+        wq, ws = qk.quantize_fp8_rows(w)
+        x = torch.randn((m, k), generator=gen, device="cuda").to(torch.bfloat16)
+        flush = torch.empty(256 << 20, dtype=torch.uint8, device="cuda")
+        for _ in range(calls):
+            flush.zero_()
+            xq, sx = qk.fp8_quant_rows(x)
+            qk.fp8_scaled_mm(xq, sx, wq, ws, None, torch.bfloat16)
+        torch.cuda.synchronize()
+        print(json.dumps({"single": spec, "ok": True}))
+        return
     label, m = parts[0], int(parts[1])
     variant = int(parts[2], 0) if len(parts) > 2 else 0
     n, k = {lab: (n_, k_) for lab, n_, k_ in SHAPES}[label]
