@@ -545,9 +545,10 @@ def talker_frames(seed: int, batch: int = 8) -> dict:
     }
 
 
-def auto_kernel(m: int) -> str:
-    """The kernel the library's automatic choice launches for M activation rows (capi.cu)."""
-    return "skinny_w8a16_kernel" if m <= 16 else "umma_w8a16_kernel"
+def auto_kernel(m: int, n: int, k: int) -> str:
+    """The kernel the library's automatic choice launches (the rule in capi.cu)."""
+    umma_mid = m > 8 and -(-n // 128) * 4 <= 148 and k <= 4096
+    return "skinny_w8a16_kernel" if (m <= 16 and not umma_mid) else "umma_w8a16_kernel"
 
 
 def run_gpu_arm(args) -> None:
@@ -633,7 +634,7 @@ def run_gpu_arm(args) -> None:
     # region (every call of a point launches the same kernel).
     by_kernel: dict = {}
     for pt, ms in zip(points, per_point_ms):
-        kname = auto_kernel(pt.m) if args.variant is None else f"variant {args.variant}"
+        kname = auto_kernel(pt.m, pt.n, pt.k) if args.variant is None else f"variant {args.variant}"
         kb, kt = by_kernel.get(kname, (0.0, 0.0))
         by_kernel[kname] = (kb + pt.bytes * CALLS_PER_GRAPH * REPLAYS_PER_POINT, kt + ms)
     dom_kernel = max(by_kernel, key=lambda kk: by_kernel[kk][1])

@@ -403,10 +403,15 @@ static int w8a16_dispatch(const void* x, int64_t gsx, int64_t ldx, int x_dtype, 
   int split = variant & 0xF;
   int rgroups = (variant >> 4) & 0xF;
   if (variant == QTTS_VARIANT_AUTO) {
-    // Up to 16 rows: the split-K streaming kernel. Wider batches: the
-    // tcgen05 kernel, whose per-instruction cost does not grow with M. (The
-    // whole-K streaming kernel, 0x300, is a calibration candidate.)
-    family = skinny_ok ? (M <= 16 ? 0x100 : 0x200) : 0;
+    // Up to 8 rows: the split-K streaming kernel. Past 16: the tcgen05 kernel,
+    // whose per-instruction cost does not grow with M. 9..16 rows: tcgen05
+    // where a 4-way K split fits one wave and K is moderate (measured on
+    // B200: qkv 7.9 vs 9.6 us, o_proj 6.0 vs 6.2; gate_up and down_proj stay
+    // faster on the streaming kernel). The whole-K streaming kernel (0x300)
+    // is a calibration candidate.
+    const int zg_auto = group_index != nullptr ? 1 : G;
+    const bool umma_mid = M > 8 && ((N + 127) / 128) * zg_auto * 4 <= kNumSMs && K <= 4096;
+    family = skinny_ok ? ((M <= 16 && !umma_mid) ? 0x100 : 0x200) : 0;
     split = 0;
     rgroups = 0;
   }

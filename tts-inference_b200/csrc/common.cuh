@@ -239,6 +239,16 @@ __device__ __forceinline__ void pdl_launch_dependents() {
   asm volatile("griddepcontrol.launch_dependents;" ::: "memory");
 }
 
+// ---- split-K receive rows ------------------------------------------------------
+// A receive row holds NB fp32 partial sums (NB / 4 chunks of 16 bytes). Chunk c
+// of row r is stored at chunk c ^ (r & mask): writers keep 16-byte st.async
+// stores, and a reader taking the same chunk of consecutive rows spreads over
+// the banks instead of hitting one.
+__host__ __device__ constexpr int recv_chunk_mask(int nb) { return (nb / 4 > 16 ? 16 : nb / 4) - 1; }
+__device__ __forceinline__ int recv_offset(int row, int chunk, int nb) {
+  return row * nb + ((chunk ^ (row & recv_chunk_mask(nb))) << 2);
+}
+
 // ---- named barriers ------------------------------------------------------------
 
 __device__ __forceinline__ void named_bar_sync(int id, int nthreads) {

@@ -201,15 +201,19 @@ __global__ void __launch_bounds__(kF8Threads, 1)
         if (c0 == 0) cluster_wait();
         const int owner = row / rpo;
         const int lr = row - owner * rpo;
-        float* dst = recv + (crank * rpo + lr) * NB + c0;
+        const int rrow = static_cast<int>(crank) * rpo + lr;
         if (owner == static_cast<int>(crank)) {
 #pragma unroll
-          for (int c = 0; c < 16; c += 4) *reinterpret_cast<float4*>(dst + c) = make_float4(v[c], v[c + 1], v[c + 2], v[c + 3]);
+          for (int c = 0; c < 16; c += 4)
+            *reinterpret_cast<float4*>(recv + recv_offset(rrow, (c0 + c) >> 2, NB)) =
+                make_float4(v[c], v[c + 1], v[c + 2], v[c + 3]);
         } else {
-          const uint32_t rdst = mapa_shared(smem_u32(dst), owner);
           const uint32_t rbar = mapa_shared(smem_u32(recv_bar), owner);
 #pragma unroll
-          for (int c = 0; c < 16; c += 4) st_async_f32x4(rdst + c * 4, v[c], v[c + 1], v[c + 2], v[c + 3], rbar);
+          for (int c = 0; c < 16; c += 4) {
+            const uint32_t rdst = mapa_shared(smem_u32(recv + recv_offset(rrow, (c0 + c) >> 2, NB)), owner);
+            st_async_f32x4(rdst, v[c], v[c + 1], v[c + 2], v[c + 3], rbar);
+          }
         }
       }
     }
@@ -221,17 +225,30 @@ __global__ void __launch_bounds__(kF8Threads, 1)
         have = mbar_wait_bounded(recv_bar, 0, 4 * a.wait_ns);  // peers always send
       }
       if (have && !cta_err) {
+        // Thread = (owned row, 4 batch columns): one 16-byte load per peer.
         const int rbase = static_cast<int>(crank) * rpo;
-        for (int i = tid; i < rpo * mrows; i += kF8EpiWarps * 32) {
-          const int m = i / rpo;
-          const int lr = i - m * rpo;
+        const int quads = (mrows + 3) / 4;
+        for (int i = tid; i < rpo * quads; i += kF8EpiWarps * 32) {
+          const int mq = i / rpo;
+          const int lr = i - mq * rpo;
           const int nn = n0 + rbase + lr;
           if (nn < a.N) {
-            float r = 0.f;
-            for (int p = 0; p < split; ++p) r += recv[(p * rpo + lr) * NB + m];
-            r = r * a.scale_x[m0 + m] * a.scale_w[nn];
-            if (a.bias != nullptr) r += to_float(static_cast<const OT*>(a.bias)[nn]);
-            og[static_cast<int64_t>(m) * a.ldo + nn] = from_float<OT>(r);
+            float4 r = make_float4(0.f, 0.f, 0.f, 0.f);
+            for (int p = 0; p < split; ++p) {
+              const float4 t = *reinterpret_cast<const float4*>(recv + recv_offset(p * rpo + lr, mq, NB));
+              r.x += t.x;
+              r.y += t.y;
+              r.z += t.z;
+              r.w += t.w;
+            }
+            const float sw = a.scale_w[nn];
+            const float bias = a.bias != nullptr ? to_float(static_cast<const OT*>(a.bias)[nn]) : 0.f;
+            const float rv[4] = {r.x, r.y, r.z, r.w};
+#pragma unroll
+            for (int q = 0; q < 4; ++q) {
+              const int m = 4 * mq + q;
+              if (m < mrows) og[static_cast<int64_t>(m) * a.ldo + nn] = from_float<OT>(rv[q] * a.scale_x[m0 + m] * sw + bias);
+            }
           }
         }
       }
@@ -326,15 +343,11 @@ Fp8Plan plan_fp8(int M, int N, int K, int split_req) {
   int split = split_req;
   if (split == 0) {
     // One CTA per SM at most (each MMA instruction is the unit of tensor
-    // work), K split within 4 CTAs. The partial sums a split exchanges grow
-    // with the batch tile, so past 16 rows a CTA keeps >= 1536 of K
-    // (measured on B200: splitting K = 2048 at 32+ rows costs more than the
-    // extra CTAs gain; K = 6144 gains from a split of 4 at every M).
+    // work), K split within 4 CTAs: a narrow weight (32 row tiles) otherwise
+    // leaves most SMs idle, and the partial-sum exchange is cheap.
     split = 1;
     for (int s = 1; s <= 4; s *= 2) {
-      if (n_tiles * m_chunks * s > kNumSMs) break;
-      if (p.nb > 16 && s > 1 && K / s < 1536) break;
-      split = s;
+      if (n_tiles * m_chunks * s <= kNumSMs) split = s;
     }
   }
   p.split = split;

@@ -355,15 +355,19 @@ __global__ void __launch_bounds__(kUmThreads, 1)
       cluster_wait();  // every peer's receive barrier is initialized
       const int owner = row / rpo;
       const int lr = row - owner * rpo;
-      float* dst = recv + (crank * rpo + lr) * NB + HALF * half;
+      const int rrow = static_cast<int>(crank) * rpo + lr;
       if (owner == static_cast<int>(crank)) {
 #pragma unroll
-        for (int c = 0; c < HALF; c += 4) *reinterpret_cast<float4*>(dst + c) = make_float4(v[c], v[c + 1], v[c + 2], v[c + 3]);
+        for (int c = 0; c < HALF; c += 4)
+          *reinterpret_cast<float4*>(recv + recv_offset(rrow, (HALF * half + c) >> 2, NB)) =
+              make_float4(v[c], v[c + 1], v[c + 2], v[c + 3]);
       } else {
-        const uint32_t rdst = mapa_shared(smem_u32(dst), owner);
         const uint32_t rbar = mapa_shared(smem_u32(recv_bar), owner);
 #pragma unroll
-        for (int c = 0; c < HALF; c += 4) st_async_f32x4(rdst + c * 4, v[c], v[c + 1], v[c + 2], v[c + 3], rbar);
+        for (int c = 0; c < HALF; c += 4) {
+          const uint32_t rdst = mapa_shared(smem_u32(recv + recv_offset(rrow, (HALF * half + c) >> 2, NB)), owner);
+          st_async_f32x4(rdst, v[c], v[c + 1], v[c + 2], v[c + 3], rbar);
+        }
       }
       named_bar_sync(1, kUmDqWarps * 32);
       bool have = mbar_wait_bounded(recv_bar, 0, a.wait_ns);
@@ -372,18 +376,31 @@ __global__ void __launch_bounds__(kUmThreads, 1)
         have = mbar_wait_bounded(recv_bar, 0, 4 * a.wait_ns);  // peers always send
       }
       if (have && valid && !cta_err) {
+        // Thread = (owned row, 4 batch columns): one 16-byte load per peer.
         const int rbase = static_cast<int>(crank) * rpo;
-        for (int i = tid; i < rpo * mrows; i += kUmDqWarps * 32) {
-          const int m = i / rpo;
-          const int lr = i - m * rpo;
+        const int quads = (mrows + 3) / 4;
+        for (int i = tid; i < rpo * quads; i += kUmDqWarps * 32) {
+          const int mq = i / rpo;
+          const int lr = i - mq * rpo;
           const int n = n0 + rbase + lr;
           if (n < a.N) {
-            float r = 0.f;
-            for (int p = 0; p < split; ++p) r += recv[(p * rpo + lr) * NB + m];
+            float4 r = make_float4(0.f, 0.f, 0.f, 0.f);
+            for (int p = 0; p < split; ++p) {
+              const float4 t = *reinterpret_cast<const float4*>(recv + recv_offset(p * rpo + lr, mq, NB));
+              r.x += t.x;
+              r.y += t.y;
+              r.z += t.z;
+              r.w += t.w;
+            }
             const int64_t ch = static_cast<int64_t>(group) * a.N + n;
-            r *= load_as_float(a.scale, a.scale_dtype, ch);
-            if (a.bias != nullptr) r += to_float(static_cast<const XT*>(a.bias)[ch]);
-            og[static_cast<int64_t>(m) * a.ldo + n] = from_float<XT>(r);
+            const float sc = load_as_float(a.scale, a.scale_dtype, ch);
+            const float bias = a.bias != nullptr ? to_float(static_cast<const XT*>(a.bias)[ch]) : 0.f;
+            const float rv[4] = {r.x, r.y, r.z, r.w};
+#pragma unroll
+            for (int q = 0; q < 4; ++q) {
+              const int m = 4 * mq + q;
+              if (m < mrows) og[static_cast<int64_t>(m) * a.ldo + n] = from_float<XT>(rv[q] * sc + bias);
+            }
           }
         }
       }
