@@ -397,7 +397,8 @@ __global__ void __launch_bounds__(kSkThreads, 2)
         have = mbar_wait_bounded(recv_bar, 0, 4 * a.wait_ns);
       }
       if (tid == 0) QTTS_TRACE_STAMP(7);
-      if (have && valid && !cta_err) {
+      if (have && valid && !cta_err && mrows <= 2) {
+        // One or two real batch rows: thread = (owned row, batch row).
         const int rbase = static_cast<int>(crank) * rpo;
         for (int i = tid; i < rpo * mrows; i += kSkConsumerWarps * 32) {
           const int m = i / rpo;
@@ -412,6 +413,36 @@ __global__ void __launch_bounds__(kSkThreads, 2)
             r *= load_as_float(a.scale, a.scale_dtype, ch);
             if (a.bias != nullptr) r += to_float(static_cast<const XT*>(a.bias)[ch]);
             og[static_cast<int64_t>(m) * a.ldo + n] = from_float<XT>(r);
+          }
+        }
+      } else if (have && valid && !cta_err) {
+        // Thread = (owned row, 4 batch columns): one 16-byte load per CTA of
+        // the cluster, in rank order.
+        const int rbase = static_cast<int>(crank) * rpo;
+        const int quads = (mrows + 3) / 4;
+        for (int i = tid; i < rpo * quads; i += kSkConsumerWarps * 32) {
+          const int mq = i / rpo;
+          const int lr = i - mq * rpo;
+          const int n = n0 + rbase + lr;
+          if (n < a.N) {
+            float4 r = make_float4(0.f, 0.f, 0.f, 0.f);
+            for (int p = 0; p < split; ++p) {
+              const float* src = (p == static_cast<int>(crank)) ? red + (rbase + lr) * MB : recv + (p * rpo + lr) * MB;
+              const float4 t = *reinterpret_cast<const float4*>(src + 4 * mq);
+              r.x += t.x;
+              r.y += t.y;
+              r.z += t.z;
+              r.w += t.w;
+            }
+            const int64_t ch = static_cast<int64_t>(group) * a.N + n;
+            const float sc = load_as_float(a.scale, a.scale_dtype, ch);
+            const float bias = a.bias != nullptr ? to_float(static_cast<const XT*>(a.bias)[ch]) : 0.f;
+            const float rv[4] = {r.x, r.y, r.z, r.w};
+#pragma unroll
+            for (int q = 0; q < 4; ++q) {
+              const int m = 4 * mq + q;
+              if (m < mrows) og[static_cast<int64_t>(m) * a.ldo + n] = from_float<XT>(rv[q] * sc + bias);
+            }
           }
         }
       }
