@@ -294,6 +294,22 @@ def capture(fn):
 FP8_ROWS = (16, 32, 64, 128)
 
 
+def graph_us_per_call(fn, reps=3) -> float:
+    """Capture ``fn`` (CALLS_PER_GRAPH calls) in a CUDA graph, replay it once
+    untimed and ``reps`` times between CUDA events; microseconds per call."""
+    stream = torch.cuda.current_stream()
+    g = capture(fn)
+    e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    g.replay()
+    e0.record(stream)
+    for _ in range(reps):
+        g.replay()
+    e1.record(stream)
+    torch.cuda.synchronize()
+    del g
+    return e0.elapsed_time(e1) * 1e3 / (reps * CALLS_PER_GRAPH)
+
+
 def fp8_algo_bytes(n: int, k: int, m: int) -> int:
     """Config-3 bytes of one fp8 linear: e4m3 W + fp32 scale, bf16 x in, e4m3 x + fp32 scale
     out and back in (the separate quantization step), bf16 out."""
@@ -310,19 +326,7 @@ def fp8_sweep(device, seed: int) -> dict:
     gen = torch.Generator(device=device)
     gen.manual_seed(seed + 7)
     out: dict = {}
-    stream = torch.cuda.current_stream()
-
-    def timed(fn, reps=3):
-        g = capture(fn)
-        e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
-        g.replay()
-        e0.record(stream)
-        for _ in range(reps):
-            g.replay()
-        e1.record(stream)
-        torch.cuda.synchronize()
-        del g
-        return e0.elapsed_time(e1) * 1e3 / (reps * CALLS_PER_GRAPH)
+    timed = graph_us_per_call
 
     tot_bytes = tot_us = tot_ref_us = 0.0
     for label, n, k in SHAPES:
@@ -375,6 +379,65 @@ def fp8_sweep(device, seed: int) -> dict:
         "4 talker shapes at M in {16,32,64,128}; weights rotate through >= 256 MB per shape",
         "gbs": round(tot_bytes / (tot_us * 1e-6) / 1e9, 1),
         "torch_gbs": round(tot_bytes / (tot_ref_us * 1e-6) / 1e9, 1) if tot_ref_us else None,
+        "per_point": out,
+    }
+
+
+def fp8w_sweep(device, seed: int) -> dict:
+    """fp8 weight-only (e4m3 weights, bf16 activations, Fp8WeightOnlyMethod.apply) on the
+    config-2 grid: the four talker shapes at M in {1..64}, weights rotating through
+    >= 256 MB per shape. Beside it, the one route open to the reference, whose
+    Fp8WeightOnlyMethod is unimplemented (qtts/quant/fp8.py:92-122): dequantize the
+    weight to bf16 in global memory, then F.linear. Bytes per call as config 2 (N*K
+    weight bytes, fp32 scale)."""
+    from qtts_b200.quant import kernels as qk
+
+    gen = torch.Generator(device=device)
+    gen.manual_seed(seed + 11)
+    out: dict = {}
+    tot_bytes = tot_us = tot_ref_us = 0.0
+    for label, n, k in SHAPES:
+        p = pool_size(n, k)
+        wq = torch.empty((p, n, k), dtype=torch.float8_e4m3fn, device=device)
+        ws = torch.empty((p, n), dtype=torch.float32, device=device)
+        for i in range(p):
+            w = torch.randn((n, k), generator=gen, device=device) * 0.02
+            q, s = qk.quantize_fp8_rows(w)
+            wq[i].copy_(q)
+            ws[i].copy_(s)
+            del w, q, s
+        for m in ROWS:
+            x = torch.randn((m, k), generator=gen, device=device).to(torch.bfloat16)
+            y = torch.empty((m, n), dtype=torch.bfloat16, device=device)
+
+            def ours(x=x, y=y):
+                for c in range(CALLS_PER_GRAPH):
+                    qk.fp8w_gemm(x, wq[c % p], ws[c % p], None, out=y)
+
+            def dequant_linear(x=x):
+                for c in range(CALLS_PER_GRAPH):
+                    w_bf16 = (wq[c % p].to(torch.float32) * ws[c % p][:, None]).to(torch.bfloat16)
+                    torch.nn.functional.linear(x, w_bf16)
+
+            us = graph_us_per_call(ours)
+            ref_us = graph_us_per_call(dequant_linear, reps=1)
+            b = n * k + 4 * n + 2 * m * k + 2 * m * n
+            out.setdefault(label, {})[str(m)] = {
+                "us": round(us, 3),
+                "gbs": round(b / (us * 1e-6) / 1e9, 1),
+                "dequant_linear_us": round(ref_us, 3),
+                "speedup": round(ref_us / us, 2),
+            }
+            tot_bytes += b
+            tot_us += us
+            tot_ref_us += ref_us
+        del wq, ws
+        torch.cuda.empty_cache()
+    return {
+        "workload": "fp8 e4m3 weight-only (one fused launch per linear) on the 4 talker shapes at "
+        "M in {1,2,4,8,16,32,64}; weights rotate through >= 256 MB per shape",
+        "gbs": round(tot_bytes / (tot_us * 1e-6) / 1e9, 1),
+        "dequant_linear_gbs": round(tot_bytes / (tot_ref_us * 1e-6) / 1e9, 1),
         "per_point": out,
     }
 
@@ -682,6 +745,7 @@ def run_gpu_arm(args) -> None:
 
     # ---- config 3 (fp8) and config 5 (N-sharded GEMM + all-gather), outside the timed region
     fp8 = fp8_sweep(device, args.seed) if args.fp8 and rank == 0 else None
+    fp8w = fp8w_sweep(device, args.seed) if args.fp8w and rank == 0 else None
     barrier(world)
     sharded = sharded_sweep(world, rank, device, args.seed) if args.sharded else None
     talker = talker_frames(args.seed) if args.talker and rank == 0 else None
@@ -764,6 +828,7 @@ def run_gpu_arm(args) -> None:
             "device_status": status,
             "per_point": per_point,
             "fp8": fp8,
+            "fp8_weight_only": fp8w,
             "sharded": sharded,
             "talker": talker,
         }
@@ -778,11 +843,28 @@ def run_gpu_arm(args) -> None:
 
 def run_single(spec: str, calls: int = 3) -> None:
     """One (shape, M) point, `calls` launches with an L2 flush before each:
-    a small case for `ncu` captures. spec = "<shape>:<M>[:<variant>]" (W8A16) or
-    "fp8:<shape>:<M>" (activation quantization + fp8 GEMM)."""
+    a small case for `ncu` captures. spec = "<shape>:<M>[:<variant>]" (W8A16),
+    "fp8:<shape>:<M>" (activation quantization + fp8 GEMM) or "fp8w:<shape>:<M>"
+    (fp8 weight-only)."""
     from qtts_b200.quant import kernels as qk
 
     parts = spec.split(":")
+    if parts[0] == "fp8w":
+        label, m = parts[1], int(parts[2])
+        n, k = {lab: (n_, k_) for lab, n_, k_ in SHAPES}[label]
+        torch.cuda.set_device(0)
+        gen = torch.Generator(device="cuda")
+        gen.manual_seed(0)
+        w = torch.randn((n, k), generator=gen, device="cuda") * 0.02
+        wq, ws = qk.quantize_fp8_rows(w)
+        x = torch.randn((m, k), generator=gen, device="cuda").to(torch.bfloat16)
+        flush = torch.empty(256 << 20, dtype=torch.uint8, device="cuda")
+        for _ in range(calls):
+            flush.zero_()
+            qk.fp8w_gemm(x, wq, ws)
+        torch.cuda.synchronize()
+        print(json.dumps({"single": spec, "ok": True}))
+        return
     if parts[0] == "fp8":
         label, m = parts[1], int(parts[2])
         n, k = {lab: (n_, k_) for lab, n_, k_ in SHAPES}[label]
@@ -828,6 +910,7 @@ def main(argv=None) -> int:
     ap.add_argument("--variant", default=None, help="force a kernel variant (e.g. 0x104); default: library choice")
     ap.add_argument("--no-bf16-compare", dest="bf16_compare", action="store_false")
     ap.add_argument("--no-fp8", dest="fp8", action="store_false", help="skip the config-3 fp8 sweep")
+    ap.add_argument("--no-fp8w", dest="fp8w", action="store_false", help="skip the fp8 weight-only sweep")
     ap.add_argument("--no-talker", dest="talker", action="store_false",
                     help="skip the config-4 talker + code predictor frames/s measurement")
     ap.add_argument("--no-sharded", dest="sharded", action="store_false",

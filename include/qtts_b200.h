@@ -155,6 +155,19 @@ QTTS_API int qtts_w8a16_grouped_gemm(const void* x, int64_t group_stride_x, int6
                             const int64_t* group_index,
                             int variant, unsigned flags, void* stream);
 
+/* fp8 weight-only GEMM (no counterpart in the reference, which leaves
+ * Fp8WeightOnlyMethod unimplemented, qtts/quant/fp8.py:92-122): the W8A16
+ * contract with e4m3 weights,
+ *   out[m,n] = cast( (sum_k x[m,k] * e4m3(w[n,k])) * scale[n] + bias[n] )
+ * w: [N, K] e4m3 bytes (ld ldw), scale [N] (e.g. from qtts_quantize_fp8_rows);
+ * every other argument, the variants and the status codes as for
+ * qtts_w8a16_gemm. The weights are converted to 16-bit floats in registers
+ * (exactly); the whole-K streaming variant (QTTS_VARIANT_STREAM) does not
+ * apply, and the split-K streaming variants take M <= 16. */
+QTTS_API int qtts_fp8w_gemm(const void* x, int64_t ldx, int x_dtype, const uint8_t* w, int64_t ldw,
+                   const void* scale, int scale_dtype, const void* bias, void* out, int64_t ldo,
+                   int M, int N, int K, int variant, unsigned flags, void* stream);
+
 /* ---- load-time weight quantizers ------------------------------------------
  * Division by a constant (`amax / 127`, `/ 448`) follows torch on a CUDA
  * tensor, where `tensor / number` is evaluated as `tensor * fl32(1 / number)`:

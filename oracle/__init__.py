@@ -21,6 +21,7 @@ from .qtts_ref import (  # noqa: F401
     e4m3_encode,
     fp16_round,
     fp8_scaled_mm_reference,
+    fp8_weight_only_reference,
     naive_dequant_linear,
     quantize_act_fp8,
     quantize_weight_fp8,

@@ -187,6 +187,16 @@ def naive_dequant_linear(x_bf16, q, scale_bf16) -> np.ndarray:
     return bf16_round(acc)
 
 
+def fp8_weight_only_reference(x, wq, scale_w, bias=None) -> np.ndarray:
+    """fp8 weight-only (the method qtts/quant/fp8.py:92-122 leaves unimplemented), in float64:
+    x times the decoded e4m3 weight, the per-channel scale after the sum, plus bias."""
+    w = e4m3_decode(wq).astype(np.float64)
+    out = (np.asarray(x, dtype=np.float64) @ w.T) * np.asarray(scale_w, dtype=np.float64).reshape(1, -1)
+    if bias is not None:
+        out = out + np.asarray(bias, dtype=np.float64)[None, :]
+    return out
+
+
 def fp8_scaled_mm_reference(xq, scale_x, wq, scale_w, bias=None) -> np.ndarray:
     """qtts/quant/fp8.py:79-88 -- ``_scaled_mm(q, W.t(), scale_a, scale_b) + bias`` in float64."""
     a = e4m3_decode(xq).astype(np.float64)

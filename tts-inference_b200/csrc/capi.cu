@@ -70,7 +70,7 @@ EncodeTiledFn get_encode_fn() {
 struct GenericArgs {
   const void* x;
   int64_t ldx, gsx;
-  const int8_t* w;
+  const int8_t* w;  // int8 codes, or e4m3 bytes when w_fmt == kWE4M3
   int64_t ldw;
   const void* scale;
   int scale_dtype;
@@ -79,7 +79,13 @@ struct GenericArgs {
   int64_t ldo, gso;
   int M, N, K, G;
   const int64_t* group_index;
+  int w_fmt;
 };
+
+__device__ __forceinline__ float e4m3_to_float(uint8_t v) {
+  const __half_raw h = __nv_cvt_fp8_to_halfraw(static_cast<__nv_fp8_storage_t>(v), __NV_E4M3);
+  return __half2float(__half(h));
+}
 
 template <typename XT>
 __global__ void __launch_bounds__(256) generic_w8a16_kernel(const GenericArgs a) {
@@ -109,7 +115,7 @@ __global__ void __launch_bounds__(256) generic_w8a16_kernel(const GenericArgs a)
 #pragma unroll
   for (int i = 0; i < 8; ++i) acc[i] = 0.f;
   for (int k = lane; k < a.K; k += 32) {
-    const float wv = static_cast<float>(wr[k]);
+    const float wv = a.w_fmt == kWE4M3 ? e4m3_to_float(static_cast<uint8_t>(wr[k])) : static_cast<float>(wr[k]);
 #pragma unroll
     for (int i = 0; i < 8; ++i) {
       if (m0 + i < a.M) acc[i] += to_float(xg[static_cast<int64_t>(m0 + i) * a.ldx + k]) * wv;
@@ -176,11 +182,6 @@ struct GenericFp8Args {
   int64_t ldo;
   int M, N, K;
 };
-
-__device__ __forceinline__ float e4m3_to_float(uint8_t v) {
-  const __half_raw h = __nv_cvt_fp8_to_halfraw(static_cast<__nv_fp8_storage_t>(v), __NV_E4M3);
-  return __half2float(__half(h));
-}
 
 template <typename OT>
 __global__ void __launch_bounds__(256) generic_fp8_kernel(const GenericFp8Args a) {
@@ -383,7 +384,7 @@ uint64_t qtts_set_wait_limit_ns(uint64_t limit_ns) {
 static int w8a16_dispatch(const void* x, int64_t gsx, int64_t ldx, int x_dtype, const int8_t* w, int64_t ldw,
                           const void* scale, int scale_dtype, const void* bias, void* out, int64_t gso,
                           int64_t ldo, int G, int M, int N, int K, const int64_t* group_index, int variant,
-                          unsigned flags, void* stream_ptr) {
+                          unsigned flags, void* stream_ptr, int w_fmt = kWInt8) {
   if (M < 0 || N < 0 || K < 0 || G < 1) return QTTS_ERR_SHAPE;
   if (M == 0 || N == 0) return QTTS_OK;
   if (x == nullptr || w == nullptr || scale == nullptr || out == nullptr) return QTTS_ERR_NULL;
@@ -417,10 +418,11 @@ static int w8a16_dispatch(const void* x, int64_t gsx, int64_t ldx, int x_dtype, 
   }
   if (variant == QTTS_VARIANT_GENERIC || family == 0) {
     if (variant != QTTS_VARIANT_AUTO && variant != QTTS_VARIANT_GENERIC) return QTTS_ERR_VARIANT;
-    GenericArgs ga{x, ldx, gsx, w, ldw, scale, scale_dtype, bias, out, ldo, gso, M, N, K, G, group_index};
+    GenericArgs ga{x, ldx, gsx, w, ldw, scale, scale_dtype, bias, out, ldo, gso, M, N, K, G, group_index, w_fmt};
     return launch_generic_w8a16(ga, x_dtype, pdl, stream);
   }
   if (family == 0x300) {
+    if (w_fmt != kWInt8) return QTTS_ERR_VARIANT;  // the whole-K kernel folds the int8 bias
     if (!skinny_ok) return QTTS_ERR_ALIGN;
     if (M > 16) return QTTS_ERR_VARIANT;
     if (!(rgroups == 0 || stream_rows_ok(rgroups))) return QTTS_ERR_VARIANT;
@@ -453,6 +455,7 @@ static int w8a16_dispatch(const void* x, int64_t gsx, int64_t ldx, int x_dtype, 
     sa.x_pitch = plan.x_pitch;
     sa.m_chunks = plan.m_chunks;
     sa.group_index = group_index;
+    sa.w_fmt = w_fmt;
     sa.wait_ns = current_wait_limit_ns();
     sa.trace_slot = -1;
 #ifdef QTTS_TRACE
@@ -462,6 +465,7 @@ static int w8a16_dispatch(const void* x, int64_t gsx, int64_t ldx, int x_dtype, 
   }
   if (family == 0x100) {
     if (!skinny_ok) return QTTS_ERR_ALIGN;
+    if (w_fmt == kWE4M3 && M > 16) return QTTS_ERR_VARIANT;
     if (!(split == 0 || split == 1 || split == 2 || split == 4 || split == 8)) return QTTS_ERR_VARIANT;
     if (!(rgroups == 0 || rgroups == 1 || rgroups == 2 || rgroups == 4 || rgroups == 8)) return QTTS_ERR_VARIANT;
     if ((variant & 0xF000) != 0) return QTTS_ERR_VARIANT;
@@ -493,6 +497,7 @@ static int w8a16_dispatch(const void* x, int64_t gsx, int64_t ldx, int x_dtype, 
     sa.x_pitch = plan.x_pitch;
     sa.m_chunks = plan.m_chunks;
     sa.group_index = group_index;
+    sa.w_fmt = w_fmt;
     sa.wait_ns = current_wait_limit_ns();
     sa.trace_slot = -1;
 #ifdef QTTS_TRACE
@@ -537,6 +542,7 @@ static int w8a16_dispatch(const void* x, int64_t gsx, int64_t ldx, int x_dtype, 
     sa.x_pitch = plan.x_pitch;  // activation ring depth
     sa.m_chunks = plan.m_chunks;
     sa.group_index = group_index;
+    sa.w_fmt = w_fmt;
     sa.wait_ns = current_wait_limit_ns();
     sa.trace_slot = -1;
 #ifdef QTTS_TRACE
@@ -553,6 +559,13 @@ int qtts_w8a16_gemm(const void* x, int64_t ldx, int x_dtype, const int8_t* w, in
                     unsigned flags, void* stream) {
   return w8a16_dispatch(x, 0, ldx, x_dtype, w, ldw, scale, scale_dtype, bias, out, 0, ldo, 1, M, N, K, nullptr,
                         variant, flags, stream);
+}
+
+int qtts_fp8w_gemm(const void* x, int64_t ldx, int x_dtype, const uint8_t* w, int64_t ldw, const void* scale,
+                   int scale_dtype, const void* bias, void* out, int64_t ldo, int M, int N, int K, int variant,
+                   unsigned flags, void* stream) {
+  return w8a16_dispatch(x, 0, ldx, x_dtype, reinterpret_cast<const int8_t*>(w), ldw, scale, scale_dtype, bias, out,
+                        0, ldo, 1, M, N, K, nullptr, variant, flags, stream, kWE4M3);
 }
 
 int qtts_w8a16_grouped_gemm(const void* x, int64_t group_stride_x, int64_t ldx, int x_dtype, const int8_t* w,

@@ -297,6 +297,30 @@ __device__ __forceinline__ void i8x4_to_f16x2x2(uint32_t w, uint32_t& lo, uint32
   asm("sub.f16x2 %0, %1, %2;" : "=r"(hi) : "r"(b), "r"(kBias));
 }
 
+// e4m3 weights (fp8 weight-only): every e4m3 value (3 mantissa bits, 2^-9 ..
+// 448) is exact in fp16 and in bf16. Two bytes -> one f16 pair in a single
+// conversion; bf16 goes through fp32 (exact) and a pair repack.
+__device__ __forceinline__ void e4m3x4_to_f16x2x2(uint32_t w, uint32_t& lo, uint32_t& hi) {
+  const unsigned short w01 = static_cast<unsigned short>(w & 0xFFFFu);
+  const unsigned short w23 = static_cast<unsigned short>(w >> 16);
+  asm("cvt.rn.f16x2.e4m3x2 %0, %1;" : "=r"(lo) : "h"(w01));
+  asm("cvt.rn.f16x2.e4m3x2 %0, %1;" : "=r"(hi) : "h"(w23));
+}
+__device__ __forceinline__ uint32_t f16x2_to_bf16x2(uint32_t h) {
+  uint32_t r;
+  asm("{\n.reg .f32 f0, f1;\n.reg .b16 h0, h1;\nmov.b32 {h0, h1}, %1;\ncvt.f32.f16 f0, h0;\ncvt.f32.f16 f1, h1;\n"
+      "cvt.rn.bf16x2.f32 %0, f1, f0;\n}"
+      : "=r"(r)
+      : "r"(h));
+  return r;
+}
+__device__ __forceinline__ void e4m3x4_to_bf16x2x2(uint32_t w, uint32_t& lo, uint32_t& hi) {
+  uint32_t a, b;
+  e4m3x4_to_f16x2x2(w, a, b);
+  lo = f16x2_to_bf16x2(a);
+  hi = f16x2_to_bf16x2(b);
+}
+
 template <typename T>
 struct Dequant;
 template <>
@@ -310,6 +334,20 @@ struct Dequant<__half> {
   static __device__ __forceinline__ void run(uint32_t w, uint32_t& lo, uint32_t& hi) {
     i8x4_to_f16x2x2(w, lo, hi);
   }
+};
+
+// Weight format dispatch: int8 (W8A16) or e4m3 (fp8 weight-only).
+template <typename T, bool kE4M3>
+struct WDequant {
+  static __device__ __forceinline__ void run(uint32_t w, uint32_t& lo, uint32_t& hi) { Dequant<T>::run(w, lo, hi); }
+};
+template <>
+struct WDequant<__half, true> {
+  static __device__ __forceinline__ void run(uint32_t w, uint32_t& lo, uint32_t& hi) { e4m3x4_to_f16x2x2(w, lo, hi); }
+};
+template <>
+struct WDequant<__nv_bfloat16, true> {
+  static __device__ __forceinline__ void run(uint32_t w, uint32_t& lo, uint32_t& hi) { e4m3x4_to_bf16x2x2(w, lo, hi); }
 };
 
 // ---- mma.sync m16n8k16, fp32 accumulate ---------------------------------------------

@@ -35,7 +35,11 @@ struct SkinnyArgs {
   uint64_t wait_ns;
   int trace_slot;  // timeline probe slot (-1: off); only read in -DQTTS_TRACE builds
   int64_t gsx_rows;  // group stride of x in rows (tcgen05 kernel: x is read through a tensor map)
+  int w_fmt;         // kWInt8 or kWE4M3
 };
+
+constexpr int kWInt8 = 0;  // int8 weights (W8A16)
+constexpr int kWE4M3 = 1;  // e4m3 weights (fp8 weight-only)
 
 struct SkinnyPlan {
   int mt;        // batch n-tiles of 8 (1, 2, 4, 8)

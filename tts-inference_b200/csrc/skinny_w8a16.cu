@@ -59,7 +59,7 @@ __device__ __forceinline__ void bulk_load(void* dst, const void* src, uint32_t b
       : "memory");
 }
 
-template <int MT, int R, typename XT>
+template <int MT, int R, typename XT, bool E4M3 = false>
 __global__ void __launch_bounds__(kSkThreads, 2)
     skinny_w8a16_kernel(const __grid_constant__ CUtensorMap wmap, const SkinnyArgs a) {
   constexpr int MB = MT * 8;       // batch rows per CTA (MMA N dimension)
@@ -285,22 +285,22 @@ __global__ void __launch_bounds__(kSkThreads, 2)
       if (lane == 0) mbar_arrive(&empty[s]);
 
       uint32_t A[2][4][4];
-      i8x4_to_f16x2x2(wa0.x, A[0][0][0], A[0][0][2]);
-      i8x4_to_f16x2x2(wb0.x, A[0][0][1], A[0][0][3]);
-      i8x4_to_f16x2x2(wa0.y, A[0][1][0], A[0][1][2]);
-      i8x4_to_f16x2x2(wb0.y, A[0][1][1], A[0][1][3]);
-      i8x4_to_f16x2x2(wa0.z, A[0][2][0], A[0][2][2]);
-      i8x4_to_f16x2x2(wb0.z, A[0][2][1], A[0][2][3]);
-      i8x4_to_f16x2x2(wa0.w, A[0][3][0], A[0][3][2]);
-      i8x4_to_f16x2x2(wb0.w, A[0][3][1], A[0][3][3]);
-      i8x4_to_f16x2x2(wa1.x, A[1][0][0], A[1][0][2]);
-      i8x4_to_f16x2x2(wb1.x, A[1][0][1], A[1][0][3]);
-      i8x4_to_f16x2x2(wa1.y, A[1][1][0], A[1][1][2]);
-      i8x4_to_f16x2x2(wb1.y, A[1][1][1], A[1][1][3]);
-      i8x4_to_f16x2x2(wa1.z, A[1][2][0], A[1][2][2]);
-      i8x4_to_f16x2x2(wb1.z, A[1][2][1], A[1][2][3]);
-      i8x4_to_f16x2x2(wa1.w, A[1][3][0], A[1][3][2]);
-      i8x4_to_f16x2x2(wb1.w, A[1][3][1], A[1][3][3]);
+      WDequant<__half, E4M3>::run(wa0.x, A[0][0][0], A[0][0][2]);
+      WDequant<__half, E4M3>::run(wb0.x, A[0][0][1], A[0][0][3]);
+      WDequant<__half, E4M3>::run(wa0.y, A[0][1][0], A[0][1][2]);
+      WDequant<__half, E4M3>::run(wb0.y, A[0][1][1], A[0][1][3]);
+      WDequant<__half, E4M3>::run(wa0.z, A[0][2][0], A[0][2][2]);
+      WDequant<__half, E4M3>::run(wb0.z, A[0][2][1], A[0][2][3]);
+      WDequant<__half, E4M3>::run(wa0.w, A[0][3][0], A[0][3][2]);
+      WDequant<__half, E4M3>::run(wb0.w, A[0][3][1], A[0][3][3]);
+      WDequant<__half, E4M3>::run(wa1.x, A[1][0][0], A[1][0][2]);
+      WDequant<__half, E4M3>::run(wb1.x, A[1][0][1], A[1][0][3]);
+      WDequant<__half, E4M3>::run(wa1.y, A[1][1][0], A[1][1][2]);
+      WDequant<__half, E4M3>::run(wb1.y, A[1][1][1], A[1][1][3]);
+      WDequant<__half, E4M3>::run(wa1.z, A[1][2][0], A[1][2][2]);
+      WDequant<__half, E4M3>::run(wb1.z, A[1][2][1], A[1][2][3]);
+      WDequant<__half, E4M3>::run(wa1.w, A[1][3][0], A[1][3][2]);
+      WDequant<__half, E4M3>::run(wb1.w, A[1][3][1], A[1][3][3]);
 
       const uint32_t xk = xbase + it * SW * 2;
 #pragma unroll
@@ -473,10 +473,10 @@ __global__ void __launch_bounds__(kSkThreads, 2)
 
 namespace {
 
-template <int MT, int R, typename XT>
+template <int MT, int R, typename XT, bool E4M3>
 int launch_skinny_t(const CUtensorMap& map, const SkinnyArgs& args, dim3 grid, int split, size_t smem,
                     bool pdl, cudaStream_t stream) {
-  auto kern = skinny_w8a16_kernel<MT, R, XT>;
+  auto kern = skinny_w8a16_kernel<MT, R, XT, E4M3>;
   static int configured[64] = {0};
   int dev = 0;
   cudaGetDevice(&dev);
@@ -511,33 +511,39 @@ int launch_skinny_t(const CUtensorMap& map, const SkinnyArgs& args, dim3 grid, i
   return e == cudaSuccess ? QTTS_OK : QTTS_ERR_LAUNCH;
 }
 
-template <int MT, typename XT>
+template <int MT, typename XT, bool E4M3>
 int launch_skinny_r(int r, const CUtensorMap& map, const SkinnyArgs& args, dim3 grid, int split, size_t smem,
                     bool pdl, cudaStream_t stream) {
   switch (r) {
     case 1:
-      return launch_skinny_t<MT, 1, XT>(map, args, grid, split, smem, pdl, stream);
+      return launch_skinny_t<MT, 1, XT, E4M3>(map, args, grid, split, smem, pdl, stream);
     case 2:
-      return launch_skinny_t<MT, 2, XT>(map, args, grid, split, smem, pdl, stream);
+      return launch_skinny_t<MT, 2, XT, E4M3>(map, args, grid, split, smem, pdl, stream);
     case 4:
-      return launch_skinny_t<MT, 4, XT>(map, args, grid, split, smem, pdl, stream);
+      return launch_skinny_t<MT, 4, XT, E4M3>(map, args, grid, split, smem, pdl, stream);
     default:
-      return launch_skinny_t<MT, 8, XT>(map, args, grid, split, smem, pdl, stream);
+      return launch_skinny_t<MT, 8, XT, E4M3>(map, args, grid, split, smem, pdl, stream);
   }
 }
 
 template <typename XT>
 int launch_skinny_mt(const SkinnyPlan& p, const CUtensorMap& map, const SkinnyArgs& args, bool pdl,
                      cudaStream_t stream) {
+  if (args.w_fmt == kWE4M3) {
+    // fp8 weight-only takes this kernel up to 16 rows only.
+    if (p.mt == 1) return launch_skinny_r<1, XT, true>(p.r, map, args, p.grid, p.split, p.smem, pdl, stream);
+    if (p.mt == 2) return launch_skinny_r<2, XT, true>(p.r, map, args, p.grid, p.split, p.smem, pdl, stream);
+    return QTTS_ERR_VARIANT;
+  }
   switch (p.mt) {
     case 1:
-      return launch_skinny_r<1, XT>(p.r, map, args, p.grid, p.split, p.smem, pdl, stream);
+      return launch_skinny_r<1, XT, false>(p.r, map, args, p.grid, p.split, p.smem, pdl, stream);
     case 2:
-      return launch_skinny_r<2, XT>(p.r, map, args, p.grid, p.split, p.smem, pdl, stream);
+      return launch_skinny_r<2, XT, false>(p.r, map, args, p.grid, p.split, p.smem, pdl, stream);
     case 4:
-      return launch_skinny_r<4, XT>(p.r, map, args, p.grid, p.split, p.smem, pdl, stream);
+      return launch_skinny_r<4, XT, false>(p.r, map, args, p.grid, p.split, p.smem, pdl, stream);
     default:
-      return launch_skinny_r<8, XT>(p.r, map, args, p.grid, p.split, p.smem, pdl, stream);
+      return launch_skinny_r<8, XT, false>(p.r, map, args, p.grid, p.split, p.smem, pdl, stream);
   }
 }
 

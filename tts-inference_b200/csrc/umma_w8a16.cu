@@ -84,7 +84,7 @@ __device__ __forceinline__ void tmem_ld<32>(uint32_t taddr, uint32_t (&r)[32]) {
       : "r"(taddr));
 }
 
-template <int NB, typename XT>
+template <int NB, typename XT, bool E4M3 = false>
 __global__ void __launch_bounds__(kUmThreads, 1)
     umma_w8a16_kernel(const __grid_constant__ CUtensorMap wmap, const __grid_constant__ CUtensorMap xmap,
                       const SkinnyArgs a) {
@@ -295,7 +295,7 @@ __global__ void __launch_bounds__(kUmThreads, 1)
       for (int cc = 0; cc < 4; ++cc) {
         const uint32_t wd[4] = {v[cc].x, v[cc].y, v[cc].z, v[cc].w};
 #pragma unroll
-        for (int e = 0; e < 4; ++e) Dequant<XT>::run(wd[e], r1[8 * cc + 2 * e], r1[8 * cc + 2 * e + 1]);
+        for (int e = 0; e < 4; ++e) WDequant<XT, E4M3>::run(wd[e], r1[8 * cc + 2 * e], r1[8 * cc + 2 * e + 1]);
       }
       const int slot = hs % kNA;
       if (hs >= kNA) {
@@ -438,10 +438,10 @@ __global__ void __launch_bounds__(kUmThreads, 1)
 
 namespace {
 
-template <int NB, typename XT>
+template <int NB, typename XT, bool E4M3>
 int launch_umma_t(const CUtensorMap& map, const CUtensorMap& xmap, const SkinnyArgs& args, const SkinnyPlan& p,
                   bool pdl, cudaStream_t stream) {
-  auto kern = umma_w8a16_kernel<NB, XT>;
+  auto kern = umma_w8a16_kernel<NB, XT, E4M3>;
   static int configured[64] = {0};
   int dev = 0;
   cudaGetDevice(&dev);
@@ -475,17 +475,24 @@ int launch_umma_t(const CUtensorMap& map, const CUtensorMap& xmap, const SkinnyA
   return cudaLaunchKernelEx(&cfg, kern, map, xmap, args) == cudaSuccess ? QTTS_OK : QTTS_ERR_LAUNCH;
 }
 
+template <typename XT, bool E4M3>
+int launch_umma_w(const CUtensorMap& map, const CUtensorMap& xmap, const SkinnyArgs& args, const SkinnyPlan& p,
+                  bool pdl, cudaStream_t stream) {
+  switch (p.mt) {
+    case 2:
+      return launch_umma_t<16, XT, E4M3>(map, xmap, args, p, pdl, stream);
+    case 4:
+      return launch_umma_t<32, XT, E4M3>(map, xmap, args, p, pdl, stream);
+    default:
+      return launch_umma_t<64, XT, E4M3>(map, xmap, args, p, pdl, stream);
+  }
+}
+
 template <typename XT>
 int launch_umma_nb(const CUtensorMap& map, const CUtensorMap& xmap, const SkinnyArgs& args, const SkinnyPlan& p,
                    bool pdl, cudaStream_t stream) {
-  switch (p.mt) {
-    case 2:
-      return launch_umma_t<16, XT>(map, xmap, args, p, pdl, stream);
-    case 4:
-      return launch_umma_t<32, XT>(map, xmap, args, p, pdl, stream);
-    default:
-      return launch_umma_t<64, XT>(map, xmap, args, p, pdl, stream);
-  }
+  return args.w_fmt == kWE4M3 ? launch_umma_w<XT, true>(map, xmap, args, p, pdl, stream)
+                              : launch_umma_w<XT, false>(map, xmap, args, p, pdl, stream);
 }
 
 size_t umma_smem(int nb, int wstages, int xstages, int split) {

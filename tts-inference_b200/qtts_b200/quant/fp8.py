@@ -9,18 +9,20 @@ epilogue applies the row scale, the column scale and the bias.
 
 :class:`Fp8WeightOnlyMethod` is the variant the reference leaves unimplemented
 (fp8.py:92-122) because its only available form dequantizes into global
-memory. Here it runs on the same fused weight-streaming design as int8
-weight-only; until that kernel lands it raises like the reference.
+memory. Here it runs on the same fused weight-streaming kernels as int8
+weight-only, with the e4m3 weights converted in registers.
 """
 
 from __future__ import annotations
 
 import torch
+import torch.nn.functional as F
 
 from ..layers.linear import LinearBase
 from ..utils import get_logger
 from .base import QuantMethodBase
-from .kernels import fp8_quant_rows, fp8_scaled_mm, kernel_available, quantize_fp8_rows
+from .calibrate import worth_quantizing
+from .kernels import fp8_quant_rows, fp8_scaled_mm, fp8w_gemm, kernel_available, quantize_fp8_rows
 
 logger = get_logger("quant.fp8")
 
@@ -75,12 +77,65 @@ class Fp8Method(QuantMethodBase):
 
 
 class Fp8WeightOnlyMethod(QuantMethodBase):
-    """fp8 weights, bf16 activations -- not implemented yet, as in the reference."""
+    """fp8 (e4m3) weights, bf16 activations, converted inside the GEMM.
+
+    The reference leaves this method unimplemented (fp8.py:92-122): its only
+    route would dequantize the weight into global memory on every call. Here
+    the weight streams as e4m3 bytes into the same kernels as int8
+    weight-only and is converted to 16-bit floats in registers (one
+    conversion per two weights, exact), with the per-channel scale applied
+    after the fp32 K loop. Buffers follow :class:`Fp8Method`: ``fp8_weight``
+    is the [K, N] transposed view of the [N, K] e4m3 weight, ``fp8_scale``
+    [1, N] fp32 (amax / 448, fp8.py:45-49). With ``calibrate`` a layer keeps
+    F.linear where the quantized GEMM measures slower at
+    ``calibration_batch`` rows, as int8 weight-only does.
+    """
 
     name = "fp8_weight_only"
 
     def __init__(self, calibrate: bool = True, calibration_batch: int = 16) -> None:
-        raise NotImplementedError(
-            "fp8 weight-only is not implemented: use --quant-method int8_weight_only for the same "
-            "footprint, or --quant-method fp8 for the W8A8 path."
+        available, reason = kernel_available()
+        if not available:
+            raise RuntimeError(f"fp8 weight-only needs the sm_100a kernels of qtts_b200: {reason}")
+        self.calibrate = calibrate
+        self.calibration_batch = calibration_batch
+        self.quantized = 0
+        self.declined = 0
+
+    def _profitable(self, layer: LinearBase, q: torch.Tensor, scale: torch.Tensor) -> bool:
+        if not self.calibrate:
+            return True
+        weight = layer.weight
+        if weight.device.type != "cuda":
+            return False
+        rows = max(1, self.calibration_batch)
+        x = torch.zeros(rows, layer.in_features, device=weight.device, dtype=weight.dtype)
+        return worth_quantizing(
+            lambda: fp8w_gemm(x, q, scale, None),
+            lambda: F.linear(x, weight, None),
+            key=("fp8_wo", layer.out_features, layer.in_features, rows, str(weight.dtype)),
+        )
+
+    def process_weights(self, layer: LinearBase) -> None:
+        q, scale = quantize_weight_fp8(layer.weight)
+        if not self._profitable(layer, q, scale):
+            self.declined += 1
+            layer.register_buffer("fp8_weight", None, persistent=False)
+            return
+        layer.register_buffer("fp8_weight", q.t(), persistent=False)
+        layer.register_buffer("fp8_scale", scale.reshape(1, -1), persistent=False)
+        layer.weight = torch.nn.Parameter(
+            torch.empty(0, dtype=layer.weight.dtype, device=layer.weight.device), requires_grad=False
+        )
+        self.quantized += 1
+
+    def applies_to(self, layer: LinearBase) -> bool:
+        return getattr(layer, "fp8_weight", None) is not None
+
+    def apply(self, layer: LinearBase, x: torch.Tensor, bias: torch.Tensor | None) -> torch.Tensor:
+        return fp8w_gemm(
+            x,
+            layer.fp8_weight.t(),  # type: ignore[attr-defined]
+            layer.fp8_scale.reshape(-1),  # type: ignore[attr-defined]
+            bias,
         )

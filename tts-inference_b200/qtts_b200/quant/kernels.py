@@ -73,13 +73,33 @@ def w8_gemm(
     ``[..., N]``. ``variant`` selects a kernel (see ``include/qtts_b200.h``);
     the default lets the library choose.
     """
+    if weight.dim() != 2 or weight.dtype != torch.int8:
+        raise ValueError(f"weight must be a 2-D int8 tensor, got {tuple(weight.shape)} {weight.dtype}")
+    return _weight_only_gemm(x, weight, scale, bias, variant, out, "qtts_w8a16_gemm")
+
+
+def fp8w_gemm(
+    x: torch.Tensor,
+    weight: torch.Tensor,
+    scale: torch.Tensor,
+    bias: torch.Tensor | None = None,
+    *,
+    variant: int = nat.VARIANT_AUTO,
+    out: torch.Tensor | None = None,
+) -> torch.Tensor:
+    """fp8 weight-only: ``x @ (e4m3(weight) * scale).T + bias``, the W8A16 contract with an
+    e4m3 ``[N, K]`` weight (``torch.float8_e4m3fn``, row-major) converted in registers."""
+    if weight.dim() != 2 or weight.dtype != torch.float8_e4m3fn:
+        raise ValueError(f"weight must be a 2-D float8_e4m3fn tensor, got {tuple(weight.shape)} {weight.dtype}")
+    return _weight_only_gemm(x, weight, scale, bias, variant, out, "qtts_fp8w_gemm")
+
+
+def _weight_only_gemm(x, weight, scale, bias, variant, out, entry: str) -> torch.Tensor:
     ok, reason = nat.available()
     if not ok:
         raise RuntimeError(reason)
     shape = x.shape
     k = shape[-1]
-    if weight.dim() != 2 or weight.dtype != torch.int8:
-        raise ValueError(f"weight must be a 2-D int8 tensor, got {tuple(weight.shape)} {weight.dtype}")
     n = weight.shape[0]
     if weight.shape[1] != k:
         raise ValueError(f"weight is [{n}, {weight.shape[1]}] but x has K={k}")
@@ -101,7 +121,7 @@ def w8_gemm(
         out = torch.empty((rows, n), device=device, dtype=x.dtype)
     elif out.shape != (rows, n) or out.dtype != x.dtype or out.stride(1) != 1:
         raise ValueError(f"out must be [{rows}, {n}] {x.dtype} with unit column stride")
-    code = nat.lib().qtts_w8a16_gemm(
+    code = getattr(nat.lib(), entry)(
         a.data_ptr(), a.stride(0) if rows > 1 else k, nat.dtype_code(a.dtype),
         weight.data_ptr(), weight.stride(0),
         scale.data_ptr(), nat.dtype_code(scale.dtype),
@@ -109,7 +129,7 @@ def w8_gemm(
         out.data_ptr(), out.stride(0) if rows > 1 else n,
         rows, n, k, variant, _flags(), nat.stream_ptr(device),
     )
-    nat.check(code, "qtts_w8a16_gemm")
+    nat.check(code, entry)
     return out.reshape(*shape[:-1], n)
 
 
