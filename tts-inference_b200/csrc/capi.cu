@@ -404,17 +404,30 @@ static int w8a16_dispatch(const void* x, int64_t gsx, int64_t ldx, int x_dtype, 
   int split = variant & 0xF;
   int rgroups = (variant >> 4) & 0xF;
   if (variant == QTTS_VARIANT_AUTO) {
-    // Up to 8 rows: the split-K streaming kernel. Past 16: the tcgen05 kernel,
-    // whose per-instruction cost does not grow with M. 9..16 rows: tcgen05
-    // where a 4-way K split fits one wave and K is moderate (measured on
-    // B200: qkv 7.9 vs 9.6 us, o_proj 6.0 vs 6.2; gate_up and down_proj stay
-    // faster on the streaming kernel). The whole-K streaming kernel (0x300)
-    // is a calibration candidate.
+    // Up to 16 rows: the split-K streaming kernel with its planner's tile and
+    // split (up to two CTAs per SM). Past 16: the tcgen05 kernel, whose
+    // per-instruction cost does not grow with M. Up to 4 rows of int8, the
+    // whole-K streaming kernel where its row tiles (16..96 rows) reach more
+    // CTAs within two per SM than the split-K plan can (gate_up 12288 x 2048
+    // at M = 1: 256 CTAs, 7.2 us, vs 192 CTAs, 9.3 us, measured on B200).
     const int zg_auto = group_index != nullptr ? 1 : G;
-    const bool umma_mid = M > 8 && ((N + 127) / 128) * zg_auto * 4 <= kNumSMs && K <= 4096;
-    family = skinny_ok ? ((M <= 16 && !umma_mid) ? 0x100 : 0x200) : 0;
+    family = skinny_ok ? (M <= 16 ? 0x100 : 0x200) : 0;
     split = 0;
     rgroups = 0;
+    if (family == 0x100 && M <= 4 && w_fmt == kWInt8) {
+      const SkinnyPlan sk = plan_skinny(M, N, K, zg_auto, 0, 0);
+      int best = static_cast<int>(sk.grid.x * sk.grid.y * sk.grid.z);
+      const int rows[5] = {6, 4, 3, 2, 1};
+      for (int i = 0; i < 5; ++i) {
+        const SkinnyPlan st = plan_stream(M, N, K, zg_auto, rows[i]);
+        const int c = static_cast<int>(st.grid.x * st.grid.y * st.grid.z);
+        if (c <= kCtaSlots && c > best && st.smem <= kMaxDynSmem) {
+          best = c;
+          family = 0x300;
+          rgroups = rows[i];
+        }
+      }
+    }
   }
   if (variant == QTTS_VARIANT_GENERIC || family == 0) {
     if (variant != QTTS_VARIANT_AUTO && variant != QTTS_VARIANT_GENERIC) return QTTS_ERR_VARIANT;

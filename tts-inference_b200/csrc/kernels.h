@@ -12,6 +12,7 @@
 namespace qtts {
 
 constexpr int kNumSMs = 148;                 // B200: 2 dies x 74 SMs
+constexpr int kCtaSlots = 2 * kNumSMs;        // two weight-streaming CTAs per SM
 constexpr size_t kMaxDynSmem = 227 * 1024;   // opt-in dynamic shared memory per CTA
 
 // ---- skinny W8A16 ------------------------------------------------------------

@@ -566,18 +566,46 @@ SkinnyPlan plan_skinny(int M, int N, int K, int G, int split_req, int r_req) {
   auto xbytes = [&](int s, int r) { return static_cast<size_t>(mb) * (kpc_for(K, s, 128 * (8 / r)) + 8) * 2; };
   auto ctas = [&](int s, int r) { return ((N + 16 * r - 1) / (16 * r)) * s * G * p.m_chunks; };
   const int splits[4] = {1, 2, 4, 8};
+  const int rgs[4] = {8, 4, 2, 1};
   int split = split_req, r = r_req;
-  if (r == 0) r = 8;  // 128-row tiles: no k-group reduction inside the CTA
-  if (split == 0) {
-    // Smallest cluster split that puts ~a CTA on each of the 148 SMs with the
-    // activation slice in 48 KiB; the largest otherwise.
-    split = 8;
-    for (int si = 0; si < 4; ++si) {
-      const int s_ = splits[si];
-      if (xbytes(s_, r) <= 48 * 1024 && ctas(s_, r) >= 120) {
-        split = s_;
-        break;
+  if (split == 0 || r == 0) {
+    // The most CTAs that still run two to an SM (the chained decode calls are
+    // latency-bound: two CTAs per SM overlap each other's activation fetch,
+    // loop and split-K exchange), activation slice within 48 KiB; ties go to
+    // the larger row tile, then the smaller split. Measured on B200 in chains of
+    // talker linears: qkv and down_proj at M = 1..16 gain 10-15 % over one CTA
+    // per SM. When every choice exceeds two per SM: the fewest CTAs.
+    int best_c = -1, best_s = 0, best_r = 0, min_c = 0, min_s = 0, min_r = 0;
+    for (int ri = 0; ri < 4; ++ri) {
+      if (r != 0 && rgs[ri] != r) continue;
+      for (int si = 0; si < 4; ++si) {
+        if (split != 0 && splits[si] != split) continue;
+        if (xbytes(splits[si], rgs[ri]) > 48 * 1024) continue;
+        // Every CTA of the split must own part of K.
+        if (splits[si] > 1 && (splits[si] - 1) * kpc_for(K, splits[si], 128 * (8 / rgs[ri])) >= K) continue;
+        const int c = ctas(splits[si], rgs[ri]);
+        if (c <= kCtaSlots && c > best_c) {
+          best_c = c;
+          best_s = splits[si];
+          best_r = rgs[ri];
+        }
+        if (min_c == 0 || c < min_c) {
+          min_c = c;
+          min_s = splits[si];
+          min_r = rgs[ri];
+        }
       }
+    }
+    if (best_c > 0) {
+      split = best_s;
+      r = best_r;
+    } else if (min_c > 0) {
+      split = min_s;
+      r = min_r;
+    } else {
+      // No activation slice fits 48 KiB: the largest split (smallest slice).
+      if (r == 0) r = 8;
+      if (split == 0) split = 8;
     }
   }
   (void)x_cap;
@@ -588,9 +616,10 @@ SkinnyPlan plan_skinny(int M, int N, int K, int G, int split_req, int r_req) {
   p.k_per_cta = kpc_for(K, split, sw);
   p.x_pitch = p.k_per_cta + 8;  // +16 bytes: rows of one LDS phase hit distinct banks
   const int n_iters = p.k_per_cta / sw;
-  // Stage ring: fill a ~100 KiB budget (so the next kernel's CTA fits beside
-  // this one under programmatic dependent launch), 2..6 stages, never more
-  // than the slice needs; at least enough to hold the k-group reduction.
+  // Stage ring: fill a ~100 KiB budget (two CTAs per SM), 2..6 stages, never
+  // more than the slice needs; at least enough to hold the k-group reduction.
+  // (Three CTAs per SM up to 8 rows -- 64 registers, 72 KiB -- measured 10-25 %
+  // slower in chained calls.)
   const size_t fixed = skinny_smem(mb, bn, p.x_pitch, 0, split);
   const size_t budget = 100 * 1024;
   int stages = fixed < budget ? static_cast<int>((budget - fixed) / kSkStageBytes) : 0;

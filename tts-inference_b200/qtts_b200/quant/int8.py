@@ -33,8 +33,12 @@ _INT_MM_MIN_ROWS = 17
 #: Batch-row buckets calibration times separately (the kernels' costs change
 #: with the rows of an 8-wide MMA tile that are real, and between tiles).
 _ROW_BUCKETS = (1, 2, 4, 8, 16, 32, 64)
-#: Split-K factors of the split-K streaming kernel calibration chooses from.
+#: Split-K factors and row tiles (groups of 16 weight rows per CTA) of the
+#: split-K streaming kernel calibration chooses from.
 _SPLITS = (1, 2, 4, 8)
+_ROW_GROUPS = (1, 2, 4, 8)
+#: Row tiles of the whole-K streaming kernel (16 * r rows per CTA).
+_STREAM_ROWS = (1, 2, 3, 4, 6)
 #: Split-K factors of the tcgen05 kernel (M > 16).
 _UMMA_SPLITS = (1, 2, 4)
 
@@ -43,7 +47,8 @@ def variant_candidates(bucket: int) -> list[int]:
     """Kernel variants worth timing for up to ``bucket`` activation rows."""
     out = [nat.VARIANT_AUTO]
     if bucket <= 16:
-        out += [nat.variant_skinny(s) for s in _SPLITS] + [nat.variant_stream(0)]
+        out += [nat.variant_skinny(s, r) for s in _SPLITS for r in _ROW_GROUPS]
+        out += [nat.variant_stream(r) for r in _STREAM_ROWS]
     if bucket >= 16:
         out += [nat.variant_umma(s) for s in _UMMA_SPLITS]
     return out
