@@ -203,21 +203,6 @@ __host__ __device__ constexpr uint32_t umma_idesc(uint32_t a_fmt, uint32_t b_fmt
          (static_cast<uint32_t>(m >> 4) << 24);
 }
 
-// Bulk copy from this CTA's shared memory into a peer CTA's shared memory
-// (shared::cluster address), counted in bytes on the peer's mbarrier. Both
-// addresses 16-byte aligned, size a multiple of 16. The source must have been
-// made visible to the async proxy (fence_proxy_async_smem) first.
-__device__ __forceinline__ void bulk_s2s_cluster(uint32_t dst_cluster, const void* src, uint32_t bytes,
-                                                 uint32_t bar_cluster) {
-  asm volatile("cp.async.bulk.shared::cluster.shared::cta.mbarrier::complete_tx::bytes [%0], [%1], %2, [%3];" ::"r"(
-                   dst_cluster),
-               "r"(smem_u32(src)), "r"(bytes), "r"(bar_cluster)
-               : "memory");
-}
-// Waits until this thread's bulk copies have finished reading their sources.
-__device__ __forceinline__ void bulk_wait_read() {
-  asm volatile("cp.async.bulk.commit_group;\ncp.async.bulk.wait_group.read 0;" ::: "memory");
-}
 
 __device__ __forceinline__ void st_async_f32x4(uint32_t remote_addr, float a, float b, float c, float d,
                                                uint32_t remote_bar) {
