@@ -452,7 +452,7 @@ def sharded_sweep(world: int, rank: int, device, seed: int) -> dict:
     timed in a CUDA graph, the all-gather of its [M, ceil(N/g)] block in an eager loop (no
     collective is captured into a graph), each as the max over ranks of CUDA-event time;
     GEMM + all-gather is their sum."""
-    from qtts_b200.sharded import ShardedW8Linear, shard_rows
+    from qtts_b200.sharded import FusedAllGatherW8Linear, ShardedW8Linear, shard_rows
 
     gen = torch.Generator(device=device)
     gen.manual_seed(seed + 11)
@@ -506,22 +506,36 @@ def sharded_sweep(world: int, rank: int, device, seed: int) -> dict:
             for _ in range(SHARD_CALLS):
                 lins[0].gather(block, gathered)
 
+        # The fused form: one kernel per rank per call stores its block into every
+        # rank's gathered buffer over peer memory (the copies share one buffer set).
+        fused = [FusedAllGatherW8Linear(ws[0], ss[0], n, max_rows=m)]
+        fused += [FusedAllGatherW8Linear(ws[i], ss[i], n, max_rows=m, share_from=fused[0]) for i in range(1, copies)]
+
+        def fused_calls():
+            for c in range(SHARD_CALLS):
+                fused[c % copies](x)
+
         gemm_us = time_graph(gemm_only)
         gather_us = time_eager(gather_only) if world > 1 else 0.0  # one GPU: the block is the output
+        fused_us = time_graph(fused_calls)
         total_us = gemm_us + gather_us
         res[f"K{k}_N{n}_M{m}"] = {
             "gemm_us": round(gemm_us, 3),
             "allgather_us": round(gather_us, 3),
             "gemm_allgather_us": round(total_us, 3),
+            "fused_gemm_allgather_us": round(fused_us, 3),
+            "fused_speedup": round(total_us / fused_us, 3),
             "agg_weight_gbs": round(n * k / (total_us * 1e-6) / 1e9, 1),
+            "agg_weight_gbs_fused": round(n * k / (fused_us * 1e-6) / 1e9, 1),
             "agg_weight_gbs_gemm_only": round(n * k / (gemm_us * 1e-6) / 1e9, 1),
             "per_gpu_frac_of_hbm": round(rows * k / (gemm_us * 1e-6) / 1e9 / pk["hbm_gbs"], 4),
         }
-        del ws, ss, lins, x, block, gathered
+        del ws, ss, lins, fused, x, block, gathered
         torch.cuda.empty_cache()
     return {
         "workload": "config 5: int8 W8A16 GEMM sharded along N over the ranks (ceil(N/g) rows each), bf16 "
-        "outputs all-gathered over NCCL; K in {2048,6144}, N in {12288,49152}, M in {1,8,64}",
+        "outputs all-gathered over NCCL (gemm_allgather_us) or by the GEMM kernel itself over peer memory "
+        "(fused_gemm_allgather_us); K in {2048,6144}, N in {12288,49152}, M in {1,8,64}",
         "scaling": "strong",
         "n_gpus": world,
         "allgather_timed": "eager loop, CUDA events" if world > 1 else "single GPU: no exchange",

@@ -168,6 +168,34 @@ QTTS_API int qtts_fp8w_gemm(const void* x, int64_t ldx, int x_dtype, const uint8
                    const void* scale, int scale_dtype, const void* bias, void* out, int64_t ldo,
                    int M, int N, int K, int variant, unsigned flags, void* stream);
 
+/* N-sharded W8A16 GEMM fused with the all-gather of its output. Replaces the
+ * per-rank w8a16 GEMM followed by ncclAllGather of the bf16 blocks (the
+ * multi-GPU form of the standalone GEMM, one exchange step): this rank
+ * computes out = x @ (w * scale).T + bias for its N output channels and the
+ * kernel stores every element straight into the gathered output of EVERY
+ * rank, over peer memory (P2P stores through NVLink), at columns
+ * [col_offset, col_offset + N) of rows [0, M) with leading dimension ldo.
+ *   peer_out    device array [world] of device pointers: rank q's gathered
+ *               buffer (this rank's own included, at index rank), x_dtype
+ *   peer_signal device array [world] of device pointers: rank q's signal pad,
+ *               uint32[2 * world], zero before the first call
+ *   sync        this rank's uint32[2], zero before the first call
+ * Calls are numbered on the device, so the call is CUDA-graph capturable.
+ * When the kernel completes, this rank's gathered buffer holds every rank's
+ * block of the same call. Every rank must make the same sequence of calls
+ * (same M and ldo) with its own shard; a rank that stops calling makes the
+ * others record QTTS_ERR_TIMEOUT after the wait limit instead of hanging.
+ * Every rank owns at least one output channel (N >= 1; M == 0 on every rank
+ * is a no-op). One signal pad / sync pair serves one stream. Other arguments as for
+ * qtts_w8a16_gemm (bf16/fp16 activations, 16-byte aligned rows, K % 16 == 0;
+ * AUTO or the split-K (M <= 16) and tcgen05 variants). */
+#define QTTS_ALLGATHER_MAX_WORLD 64
+QTTS_API int qtts_w8a16_gemm_allgather(const void* x, int64_t ldx, int x_dtype, const int8_t* w, int64_t ldw,
+                              const void* scale, int scale_dtype, const void* bias,
+                              void* const* peer_out, int64_t ldo, int64_t col_offset,
+                              uint32_t* const* peer_signal, uint32_t* sync, int rank, int world,
+                              int M, int N, int K, int variant, unsigned flags, void* stream);
+
 /* ---- load-time weight quantizers ------------------------------------------
  * Division by a constant (`amax / 127`, `/ 448`) follows torch on a CUDA
  * tensor, where `tensor / number` is evaluated as `tensor * fl32(1 / number)`:

@@ -381,15 +381,36 @@ uint64_t qtts_set_wait_limit_ns(uint64_t limit_ns) {
   return g_wait_limit_ns.exchange(limit_ns == 0 ? 2000000000ull : limit_ns);
 }
 
+// All-gather form of a call (qtts_w8a16_gemm_allgather); see csrc/allgather.cuh.
+struct AllGatherForm {
+  void* const* peer_out;
+  uint32_t* const* peer_sig;
+  uint32_t* sync;
+  int64_t col_offset;
+  int rank, world;
+};
+
+static void set_allgather(SkinnyArgs& sa, const AllGatherForm* ag) {
+  sa.peer_out = ag != nullptr ? ag->peer_out : nullptr;
+  sa.peer_sig = ag != nullptr ? ag->peer_sig : nullptr;
+  sa.sync = ag != nullptr ? ag->sync : nullptr;
+  sa.col_offset = ag != nullptr ? ag->col_offset : 0;
+  sa.rank = ag != nullptr ? ag->rank : 0;
+  sa.world = ag != nullptr ? ag->world : 1;
+}
+
 static int w8a16_dispatch(const void* x, int64_t gsx, int64_t ldx, int x_dtype, const int8_t* w, int64_t ldw,
                           const void* scale, int scale_dtype, const void* bias, void* out, int64_t gso,
                           int64_t ldo, int G, int M, int N, int K, const int64_t* group_index, int variant,
-                          unsigned flags, void* stream_ptr, int w_fmt = kWInt8) {
+                          unsigned flags, void* stream_ptr, int w_fmt = kWInt8,
+                          const AllGatherForm* ag = nullptr) {
   if (M < 0 || N < 0 || K < 0 || G < 1) return QTTS_ERR_SHAPE;
+  if (ag != nullptr && N == 0) return QTTS_ERR_SHAPE;  // every rank takes part in the exchange
   if (M == 0 || N == 0) return QTTS_OK;
-  if (x == nullptr || w == nullptr || scale == nullptr || out == nullptr) return QTTS_ERR_NULL;
+  if (x == nullptr || w == nullptr || scale == nullptr || (out == nullptr && ag == nullptr)) return QTTS_ERR_NULL;
   if (!is_float_dtype(x_dtype) || !is_float_dtype(scale_dtype)) return QTTS_ERR_DTYPE;
   if (ldx < K || ldw < K || ldo < N) return QTTS_ERR_SHAPE;
+  if (ag != nullptr && (ldo - ag->col_offset < N || G != 1 || group_index != nullptr)) return QTTS_ERR_SHAPE;
   if (G > 1 && group_index == nullptr && (gsx < static_cast<int64_t>(M) * ldx || gso < static_cast<int64_t>(M) * ldo))
     return QTTS_ERR_SHAPE;
   const int dev_ok = check_device();
@@ -414,7 +435,7 @@ static int w8a16_dispatch(const void* x, int64_t gsx, int64_t ldx, int x_dtype, 
     family = skinny_ok ? (M <= 16 ? 0x100 : 0x200) : 0;
     split = 0;
     rgroups = 0;
-    if (family == 0x100 && M <= 4 && w_fmt == kWInt8) {
+    if (family == 0x100 && M <= 4 && w_fmt == kWInt8 && ag == nullptr) {
       const SkinnyPlan sk = plan_skinny(M, N, K, zg_auto, 0, 0);
       int best = static_cast<int>(sk.grid.x * sk.grid.y * sk.grid.z);
       const int rows[5] = {6, 4, 3, 2, 1};
@@ -428,6 +449,10 @@ static int w8a16_dispatch(const void* x, int64_t gsx, int64_t ldx, int x_dtype, 
         }
       }
     }
+  }
+  if (ag != nullptr && (family == 0 || family == 0x300)) {
+    // The all-gather epilogue lives in the split-K and tcgen05 kernels.
+    return skinny_ok ? QTTS_ERR_VARIANT : QTTS_ERR_ALIGN;
   }
   if (variant == QTTS_VARIANT_GENERIC || family == 0) {
     if (variant != QTTS_VARIANT_AUTO && variant != QTTS_VARIANT_GENERIC) return QTTS_ERR_VARIANT;
@@ -469,6 +494,7 @@ static int w8a16_dispatch(const void* x, int64_t gsx, int64_t ldx, int x_dtype, 
     sa.m_chunks = plan.m_chunks;
     sa.group_index = group_index;
     sa.w_fmt = w_fmt;
+    set_allgather(sa, ag);
     sa.wait_ns = current_wait_limit_ns();
     sa.trace_slot = -1;
 #ifdef QTTS_TRACE
@@ -511,6 +537,7 @@ static int w8a16_dispatch(const void* x, int64_t gsx, int64_t ldx, int x_dtype, 
     sa.m_chunks = plan.m_chunks;
     sa.group_index = group_index;
     sa.w_fmt = w_fmt;
+    set_allgather(sa, ag);
     sa.wait_ns = current_wait_limit_ns();
     sa.trace_slot = -1;
 #ifdef QTTS_TRACE
@@ -556,6 +583,7 @@ static int w8a16_dispatch(const void* x, int64_t gsx, int64_t ldx, int x_dtype, 
     sa.m_chunks = plan.m_chunks;
     sa.group_index = group_index;
     sa.w_fmt = w_fmt;
+    set_allgather(sa, ag);
     sa.wait_ns = current_wait_limit_ns();
     sa.trace_slot = -1;
 #ifdef QTTS_TRACE
@@ -579,6 +607,18 @@ int qtts_fp8w_gemm(const void* x, int64_t ldx, int x_dtype, const uint8_t* w, in
                    unsigned flags, void* stream) {
   return w8a16_dispatch(x, 0, ldx, x_dtype, reinterpret_cast<const int8_t*>(w), ldw, scale, scale_dtype, bias, out,
                         0, ldo, 1, M, N, K, nullptr, variant, flags, stream, kWE4M3);
+}
+
+int qtts_w8a16_gemm_allgather(const void* x, int64_t ldx, int x_dtype, const int8_t* w, int64_t ldw,
+                              const void* scale, int scale_dtype, const void* bias, void* const* peer_out,
+                              int64_t ldo, int64_t col_offset, uint32_t* const* peer_signal, uint32_t* sync,
+                              int rank, int world, int M, int N, int K, int variant, unsigned flags, void* stream) {
+  if (peer_out == nullptr || peer_signal == nullptr || sync == nullptr) return QTTS_ERR_NULL;
+  if (world < 1 || world > QTTS_ALLGATHER_MAX_WORLD || rank < 0 || rank >= world || col_offset < 0)
+    return QTTS_ERR_SHAPE;
+  const AllGatherForm ag{peer_out, peer_signal, sync, col_offset, rank, world};
+  return w8a16_dispatch(x, 0, ldx, x_dtype, w, ldw, scale, scale_dtype, bias, nullptr, 0, ldo, 1, M, N, K, nullptr,
+                        variant, flags, stream, kWInt8, &ag);
 }
 
 int qtts_w8a16_grouped_gemm(const void* x, int64_t group_stride_x, int64_t ldx, int x_dtype, const int8_t* w,

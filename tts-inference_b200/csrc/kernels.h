@@ -37,6 +37,14 @@ struct SkinnyArgs {
   int trace_slot;  // timeline probe slot (-1: off); only read in -DQTTS_TRACE builds
   int64_t gsx_rows;  // group stride of x in rows (tcgen05 kernel: x is read through a tensor map)
   int w_fmt;         // kWInt8 or kWE4M3
+  // All-gather form (qtts_w8a16_gemm_allgather, csrc/allgather.cuh); peer_out
+  // is nullptr otherwise.
+  void* const* peer_out;      // [world] every rank's gathered output (device pointers)
+  uint32_t* const* peer_sig;  // [world] every rank's signal pad, uint32[2 * world] each
+  uint32_t* sync;             // this rank's uint32[2]: CTA arrivals, epoch of the last call
+  int64_t col_offset;         // gathered column of this rank's first output channel
+  int rank;
+  int world;
 };
 
 constexpr int kWInt8 = 0;  // int8 weights (W8A16)

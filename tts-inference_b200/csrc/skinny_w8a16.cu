@@ -42,6 +42,7 @@
 //     QTTS_ERR_TIMEOUT in the device status word, keeps the remote-store
 //     protocol (so no peer waits on it), skips its global stores and drains its
 //     own copies in flight before exiting.
+#include "allgather.cuh"
 #include "common.cuh"
 #include "kernels.h"
 
@@ -73,6 +74,7 @@ __global__ void __launch_bounds__(kSkThreads, 2)
   uint64_t* empty = full + a.stages;
   uint64_t* recv_bar = empty + a.stages;
   int* err_flag = reinterpret_cast<int*>(recv_bar + 2);
+  int* gate_flag = err_flag + 1;  // all-gather form: every rank is ready to receive
   float* red = reinterpret_cast<float*>(wbuf);  // [KG][BN][MB], reuses the ring after the loop
 
   const int tid = threadIdx.x;
@@ -108,6 +110,7 @@ __global__ void __launch_bounds__(kSkThreads, 2)
   __syncthreads();
   if (split > 1) cluster_arrive_relaxed();
   pdl_launch_dependents();
+  if (a.peer_out != nullptr && tid == 0) ag_prefetch_tables(a);
 
   // Device-indexed single group: the index may be produced by the preceding
   // kernel, so everything (including the weight stream) waits for it.
@@ -129,6 +132,8 @@ __global__ void __launch_bounds__(kSkThreads, 2)
   const XT* xg = static_cast<const XT*>(a.x) + goff_x + static_cast<int64_t>(m0) * a.ldx;
   XT* og = static_cast<XT*>(a.out) + goff_o + static_cast<int64_t>(m0) * a.ldo;
   const int mrows = min(MB, a.M - m0);
+  const int64_t pbase = static_cast<int64_t>(m0) * a.ldo + a.col_offset;  // all-gather form
+  uint32_t ag_ep = 0;  // all-gather form: epoch of this call (consumer threads)
 
   int n_issued = 0;  // meaningful in the producer lane only
   if (warp == kSkConsumerWarps) {
@@ -159,6 +164,7 @@ __global__ void __launch_bounds__(kSkThreads, 2)
     // ---------------- consumers ----------------
     pdl_wait();
     if (tid == 0) QTTS_TRACE_STAMP(2);
+    if (a.peer_out != nullptr) ag_ep = ag_epoch(a);  // consumed after the activation staging
 #ifdef QTTS_TRACE
     if (tid == 0 && a.trace_slot == 5 && blockIdx.x == 0 && blockIdx.y == 0 && blockIdx.z == 0) {
       g_trace_detail[3][0] = globaltimer_ns();
@@ -231,6 +237,8 @@ __global__ void __launch_bounds__(kSkThreads, 2)
       }
     }
     if (tid == 0) QTTS_TRACE_STAMP(3);
+    // Every CTA announces (no wait depends on another CTA of this grid having started).
+    if (a.peer_out != nullptr && tid == 0) ag_announce_ready(a, ag_ep);
 
     // 2) Main loop.
     const int rg = warp / KG;  // row group
@@ -349,7 +357,10 @@ __global__ void __launch_bounds__(kSkThreads, 2)
         }
         named_bar_sync(1, kSkConsumerWarps * 32);
       }
-      if (valid && !cta_err) {
+      bool store_ok = valid && !cta_err;
+      if (a.peer_out != nullptr)
+        store_ok = ag_gate_stores(a, ag_ep, gate_flag, 1, kSkConsumerWarps * 32, tid == 0) && store_ok;
+      if (store_ok) {
         for (int i = tid; i < BN * mrows; i += kSkConsumerWarps * 32) {
           const int m = i / BN;
           const int row = i - m * BN;
@@ -358,7 +369,7 @@ __global__ void __launch_bounds__(kSkThreads, 2)
             const int64_t ch = static_cast<int64_t>(group) * a.N + n;
             float r = red[row * MB + m] * load_as_float(a.scale, a.scale_dtype, ch);
             if (a.bias != nullptr) r += to_float(static_cast<const XT*>(a.bias)[ch]);
-            og[static_cast<int64_t>(m) * a.ldo + n] = from_float<XT>(r);
+            put_out(a, og, pbase, static_cast<int64_t>(m) * a.ldo + n, from_float<XT>(r));
           }
         }
       }
@@ -402,6 +413,7 @@ __global__ void __launch_bounds__(kSkThreads, 2)
         have = mbar_wait_bounded(recv_bar, 0, 4 * a.wait_ns);
       }
       if (tid == 0) QTTS_TRACE_STAMP(7);
+      if (a.peer_out != nullptr) have = ag_gate_stores(a, ag_ep, gate_flag, 1, kSkConsumerWarps * 32, tid == 0) && have;
       if (have && valid && !cta_err && mrows <= 2) {
         // One or two real batch rows: thread = (owned row, batch row).
         const int rbase = static_cast<int>(crank) * rpo;
@@ -415,7 +427,7 @@ __global__ void __launch_bounds__(kSkThreads, 2)
             const int64_t ch = static_cast<int64_t>(group) * a.N + n;
             r *= load_as_float(a.scale, a.scale_dtype, ch);
             if (a.bias != nullptr) r += to_float(static_cast<const XT*>(a.bias)[ch]);
-            og[static_cast<int64_t>(m) * a.ldo + n] = from_float<XT>(r);
+            put_out(a, og, pbase, static_cast<int64_t>(m) * a.ldo + n, from_float<XT>(r));
           }
         }
       } else if (have && valid && !cta_err) {
@@ -442,7 +454,7 @@ __global__ void __launch_bounds__(kSkThreads, 2)
 #pragma unroll
             for (int q = 0; q < 4; ++q) {
               const int m = 4 * mq + q;
-              if (m < mrows) og[static_cast<int64_t>(m) * a.ldo + n] = from_float<XT>(rv[q] * sc + bias);
+              if (m < mrows) put_out(a, og, pbase, static_cast<int64_t>(m) * a.ldo + n, from_float<XT>(rv[q] * sc + bias));
             }
           }
         }
@@ -464,6 +476,7 @@ __global__ void __launch_bounds__(kSkThreads, 2)
     cluster_arrive_relaxed();
     cluster_wait();
   }
+  if (a.peer_out != nullptr) ag_finish(a, ag_ep);
   // Error path: make sure no copy of ours is still landing in shared memory.
   if (warp == kSkConsumerWarps && lane == 0 && *reinterpret_cast<volatile int*>(err_flag) != 0) {
     for (int s = 0; s < a.stages && s < n_issued; ++s) {

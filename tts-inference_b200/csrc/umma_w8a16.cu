@@ -32,6 +32,7 @@
 // released.
 #include <type_traits>
 
+#include "allgather.cuh"
 #include "common.cuh"
 #include "kernels.h"
 
@@ -117,6 +118,7 @@ __global__ void __launch_bounds__(kUmThreads, 1)
   uint64_t* recv_bar = dfull + 1;
   uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(recv_bar + 1);
   int* err_flag = reinterpret_cast<int*>(tmem_slot + 1);
+  int* gate_flag = err_flag + 1;  // all-gather form: every rank is ready to receive
 
   const int tid = threadIdx.x;
   const int warp = tid >> 5;
@@ -162,6 +164,7 @@ __global__ void __launch_bounds__(kUmThreads, 1)
   const uint32_t tmem = *reinterpret_cast<volatile uint32_t*>(tmem_slot);
   if (split > 1) cluster_arrive_relaxed();
   pdl_launch_dependents();
+  if (a.peer_out != nullptr && tid == 0) ag_prefetch_tables(a);
 
   bool valid = true;
   if (a.group_index != nullptr) {
@@ -181,6 +184,8 @@ __global__ void __launch_bounds__(kUmThreads, 1)
   XT* og = static_cast<XT*>(a.out) + goff_o + static_cast<int64_t>(m0) * a.ldo;
   const int mrows = min(NB, a.M - m0);
   volatile int* verr = err_flag;
+  const int64_t pbase = static_cast<int64_t>(m0) * a.ldo + a.col_offset;  // all-gather form
+  uint32_t ag_ep = 0;  // all-gather form: epoch of this call (dequant threads)
 
   int w_issued = 0, x_issued = 0;
   if (warp == kUmProducerWarp) {
@@ -322,7 +327,10 @@ __global__ void __launch_bounds__(kUmThreads, 1)
     // Epilogue: accumulator -> registers -> output (or the row owners).
     pdl_wait();
     if (tid == 0) QTTS_TRACE_STAMP(5);
+    if (a.peer_out != nullptr) ag_ep = ag_epoch(a);  // the load overlaps the accumulator wait
     const bool dready = mbar_wait_bounded(dfull, 0, a.wait_ns);
+    // Every CTA announces (no wait depends on another CTA of this grid having started).
+    if (a.peer_out != nullptr && tid == 0) ag_announce_ready(a, ag_ep);
     if (!dready) {
       if (lane == 0) record_status(QTTS_ERR_TIMEOUT);
       *verr = 1;
@@ -338,14 +346,17 @@ __global__ void __launch_bounds__(kUmThreads, 1)
     for (int c = 0; c < HALF; ++c) v[c] = (n_iters > 0 && !cta_err) ? __uint_as_float(d[c]) : 0.f;
     if (split == 1) {
       const int n = n0 + row;
-      if (valid && !cta_err && n < a.N) {
+      bool store_ok = valid && !cta_err;
+      if (a.peer_out != nullptr)
+        store_ok = ag_gate_stores(a, ag_ep, gate_flag, 1, kUmDqWarps * 32, tid == 0) && store_ok;
+      if (store_ok && n < a.N) {
         const int64_t ch = static_cast<int64_t>(group) * a.N + n;
         const float sc = load_as_float(a.scale, a.scale_dtype, ch);
         const float bias = a.bias != nullptr ? to_float(static_cast<const XT*>(a.bias)[ch]) : 0.f;
 #pragma unroll
         for (int c = 0; c < HALF; ++c) {
           const int col = HALF * half + c;
-          if (col < mrows) og[static_cast<int64_t>(col) * a.ldo + n] = from_float<XT>(v[c] * sc + bias);
+          if (col < mrows) put_out(a, og, pbase, static_cast<int64_t>(col) * a.ldo + n, from_float<XT>(v[c] * sc + bias));
         }
       }
     } else {
@@ -375,6 +386,7 @@ __global__ void __launch_bounds__(kUmThreads, 1)
         if (tid == 0) record_status(QTTS_ERR_TIMEOUT);
         have = mbar_wait_bounded(recv_bar, 0, 4 * a.wait_ns);  // peers always send
       }
+      if (a.peer_out != nullptr) have = ag_gate_stores(a, ag_ep, gate_flag, 1, kUmDqWarps * 32, tid == 0) && have;
       if (have && valid && !cta_err) {
         // Thread = (owned row, 4 batch columns): one 16-byte load per peer.
         const int rbase = static_cast<int>(crank) * rpo;
@@ -399,7 +411,7 @@ __global__ void __launch_bounds__(kUmThreads, 1)
 #pragma unroll
             for (int q = 0; q < 4; ++q) {
               const int m = 4 * mq + q;
-              if (m < mrows) og[static_cast<int64_t>(m) * a.ldo + n] = from_float<XT>(rv[q] * sc + bias);
+              if (m < mrows) put_out(a, og, pbase, static_cast<int64_t>(m) * a.ldo + n, from_float<XT>(rv[q] * sc + bias));
             }
           }
         }
@@ -420,6 +432,7 @@ __global__ void __launch_bounds__(kUmThreads, 1)
   // registers need no source kept alive, and each CTA waited for everything
   // sent to it.
   if (split > 1 && (warp == kUmProducerWarp || warp == kUmMmaWarp)) cluster_wait();
+  if (a.peer_out != nullptr) ag_finish(a, ag_ep);
   if (warp == kUmProducerWarp && lane == 0 && *verr != 0) {
     // Drain our own copies in flight (weights and activations).
     for (int s = 0; s < WS && s < w_issued; ++s) {

@@ -71,6 +71,11 @@ SIGNATURES: dict[str, tuple[object, list[object]]] = {
         [_c_vp, _c_i64, _c_int, _c_vp, _c_i64, _c_vp, _c_int, _c_vp, _c_vp, _c_i64, _c_int, _c_int, _c_int,
          _c_int, _c_uint, _c_vp],
     ),
+    "qtts_w8a16_gemm_allgather": (
+        _c_int,
+        [_c_vp, _c_i64, _c_int, _c_vp, _c_i64, _c_vp, _c_int, _c_vp, _c_vp, _c_i64, _c_i64, _c_vp, _c_vp, _c_int,
+         _c_int, _c_int, _c_int, _c_int, _c_int, _c_uint, _c_vp],
+    ),
     "qtts_w8a16_grouped_gemm": (
         _c_int,
         [_c_vp, _c_i64, _c_i64, _c_int, _c_vp, _c_i64, _c_vp, _c_int, _c_vp, _c_vp, _c_i64, _c_i64, _c_int, _c_int,

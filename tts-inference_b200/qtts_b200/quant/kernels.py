@@ -133,6 +133,61 @@ def _weight_only_gemm(x, weight, scale, bias, variant, out, entry: str) -> torch
     return out.reshape(*shape[:-1], n)
 
 
+def w8_gemm_allgather(
+    x: torch.Tensor,
+    weight: torch.Tensor,
+    scale: torch.Tensor,
+    bias: torch.Tensor | None,
+    *,
+    peer_out: torch.Tensor,
+    ldo: int,
+    col_offset: int,
+    peer_signal: torch.Tensor,
+    sync: torch.Tensor,
+    rank: int,
+    world: int,
+    variant: int = nat.VARIANT_AUTO,
+) -> None:
+    """This rank's block of an N-sharded W8A16 GEMM, stored by the kernel into every
+    rank's gathered output (``qtts_w8a16_gemm_allgather``).
+
+    ``peer_out`` / ``peer_signal``: int64 CUDA tensors of ``world`` device addresses
+    (each rank's gathered buffer and signal pad, this rank's own at ``rank``);
+    ``sync``: this rank's int32 [2] CUDA tensor. The gathered buffers hold rows of
+    ``ldo`` elements of x's dtype; this rank's block lands at columns
+    ``[col_offset, col_offset + N)``.
+    """
+    ok, reason = nat.available()
+    if not ok:
+        raise RuntimeError(reason)
+    k = x.shape[-1]
+    n = weight.shape[0]
+    if x.dim() != 2 or weight.dim() != 2 or weight.shape[1] != k or scale.numel() != n:
+        raise ValueError(f"x {tuple(x.shape)}, weight {tuple(weight.shape)}, scale {scale.numel()} do not agree")
+    for name, t, dt, numel in (("peer_out", peer_out, torch.int64, world), ("peer_signal", peer_signal, torch.int64,
+                                                                             world), ("sync", sync, torch.int32, 2)):
+        if t.dtype != dt or t.numel() != numel or not t.is_contiguous():
+            raise ValueError(f"{name} must be a contiguous {dt} tensor of {numel} elements")
+    device = _require_cuda(x, weight, scale, bias, peer_out, peer_signal, sync)
+    if x.stride(1) != 1:
+        x = x.contiguous()
+    if weight.stride(1) != 1:
+        weight = weight.contiguous()
+    scale = scale.reshape(-1).contiguous()
+    if bias is not None:
+        bias = bias.reshape(-1).to(x.dtype).contiguous()
+    rows = x.shape[0]
+    code = nat.lib().qtts_w8a16_gemm_allgather(
+        x.data_ptr(), x.stride(0) if rows > 1 else k, nat.dtype_code(x.dtype),
+        weight.data_ptr(), weight.stride(0),
+        scale.data_ptr(), nat.dtype_code(scale.dtype),
+        bias.data_ptr() if bias is not None else None,
+        peer_out.data_ptr(), ldo, col_offset, peer_signal.data_ptr(), sync.data_ptr(),
+        rank, world, rows, n, k, variant, _flags(), nat.stream_ptr(device),
+    )
+    nat.check(code, "qtts_w8a16_gemm_allgather")
+
+
 def w8_grouped_gemm(
     x: torch.Tensor,
     weight: torch.Tensor,
