@@ -452,6 +452,7 @@ def sharded_sweep(world: int, rank: int, device, seed: int) -> dict:
     timed in a CUDA graph, the all-gather of its [M, ceil(N/g)] block in an eager loop (no
     collective is captured into a graph), each as the max over ranks of CUDA-event time;
     GEMM + all-gather is their sum."""
+    from qtts_b200 import _native as nat
     from qtts_b200.sharded import FusedAllGatherW8Linear, ShardedW8Linear, shard_rows
 
     gen = torch.Generator(device=device)
@@ -486,6 +487,7 @@ def sharded_sweep(world: int, rank: int, device, seed: int) -> dict:
         torch.cuda.synchronize()
         return max_over_ranks(world, e0.elapsed_time(e1) / reps) * 1e3 / SHARD_CALLS
 
+    fused_ok, fused_error = True, None
     for k, n, m in SHARD_POINTS:
         start, stop = shard_rows(n, world, rank)
         rows = stop - start
@@ -517,16 +519,25 @@ def sharded_sweep(world: int, rank: int, device, seed: int) -> dict:
 
         gemm_us = time_graph(gemm_only)
         gather_us = time_eager(gather_only) if world > 1 else 0.0  # one GPU: the block is the output
-        fused_us = time_graph(fused_calls)
+        if fused_ok:
+            # One checked call first: a failed exchange (bounded waits, recorded in the
+            # device status) must not turn every timed call into a wait-limit expiry.
+            nat.device_status(reset=True)
+            fused[0](x)
+            torch.cuda.synchronize()
+            fused_ok = max_over_ranks(world, float(nat.device_status())) == 0.0
+            if not fused_ok:
+                fused_error = f"device status after the first fused call at K={k} N={n} M={m}"
+        fused_us = time_graph(fused_calls) if fused_ok else None
         total_us = gemm_us + gather_us
         res[f"K{k}_N{n}_M{m}"] = {
             "gemm_us": round(gemm_us, 3),
             "allgather_us": round(gather_us, 3),
             "gemm_allgather_us": round(total_us, 3),
-            "fused_gemm_allgather_us": round(fused_us, 3),
-            "fused_speedup": round(total_us / fused_us, 3),
+            "fused_gemm_allgather_us": round(fused_us, 3) if fused_us else None,
+            "fused_speedup": round(total_us / fused_us, 3) if fused_us else None,
             "agg_weight_gbs": round(n * k / (total_us * 1e-6) / 1e9, 1),
-            "agg_weight_gbs_fused": round(n * k / (fused_us * 1e-6) / 1e9, 1),
+            "agg_weight_gbs_fused": round(n * k / (fused_us * 1e-6) / 1e9, 1) if fused_us else None,
             "agg_weight_gbs_gemm_only": round(n * k / (gemm_us * 1e-6) / 1e9, 1),
             "per_gpu_frac_of_hbm": round(rows * k / (gemm_us * 1e-6) / 1e9 / pk["hbm_gbs"], 4),
         }
@@ -539,6 +550,7 @@ def sharded_sweep(world: int, rank: int, device, seed: int) -> dict:
         "scaling": "strong",
         "n_gpus": world,
         "allgather_timed": "eager loop, CUDA events" if world > 1 else "single GPU: no exchange",
+        "fused_error": fused_error,
         "per_point": res,
     }
 
@@ -757,6 +769,9 @@ def run_gpu_arm(args) -> None:
         del bf16_pools
         torch.cuda.empty_cache()
 
+    torch.cuda.synchronize()
+    status_sweep = nat.device_status()  # before the sections (the sharded one resets the word)
+
     # ---- config 3 (fp8) and config 5 (N-sharded GEMM + all-gather), outside the timed region
     fp8 = fp8_sweep(device, args.seed) if args.fp8 and rank == 0 else None
     fp8w = fp8w_sweep(device, args.seed) if args.fp8w and rank == 0 else None
@@ -790,7 +805,7 @@ def run_gpu_arm(args) -> None:
     e2e_ms = max_over_ranks(world, e0.elapsed_time(e1))
     e2e_value = bytes_per_step * args.steps * world / (e2e_ms * 1e-3) / 1e9
 
-    status = nat.device_status()
+    status = status_sweep or nat.device_status()
     cpu = None
     if rank == 0 and world == 1 and not args.no_cpu_baseline:
         cpu = cpu_port_sample(args.cpu_seconds)
