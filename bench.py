@@ -635,9 +635,10 @@ def talker_frames(seed: int, batch: int = 8) -> dict:
 
 
 def auto_kernel(m: int, n: int, k: int) -> str:
-    """The kernel the library's automatic choice launches (the rule in capi.cu)."""
-    umma_mid = m > 8 and -(-n // 128) * 4 <= 148 and k <= 4096
-    return "skinny_w8a16_kernel" if (m <= 16 and not umma_mid) else "umma_w8a16_kernel"
+    """The kernel the library's automatic choice launches (asked of the library's planner)."""
+    from qtts_b200 import _native as nat
+
+    return nat.plan(m, n, k)["kernel"]
 
 
 def run_gpu_arm(args) -> None:

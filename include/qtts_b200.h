@@ -155,6 +155,15 @@ QTTS_API int qtts_w8a16_grouped_gemm(const void* x, int64_t group_stride_x, int6
                             const int64_t* group_index,
                             int variant, unsigned flags, void* stream);
 
+/* The kernel qtts_w8a16_gemm would launch for int8 weights and aligned bf16 or
+ * fp16 activations (G groups of N rows, as qtts_w8a16_grouped_gemm without a
+ * device index): *kernel 0 = SIMT (QTTS_VARIANT_GENERIC), 1 = split-K
+ * streaming (QTTS_VARIANT_SKINNY), 2 = tcgen05 (QTTS_VARIANT_UMMA),
+ * 3 = whole-K streaming (QTTS_VARIANT_STREAM); its K split, weight rows per
+ * CTA and grid size. Host-only: needs no GPU. */
+QTTS_API int qtts_w8a16_plan(int M, int N, int K, int G, int variant, int* kernel, int* split, int* row_tile,
+                             int* ctas);
+
 /* fp8 weight-only GEMM (no counterpart in the reference, which leaves
  * Fp8WeightOnlyMethod unimplemented, qtts/quant/fp8.py:92-122): the W8A16
  * contract with e4m3 weights,

@@ -1,0 +1,60 @@
+"""The library's kernel choice (qtts_w8a16_plan, host-only) on the talker and code-predictor shapes.
+
+Pins the rule the B200 measurements chose: up to 16 rows the split-K streaming
+kernel with the most CTAs that run two per SM (ties to the larger row tile,
+every CTA of a split owning part of K); up to 4 rows of int8 the whole-K
+streaming kernel where it reaches more CTAs; past 16 rows the tcgen05 kernel.
+"""
+
+from __future__ import annotations
+
+import pytest
+
+from qtts_b200 import _native as nat
+
+
+@pytest.fixture(scope="module", autouse=True)
+def _lib():
+    nat.lib()  # raises if the library cannot be built or loaded
+
+
+@pytest.mark.parametrize(
+    "n,k,m,kernel,split,rows,ctas",
+    [
+        (4096, 2048, 1, "skinny_w8a16_kernel", 8, 128, 256),  # talker qkv
+        (4096, 2048, 16, "skinny_w8a16_kernel", 8, 128, 256),
+        (2048, 2048, 8, "skinny_w8a16_kernel", 8, 64, 256),  # o_proj
+        (12288, 2048, 1, "stream_w8a16_kernel", 1, 48, 256),  # gate_up, few rows
+        (12288, 2048, 8, "skinny_w8a16_kernel", 2, 128, 192),
+        (2048, 6144, 4, "skinny_w8a16_kernel", 8, 64, 256),  # down_proj
+        (4096, 2048, 32, "umma_w8a16_kernel", 4, 128, 128),
+        (12288, 2048, 64, "umma_w8a16_kernel", 1, 128, 96),
+        # code predictor down: every 256-CTA plan would leave a split CTA without K
+        (1024, 3072, 8, "skinny_w8a16_kernel", 2, 16, 128),
+    ],
+)
+def test_auto_plans(n, k, m, kernel, split, rows, ctas):
+    assert nat.plan(m, n, k) == {"kernel": kernel, "split": split, "row_tile": rows, "ctas": ctas}
+
+
+def test_grouped_heads_and_forced_variants():
+    assert nat.plan(8, 2048, 1024, groups=15) == {"kernel": "skinny_w8a16_kernel", "split": 1, "row_tile": 128,
+                                                  "ctas": 240}
+    assert nat.plan(8, 2048, 2048, variant=nat.variant_skinny(2, 4))["ctas"] == 32 * 2
+    assert nat.plan(40, 2048, 2048, variant=nat.variant_umma(2))["split"] == 2
+    assert nat.plan(2, 12288, 2048, variant=nat.variant_stream(6))["ctas"] == 128
+    assert nat.plan(3, 80, 272, variant=nat.VARIANT_GENERIC)["kernel"] == "generic_w8a16_kernel"
+    with pytest.raises(RuntimeError):
+        nat.plan(32, 2048, 2048, variant=nat.variant_stream(0))  # the whole-K kernel takes M <= 16
+    with pytest.raises(RuntimeError):
+        nat.plan(1, 2048, 100)  # K % 16 != 0
+
+
+def test_every_split_owns_part_of_k():
+    for n, k in [(1024, 3072), (2048, 6144), (4096, 2048), (6144, 1024), (3072, 2048), (80, 272)]:
+        for m in (1, 2, 4, 8, 9, 16):
+            p = nat.plan(m, n, k)
+            if p["kernel"] == "skinny_w8a16_kernel" and p["split"] > 1:
+                sw = 128 * (128 // p["row_tile"])  # k per stage: 8 warps / (row tile / 16) k groups
+                kpc = -(-(-(-k // p["split"])) // sw) * sw
+                assert (p["split"] - 1) * kpc < k, (n, k, m, p)

@@ -399,6 +399,35 @@ static void set_allgather(SkinnyArgs& sa, const AllGatherForm* ag) {
   sa.world = ag != nullptr ? ag->world : 1;
 }
 
+// AUTO's kernel for aligned 16-bit activations: 0x100 (split-K streaming), 0x200
+// (tcgen05) or 0x300 (whole-K streaming, with its row groups in *rgroups).
+// Up to 16 rows: the split-K streaming kernel with its planner's tile and split
+// (up to two CTAs per SM). Past 16: the tcgen05 kernel, whose per-instruction
+// cost does not grow with M. Up to 4 rows of int8, the whole-K streaming kernel
+// where its row tiles (16..96 rows) reach more CTAs within two per SM than the
+// split-K plan can (gate_up 12288 x 2048 at M = 1: 256 CTAs, 7.2 us, vs 192
+// CTAs, 9.3 us, measured on B200).
+static int auto_family(int M, int N, int K, int zg, int w_fmt, bool allgather, int* rgroups) {
+  *rgroups = 0;
+  if (M > 16) return 0x200;
+  int family = 0x100;
+  if (M <= 4 && w_fmt == kWInt8 && !allgather) {
+    const SkinnyPlan sk = plan_skinny(M, N, K, zg, 0, 0);
+    int best = static_cast<int>(sk.grid.x * sk.grid.y * sk.grid.z);
+    const int rows[5] = {6, 4, 3, 2, 1};
+    for (int i = 0; i < 5; ++i) {
+      const SkinnyPlan st = plan_stream(M, N, K, zg, rows[i]);
+      const int c = static_cast<int>(st.grid.x * st.grid.y * st.grid.z);
+      if (c <= kCtaSlots && c > best && st.smem <= kMaxDynSmem) {
+        best = c;
+        family = 0x300;
+        *rgroups = rows[i];
+      }
+    }
+  }
+  return family;
+}
+
 static int w8a16_dispatch(const void* x, int64_t gsx, int64_t ldx, int x_dtype, const int8_t* w, int64_t ldw,
                           const void* scale, int scale_dtype, const void* bias, void* out, int64_t gso,
                           int64_t ldo, int G, int M, int N, int K, const int64_t* group_index, int variant,
@@ -425,30 +454,8 @@ static int w8a16_dispatch(const void* x, int64_t gsx, int64_t ldx, int x_dtype, 
   int split = variant & 0xF;
   int rgroups = (variant >> 4) & 0xF;
   if (variant == QTTS_VARIANT_AUTO) {
-    // Up to 16 rows: the split-K streaming kernel with its planner's tile and
-    // split (up to two CTAs per SM). Past 16: the tcgen05 kernel, whose
-    // per-instruction cost does not grow with M. Up to 4 rows of int8, the
-    // whole-K streaming kernel where its row tiles (16..96 rows) reach more
-    // CTAs within two per SM than the split-K plan can (gate_up 12288 x 2048
-    // at M = 1: 256 CTAs, 7.2 us, vs 192 CTAs, 9.3 us, measured on B200).
-    const int zg_auto = group_index != nullptr ? 1 : G;
-    family = skinny_ok ? (M <= 16 ? 0x100 : 0x200) : 0;
+    family = skinny_ok ? auto_family(M, N, K, group_index != nullptr ? 1 : G, w_fmt, ag != nullptr, &rgroups) : 0;
     split = 0;
-    rgroups = 0;
-    if (family == 0x100 && M <= 4 && w_fmt == kWInt8 && ag == nullptr) {
-      const SkinnyPlan sk = plan_skinny(M, N, K, zg_auto, 0, 0);
-      int best = static_cast<int>(sk.grid.x * sk.grid.y * sk.grid.z);
-      const int rows[5] = {6, 4, 3, 2, 1};
-      for (int i = 0; i < 5; ++i) {
-        const SkinnyPlan st = plan_stream(M, N, K, zg_auto, rows[i]);
-        const int c = static_cast<int>(st.grid.x * st.grid.y * st.grid.z);
-        if (c <= kCtaSlots && c > best && st.smem <= kMaxDynSmem) {
-          best = c;
-          family = 0x300;
-          rgroups = rows[i];
-        }
-      }
-    }
   }
   if (ag != nullptr && (family == 0 || family == 0x300)) {
     // The all-gather epilogue lives in the split-K and tcgen05 kernels.
@@ -607,6 +614,40 @@ int qtts_fp8w_gemm(const void* x, int64_t ldx, int x_dtype, const uint8_t* w, in
                    unsigned flags, void* stream) {
   return w8a16_dispatch(x, 0, ldx, x_dtype, reinterpret_cast<const int8_t*>(w), ldw, scale, scale_dtype, bias, out,
                         0, ldo, 1, M, N, K, nullptr, variant, flags, stream, kWE4M3);
+}
+
+int qtts_w8a16_plan(int M, int N, int K, int G, int variant, int* kernel, int* split, int* row_tile, int* ctas) {
+  if (M < 1 || N < 1 || K < 16 || K % 16 != 0 || G < 1) return QTTS_ERR_SHAPE;
+  if (kernel == nullptr || split == nullptr || row_tile == nullptr || ctas == nullptr) return QTTS_ERR_NULL;
+  int family = variant & 0xF00, s = variant & 0xF, r = (variant >> 4) & 0xF;
+  if (variant == QTTS_VARIANT_AUTO) {
+    family = auto_family(M, N, K, G, kWInt8, false, &r);
+    s = 0;
+  }
+  SkinnyPlan p{};
+  if (variant == QTTS_VARIANT_GENERIC) {
+    *kernel = 0;
+    *split = 1;
+    *row_tile = 8;
+    *ctas = ((N + 7) / 8) * ((M + 7) / 8) * G;
+    return QTTS_OK;
+  } else if (family == 0x100) {
+    p = plan_skinny(M, N, K, G, s, r);
+    *kernel = 1;
+  } else if (family == 0x200) {
+    p = plan_umma(M, N, K, G, s);
+    *kernel = 2;
+  } else if (family == 0x300) {
+    if (M > 16 || !(r == 0 || stream_rows_ok(r))) return QTTS_ERR_VARIANT;
+    p = plan_stream(M, N, K, G, r);
+    *kernel = 3;
+  } else {
+    return QTTS_ERR_VARIANT;
+  }
+  *split = p.split;
+  *row_tile = 16 * p.r;
+  *ctas = static_cast<int>(p.grid.x * p.grid.y * p.grid.z);
+  return QTTS_OK;
 }
 
 int qtts_w8a16_gemm_allgather(const void* x, int64_t ldx, int x_dtype, const int8_t* w, int64_t ldw,

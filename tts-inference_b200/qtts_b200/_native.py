@@ -71,6 +71,7 @@ SIGNATURES: dict[str, tuple[object, list[object]]] = {
         [_c_vp, _c_i64, _c_int, _c_vp, _c_i64, _c_vp, _c_int, _c_vp, _c_vp, _c_i64, _c_int, _c_int, _c_int,
          _c_int, _c_uint, _c_vp],
     ),
+    "qtts_w8a16_plan": (_c_int, [_c_int, _c_int, _c_int, _c_int, _c_int, _c_vp, _c_vp, _c_vp, _c_vp]),
     "qtts_w8a16_gemm_allgather": (
         _c_int,
         [_c_vp, _c_i64, _c_int, _c_vp, _c_i64, _c_vp, _c_int, _c_vp, _c_vp, _c_i64, _c_i64, _c_vp, _c_vp, _c_int,
@@ -180,3 +181,14 @@ def device_status(reset: bool = False) -> int:
 
 def set_wait_limit_ns(limit_ns: int) -> int:
     return int(_load().qtts_set_wait_limit_ns(limit_ns))
+
+
+KERNEL_NAMES = {0: "generic_w8a16_kernel", 1: "skinny_w8a16_kernel", 2: "umma_w8a16_kernel", 3: "stream_w8a16_kernel"}
+
+
+def plan(m: int, n: int, k: int, groups: int = 1, variant: int = VARIANT_AUTO) -> dict:
+    """The kernel and launch shape qtts_w8a16_gemm picks (host-only; no GPU needed)."""
+    out = [ctypes.c_int() for _ in range(4)]
+    check(lib().qtts_w8a16_plan(m, n, k, groups, variant, *[ctypes.byref(v) for v in out]), "qtts_w8a16_plan")
+    kern, split, rows, ctas = (v.value for v in out)
+    return {"kernel": KERNEL_NAMES[kern], "split": split, "row_tile": rows, "ctas": ctas}
