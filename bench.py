@@ -52,10 +52,10 @@ CALLS_PER_GRAPH = 224  # multiple of every pool size below
 REPLAYS_PER_POINT = 9  # 9 x 224 = 2016 calls per point (--replays)
 POOL_MIN_BYTES = 256 << 20
 METRIC = "int8 W8A16 GEMM HBM GB/s (talker linear sweep, M=1..64)"
-# DRAM bytes per launch of the dominant kernel (skinny_w8a16_kernel, gate_up
-# M=1) from one `ncu --set full` capture (profiles/skinny_w8a16_gate_up_m1.md):
+# DRAM bytes per launch of the dominant kernel (skinny_w8a16_kernel, down_proj
+# M=1) from one `ncu --set full` capture (profiles/skinny_w8a16_down_proj_m1.md):
 # dram__bytes_read.sum + dram__bytes_write.sum, against its algorithmic bytes.
-NCU_TRAFFIC = {"case": "gate_up 12288x2048, M=1", "bytes_per_launch": 25235200, "algorithmic_bytes": 25219072}
+NCU_TRAFFIC = {"case": "down_proj 2048x6144, M=1", "bytes_per_launch": 12666624, "algorithmic_bytes": 12603392}
 
 
 def algo_bytes(n: int, k: int, m: int) -> int:
