@@ -100,11 +100,12 @@ __device__ __forceinline__ bool ag_gate_stores(const SkinnyArgs& a, uint32_t epo
   return *reinterpret_cast<volatile int*>(flag_smem) != 0;
 }
 
-// One output element: into the local output, or in the all-gather form into
-// every rank's gathered buffer (`pbase` + `off` elements from its base).
-template <typename XT>
+// One output element: into the local output, or in the all-gather form (AG,
+// a template parameter of the kernels so the plain form carries none of it)
+// into every rank's gathered buffer (`pbase` + `off` elements from its base).
+template <bool AG, typename XT>
 __device__ __forceinline__ void put_out(const SkinnyArgs& a, XT* og, int64_t pbase, int64_t off, XT v) {
-  if (a.peer_out == nullptr) {
+  if (!AG) {
     og[off] = v;
     return;
   }

@@ -250,6 +250,7 @@ __device__ __forceinline__ uint4 lds128(uint32_t addr) {
   return v;
 }
 
+
 // ---- int8 -> 16-bit float dequantization in registers ----------------------------
 //
 // A 32-bit word holds four int8 weights b0..b3 (little endian). Each routine

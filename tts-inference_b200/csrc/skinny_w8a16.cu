@@ -54,7 +54,7 @@ constexpr int kSkThreads = (kSkConsumerWarps + 1) * 32;
 
 __device__ __forceinline__ float pow2f(int e) { return __int_as_float((e + 127) << 23); }
 
-template <int MT, int R, typename XT, bool E4M3 = false>
+template <int MT, int R, typename XT, bool E4M3 = false, bool AG = false>
 __global__ void __launch_bounds__(kSkThreads, 2)
     skinny_w8a16_kernel(const __grid_constant__ CUtensorMap wmap, const SkinnyArgs a) {
   constexpr int MB = MT * 8;       // batch rows per CTA (MMA N dimension)
@@ -110,7 +110,7 @@ __global__ void __launch_bounds__(kSkThreads, 2)
   __syncthreads();
   if (split > 1) cluster_arrive_relaxed();
   pdl_launch_dependents();
-  if (a.peer_out != nullptr && tid == 0) ag_prefetch_tables(a);
+  if (AG && tid == 0) ag_prefetch_tables(a);
 
   // Device-indexed single group: the index may be produced by the preceding
   // kernel, so everything (including the weight stream) waits for it.
@@ -164,7 +164,7 @@ __global__ void __launch_bounds__(kSkThreads, 2)
     // ---------------- consumers ----------------
     pdl_wait();
     if (tid == 0) QTTS_TRACE_STAMP(2);
-    if (a.peer_out != nullptr) ag_ep = ag_epoch(a);  // consumed after the activation staging
+    if (AG) ag_ep = ag_epoch(a);  // consumed after the activation staging
 #ifdef QTTS_TRACE
     if (tid == 0 && a.trace_slot == 5 && blockIdx.x == 0 && blockIdx.y == 0 && blockIdx.z == 0) {
       g_trace_detail[3][0] = globaltimer_ns();
@@ -238,7 +238,7 @@ __global__ void __launch_bounds__(kSkThreads, 2)
     }
     if (tid == 0) QTTS_TRACE_STAMP(3);
     // Every CTA announces (no wait depends on another CTA of this grid having started).
-    if (a.peer_out != nullptr && tid == 0) ag_announce_ready(a, ag_ep);
+    if (AG && tid == 0) ag_announce_ready(a, ag_ep);
 
     // 2) Main loop.
     const int rg = warp / KG;  // row group
@@ -280,8 +280,6 @@ __global__ void __launch_bounds__(kSkThreads, 2)
       const uint4 wb0 = lds128(sb + offB0);
       const uint4 wa1 = lds128(sb + offA1);
       const uint4 wb1 = lds128(sb + offB1);
-      __syncwarp();
-      if (lane == 0) mbar_arrive(&empty[s]);
 
       uint32_t A[2][4][4];
       WDequant<__half, E4M3>::run(wa0.x, A[0][0][0], A[0][0][2]);
@@ -300,6 +298,11 @@ __global__ void __launch_bounds__(kSkThreads, 2)
       WDequant<__half, E4M3>::run(wb1.z, A[1][2][1], A[1][2][3]);
       WDequant<__half, E4M3>::run(wa1.w, A[1][3][0], A[1][3][2]);
       WDequant<__half, E4M3>::run(wb1.w, A[1][3][1], A[1][3][3]);
+      // The stage goes back to the producer only after every loaded word has
+      // been consumed: the conversions above wait for the shared loads, so a
+      // TMA refill cannot overtake a read of the stage.
+      __syncwarp();
+      if (lane == 0) mbar_arrive(&empty[s]);
 
       const uint32_t xk = xbase + it * SW * 2;
 #pragma unroll
@@ -358,8 +361,7 @@ __global__ void __launch_bounds__(kSkThreads, 2)
         named_bar_sync(1, kSkConsumerWarps * 32);
       }
       bool store_ok = valid && !cta_err;
-      if (a.peer_out != nullptr)
-        store_ok = ag_gate_stores(a, ag_ep, gate_flag, 1, kSkConsumerWarps * 32, tid == 0) && store_ok;
+      if (AG) store_ok = ag_gate_stores(a, ag_ep, gate_flag, 1, kSkConsumerWarps * 32, tid == 0) && store_ok;
       if (store_ok) {
         for (int i = tid; i < BN * mrows; i += kSkConsumerWarps * 32) {
           const int m = i / BN;
@@ -369,7 +371,7 @@ __global__ void __launch_bounds__(kSkThreads, 2)
             const int64_t ch = static_cast<int64_t>(group) * a.N + n;
             float r = red[row * MB + m] * load_as_float(a.scale, a.scale_dtype, ch);
             if (a.bias != nullptr) r += to_float(static_cast<const XT*>(a.bias)[ch]);
-            put_out(a, og, pbase, static_cast<int64_t>(m) * a.ldo + n, from_float<XT>(r));
+            put_out<AG>(a, og, pbase, static_cast<int64_t>(m) * a.ldo + n, from_float<XT>(r));
           }
         }
       }
@@ -413,7 +415,7 @@ __global__ void __launch_bounds__(kSkThreads, 2)
         have = mbar_wait_bounded(recv_bar, 0, 4 * a.wait_ns);
       }
       if (tid == 0) QTTS_TRACE_STAMP(7);
-      if (a.peer_out != nullptr) have = ag_gate_stores(a, ag_ep, gate_flag, 1, kSkConsumerWarps * 32, tid == 0) && have;
+      if (AG) have = ag_gate_stores(a, ag_ep, gate_flag, 1, kSkConsumerWarps * 32, tid == 0) && have;
       if (have && valid && !cta_err && mrows <= 2) {
         // One or two real batch rows: thread = (owned row, batch row).
         const int rbase = static_cast<int>(crank) * rpo;
@@ -427,7 +429,7 @@ __global__ void __launch_bounds__(kSkThreads, 2)
             const int64_t ch = static_cast<int64_t>(group) * a.N + n;
             r *= load_as_float(a.scale, a.scale_dtype, ch);
             if (a.bias != nullptr) r += to_float(static_cast<const XT*>(a.bias)[ch]);
-            put_out(a, og, pbase, static_cast<int64_t>(m) * a.ldo + n, from_float<XT>(r));
+            put_out<AG>(a, og, pbase, static_cast<int64_t>(m) * a.ldo + n, from_float<XT>(r));
           }
         }
       } else if (have && valid && !cta_err) {
@@ -454,7 +456,7 @@ __global__ void __launch_bounds__(kSkThreads, 2)
 #pragma unroll
             for (int q = 0; q < 4; ++q) {
               const int m = 4 * mq + q;
-              if (m < mrows) put_out(a, og, pbase, static_cast<int64_t>(m) * a.ldo + n, from_float<XT>(rv[q] * sc + bias));
+              if (m < mrows) put_out<AG>(a, og, pbase, static_cast<int64_t>(m) * a.ldo + n, from_float<XT>(rv[q] * sc + bias));
             }
           }
         }
@@ -476,7 +478,7 @@ __global__ void __launch_bounds__(kSkThreads, 2)
     cluster_arrive_relaxed();
     cluster_wait();
   }
-  if (a.peer_out != nullptr) ag_finish(a, ag_ep);
+  if (AG) ag_finish(a, ag_ep);
   // Error path: make sure no copy of ours is still landing in shared memory.
   if (warp == kSkConsumerWarps && lane == 0 && *reinterpret_cast<volatile int*>(err_flag) != 0) {
     for (int s = 0; s < a.stages && s < n_issued; ++s) {
@@ -491,10 +493,10 @@ __global__ void __launch_bounds__(kSkThreads, 2)
 
 namespace {
 
-template <int MT, int R, typename XT, bool E4M3>
+template <int MT, int R, typename XT, bool E4M3, bool AG>
 int launch_skinny_t(const CUtensorMap& map, const SkinnyArgs& args, dim3 grid, int split, size_t smem,
                     bool pdl, cudaStream_t stream) {
-  auto kern = skinny_w8a16_kernel<MT, R, XT, E4M3>;
+  auto kern = skinny_w8a16_kernel<MT, R, XT, E4M3, AG>;
   static int configured[64] = {0};
   int dev = 0;
   cudaGetDevice(&dev);
@@ -529,24 +531,31 @@ int launch_skinny_t(const CUtensorMap& map, const SkinnyArgs& args, dim3 grid, i
   return e == cudaSuccess ? QTTS_OK : QTTS_ERR_LAUNCH;
 }
 
-template <int MT, typename XT, bool E4M3>
+template <int MT, typename XT, bool E4M3, bool AG = false>
 int launch_skinny_r(int r, const CUtensorMap& map, const SkinnyArgs& args, dim3 grid, int split, size_t smem,
                     bool pdl, cudaStream_t stream) {
   switch (r) {
     case 1:
-      return launch_skinny_t<MT, 1, XT, E4M3>(map, args, grid, split, smem, pdl, stream);
+      return launch_skinny_t<MT, 1, XT, E4M3, AG>(map, args, grid, split, smem, pdl, stream);
     case 2:
-      return launch_skinny_t<MT, 2, XT, E4M3>(map, args, grid, split, smem, pdl, stream);
+      return launch_skinny_t<MT, 2, XT, E4M3, AG>(map, args, grid, split, smem, pdl, stream);
     case 4:
-      return launch_skinny_t<MT, 4, XT, E4M3>(map, args, grid, split, smem, pdl, stream);
+      return launch_skinny_t<MT, 4, XT, E4M3, AG>(map, args, grid, split, smem, pdl, stream);
     default:
-      return launch_skinny_t<MT, 8, XT, E4M3>(map, args, grid, split, smem, pdl, stream);
+      return launch_skinny_t<MT, 8, XT, E4M3, AG>(map, args, grid, split, smem, pdl, stream);
   }
 }
 
 template <typename XT>
 int launch_skinny_mt(const SkinnyPlan& p, const CUtensorMap& map, const SkinnyArgs& args, bool pdl,
                      cudaStream_t stream) {
+  if (args.peer_out != nullptr) {
+    // The all-gather form: int8 weights, up to 16 rows (AUTO's range for it).
+    if (args.w_fmt != kWInt8) return QTTS_ERR_VARIANT;
+    if (p.mt == 1) return launch_skinny_r<1, XT, false, true>(p.r, map, args, p.grid, p.split, p.smem, pdl, stream);
+    if (p.mt == 2) return launch_skinny_r<2, XT, false, true>(p.r, map, args, p.grid, p.split, p.smem, pdl, stream);
+    return QTTS_ERR_VARIANT;
+  }
   if (args.w_fmt == kWE4M3) {
     // fp8 weight-only takes this kernel up to 16 rows only.
     if (p.mt == 1) return launch_skinny_r<1, XT, true>(p.r, map, args, p.grid, p.split, p.smem, pdl, stream);

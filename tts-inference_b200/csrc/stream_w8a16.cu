@@ -346,8 +346,6 @@ __global__ void __launch_bounds__(kStThreads, 2)
       const uint4 wb0 = lds128(sb + offB0);
       const uint4 wa1 = lds128(sb + offA1);
       const uint4 wb1 = lds128(sb + offB1);
-      __syncwarp();
-      if (lane == 0) mbar_arrive(&empty[s]);
 
       const uint32_t wA[2][4] = {{wa0.x, wa0.y, wa0.z, wa0.w}, {wa1.x, wa1.y, wa1.z, wa1.w}};
       const uint32_t wB[2][4] = {{wb0.x, wb0.y, wb0.z, wb0.w}, {wb1.x, wb1.y, wb1.z, wb1.w}};
@@ -379,6 +377,10 @@ __global__ void __launch_bounds__(kStThreads, 2)
           }
         }
       }
+      // The stage goes back to the producer only after every loaded word has
+      // been consumed (a TMA refill cannot overtake a read of the stage).
+      __syncwarp();
+      if (lane == 0) mbar_arrive(&empty[s]);
     }
     if (!ok) {
       if (lane == 0) record_status(QTTS_ERR_TIMEOUT);

@@ -85,7 +85,7 @@ __device__ __forceinline__ void tmem_ld<32>(uint32_t taddr, uint32_t (&r)[32]) {
       : "r"(taddr));
 }
 
-template <int NB, typename XT, bool E4M3 = false>
+template <int NB, typename XT, bool E4M3 = false, bool AG = false>
 __global__ void __launch_bounds__(kUmThreads, 1)
     umma_w8a16_kernel(const __grid_constant__ CUtensorMap wmap, const __grid_constant__ CUtensorMap xmap,
                       const SkinnyArgs a) {
@@ -164,7 +164,7 @@ __global__ void __launch_bounds__(kUmThreads, 1)
   const uint32_t tmem = *reinterpret_cast<volatile uint32_t*>(tmem_slot);
   if (split > 1) cluster_arrive_relaxed();
   pdl_launch_dependents();
-  if (a.peer_out != nullptr && tid == 0) ag_prefetch_tables(a);
+  if (AG && tid == 0) ag_prefetch_tables(a);
 
   bool valid = true;
   if (a.group_index != nullptr) {
@@ -293,8 +293,6 @@ __global__ void __launch_bounds__(kUmThreads, 1)
       uint4 v[4];
 #pragma unroll
       for (int cc = 0; cc < 4; ++cc) v[cc] = lds128(rb + (((half * 4 + cc) ^ (row & 7)) << 4));
-      __syncwarp();
-      if (lane == 0) mbar_arrive(&wempty[s]);
       uint32_t r1[32];
 #pragma unroll
       for (int cc = 0; cc < 4; ++cc) {
@@ -302,6 +300,11 @@ __global__ void __launch_bounds__(kUmThreads, 1)
 #pragma unroll
         for (int e = 0; e < 4; ++e) WDequant<XT, E4M3>::run(wd[e], r1[8 * cc + 2 * e], r1[8 * cc + 2 * e + 1]);
       }
+      // The weight stage goes back to the producer only after the conversions
+      // above have consumed every loaded word (a TMA refill cannot overtake a
+      // read of the stage).
+      __syncwarp();
+      if (lane == 0) mbar_arrive(&wempty[s]);
       const int slot = hs % kNA;
       if (hs >= kNA) {
         const bool freed = mbar_wait_bounded(&aempty[slot], ((hs / kNA) - 1) & 1, a.wait_ns);
@@ -327,10 +330,10 @@ __global__ void __launch_bounds__(kUmThreads, 1)
     // Epilogue: accumulator -> registers -> output (or the row owners).
     pdl_wait();
     if (tid == 0) QTTS_TRACE_STAMP(5);
-    if (a.peer_out != nullptr) ag_ep = ag_epoch(a);  // the load overlaps the accumulator wait
+    if (AG) ag_ep = ag_epoch(a);  // the load overlaps the accumulator wait
     const bool dready = mbar_wait_bounded(dfull, 0, a.wait_ns);
     // Every CTA announces (no wait depends on another CTA of this grid having started).
-    if (a.peer_out != nullptr && tid == 0) ag_announce_ready(a, ag_ep);
+    if (AG && tid == 0) ag_announce_ready(a, ag_ep);
     if (!dready) {
       if (lane == 0) record_status(QTTS_ERR_TIMEOUT);
       *verr = 1;
@@ -347,8 +350,7 @@ __global__ void __launch_bounds__(kUmThreads, 1)
     if (split == 1) {
       const int n = n0 + row;
       bool store_ok = valid && !cta_err;
-      if (a.peer_out != nullptr)
-        store_ok = ag_gate_stores(a, ag_ep, gate_flag, 1, kUmDqWarps * 32, tid == 0) && store_ok;
+      if (AG) store_ok = ag_gate_stores(a, ag_ep, gate_flag, 1, kUmDqWarps * 32, tid == 0) && store_ok;
       if (store_ok && n < a.N) {
         const int64_t ch = static_cast<int64_t>(group) * a.N + n;
         const float sc = load_as_float(a.scale, a.scale_dtype, ch);
@@ -356,7 +358,7 @@ __global__ void __launch_bounds__(kUmThreads, 1)
 #pragma unroll
         for (int c = 0; c < HALF; ++c) {
           const int col = HALF * half + c;
-          if (col < mrows) put_out(a, og, pbase, static_cast<int64_t>(col) * a.ldo + n, from_float<XT>(v[c] * sc + bias));
+          if (col < mrows) put_out<AG>(a, og, pbase, static_cast<int64_t>(col) * a.ldo + n, from_float<XT>(v[c] * sc + bias));
         }
       }
     } else {
@@ -386,7 +388,7 @@ __global__ void __launch_bounds__(kUmThreads, 1)
         if (tid == 0) record_status(QTTS_ERR_TIMEOUT);
         have = mbar_wait_bounded(recv_bar, 0, 4 * a.wait_ns);  // peers always send
       }
-      if (a.peer_out != nullptr) have = ag_gate_stores(a, ag_ep, gate_flag, 1, kUmDqWarps * 32, tid == 0) && have;
+      if (AG) have = ag_gate_stores(a, ag_ep, gate_flag, 1, kUmDqWarps * 32, tid == 0) && have;
       if (have && valid && !cta_err) {
         // Thread = (owned row, 4 batch columns): one 16-byte load per peer.
         const int rbase = static_cast<int>(crank) * rpo;
@@ -411,7 +413,7 @@ __global__ void __launch_bounds__(kUmThreads, 1)
 #pragma unroll
             for (int q = 0; q < 4; ++q) {
               const int m = 4 * mq + q;
-              if (m < mrows) put_out(a, og, pbase, static_cast<int64_t>(m) * a.ldo + n, from_float<XT>(rv[q] * sc + bias));
+              if (m < mrows) put_out<AG>(a, og, pbase, static_cast<int64_t>(m) * a.ldo + n, from_float<XT>(rv[q] * sc + bias));
             }
           }
         }
@@ -432,7 +434,7 @@ __global__ void __launch_bounds__(kUmThreads, 1)
   // registers need no source kept alive, and each CTA waited for everything
   // sent to it.
   if (split > 1 && (warp == kUmProducerWarp || warp == kUmMmaWarp)) cluster_wait();
-  if (a.peer_out != nullptr) ag_finish(a, ag_ep);
+  if (AG) ag_finish(a, ag_ep);
   if (warp == kUmProducerWarp && lane == 0 && *verr != 0) {
     // Drain our own copies in flight (weights and activations).
     for (int s = 0; s < WS && s < w_issued; ++s) {
@@ -451,10 +453,10 @@ __global__ void __launch_bounds__(kUmThreads, 1)
 
 namespace {
 
-template <int NB, typename XT, bool E4M3>
+template <int NB, typename XT, bool E4M3, bool AG>
 int launch_umma_t(const CUtensorMap& map, const CUtensorMap& xmap, const SkinnyArgs& args, const SkinnyPlan& p,
                   bool pdl, cudaStream_t stream) {
-  auto kern = umma_w8a16_kernel<NB, XT, E4M3>;
+  auto kern = umma_w8a16_kernel<NB, XT, E4M3, AG>;
   static int configured[64] = {0};
   int dev = 0;
   cudaGetDevice(&dev);
@@ -488,22 +490,26 @@ int launch_umma_t(const CUtensorMap& map, const CUtensorMap& xmap, const SkinnyA
   return cudaLaunchKernelEx(&cfg, kern, map, xmap, args) == cudaSuccess ? QTTS_OK : QTTS_ERR_LAUNCH;
 }
 
-template <typename XT, bool E4M3>
+template <typename XT, bool E4M3, bool AG = false>
 int launch_umma_w(const CUtensorMap& map, const CUtensorMap& xmap, const SkinnyArgs& args, const SkinnyPlan& p,
                   bool pdl, cudaStream_t stream) {
   switch (p.mt) {
     case 2:
-      return launch_umma_t<16, XT, E4M3>(map, xmap, args, p, pdl, stream);
+      return launch_umma_t<16, XT, E4M3, AG>(map, xmap, args, p, pdl, stream);
     case 4:
-      return launch_umma_t<32, XT, E4M3>(map, xmap, args, p, pdl, stream);
+      return launch_umma_t<32, XT, E4M3, AG>(map, xmap, args, p, pdl, stream);
     default:
-      return launch_umma_t<64, XT, E4M3>(map, xmap, args, p, pdl, stream);
+      return launch_umma_t<64, XT, E4M3, AG>(map, xmap, args, p, pdl, stream);
   }
 }
 
 template <typename XT>
 int launch_umma_nb(const CUtensorMap& map, const CUtensorMap& xmap, const SkinnyArgs& args, const SkinnyPlan& p,
                    bool pdl, cudaStream_t stream) {
+  if (args.peer_out != nullptr) {
+    // The all-gather form: int8 weights only.
+    return args.w_fmt == kWInt8 ? launch_umma_w<XT, false, true>(map, xmap, args, p, pdl, stream) : QTTS_ERR_VARIANT;
+  }
   return args.w_fmt == kWE4M3 ? launch_umma_w<XT, true>(map, xmap, args, p, pdl, stream)
                               : launch_umma_w<XT, false>(map, xmap, args, p, pdl, stream);
 }
