@@ -383,6 +383,74 @@ def fp8_sweep(device, seed: int) -> dict:
     }
 
 
+def w8a8_sweep(device, seed: int) -> dict:
+    """int8 W8A8 (Int8Method.apply: per-token int8 activation quantization + tcgen05
+    kind::i8 GEMM) on the four talker shapes at M in {16, 32, 64, 128}, beside the
+    reference's op sequence on the same GPU (torch amax/clamp/div/round/clamp/cast,
+    torch._int_mm with its 17-row padding, the fp32 scaling). Same bytes as config 3.
+    Weights rotate through >= 256 MB per shape."""
+    from qtts_b200.quant import kernels as qk
+
+    gen = torch.Generator(device=device)
+    gen.manual_seed(seed + 13)
+    out: dict = {}
+    tot_bytes = tot_us = tot_ref_us = 0.0
+    for label, n, k in SHAPES:
+        p = pool_size(n, k)
+        wq = torch.empty((p, n, k), dtype=torch.int8, device=device)
+        ws = torch.empty((p, n), dtype=torch.float32, device=device)
+        for i in range(p):
+            q, s = qk.quantize_int8_rows(torch.randn((n, k), generator=gen, device=device) * 0.02)
+            wq[i].copy_(q)
+            ws[i].copy_(s)
+            del q, s
+        wkn = torch.empty((p, k, n), dtype=torch.int8, device=device)
+        for i in range(p):
+            wkn[i].copy_(wq[i].t())  # the reference's [K, N] int8_weight (int8.py:126-128)
+        for m in FP8_ROWS:
+            x = torch.randn((m, k), generator=gen, device=device).to(torch.bfloat16)
+
+            def ours(x=x):
+                for c in range(CALLS_PER_GRAPH):
+                    xq, sx = qk.int8_quant_rows(x)
+                    qk.i8_scaled_mm(xq, sx, wq[c % p], ws[c % p], None, torch.bfloat16)
+
+            def reference(x=x, m=m):
+                for c in range(CALLS_PER_GRAPH):
+                    scale_x = x.abs().amax(dim=1, keepdim=True).clamp_min(1e-6) / 127.0
+                    q = (x / scale_x).round().clamp_(-127, 127).to(torch.int8)
+                    if m < 17:
+                        q = torch.cat([q, q.new_zeros(17 - m, k)], dim=0)
+                    acc = torch._int_mm(q, wkn[c % p])[:m]
+                    (acc.float() * scale_x.float() * ws[c % p].reshape(1, -1)).to(torch.bfloat16)
+
+            us = graph_us_per_call(ours)
+            try:
+                ref_us = graph_us_per_call(reference)
+            except Exception as exc:  # torch._int_mm unavailable for this shape/build
+                ref_us = None
+                print(f"torch._int_mm reference failed: {exc}", file=sys.stderr)
+            b = fp8_algo_bytes(n, k, m)
+            out.setdefault(label, {})[str(m)] = {
+                "us": round(us, 3),
+                "gbs": round(b / (us * 1e-6) / 1e9, 1),
+                "torch_us": round(ref_us, 3) if ref_us else None,
+                "speedup_vs_torch": round(ref_us / us, 3) if ref_us else None,
+            }
+            tot_bytes += b
+            tot_us += us
+            tot_ref_us += ref_us or 0.0
+        del wq, ws, wkn
+        torch.cuda.empty_cache()
+    return {
+        "workload": "int8 W8A8 (act quant + tcgen05 kind::i8 GEMM, 2 launches per linear) on the 4 talker shapes "
+        "at M in {16,32,64,128}; weights rotate through >= 256 MB per shape",
+        "gbs": round(tot_bytes / (tot_us * 1e-6) / 1e9, 1),
+        "torch_gbs": round(tot_bytes / (tot_ref_us * 1e-6) / 1e9, 1) if tot_ref_us else None,
+        "per_point": out,
+    }
+
+
 def fp8w_sweep(device, seed: int) -> dict:
     """fp8 weight-only (e4m3 weights, bf16 activations, Fp8WeightOnlyMethod.apply) on the
     config-2 grid: the four talker shapes at M in {1..64}, weights rotating through
@@ -776,6 +844,7 @@ def run_gpu_arm(args) -> None:
     # ---- config 3 (fp8) and config 5 (N-sharded GEMM + all-gather), outside the timed region
     fp8 = fp8_sweep(device, args.seed) if args.fp8 and rank == 0 else None
     fp8w = fp8w_sweep(device, args.seed) if args.fp8w and rank == 0 else None
+    w8a8 = w8a8_sweep(device, args.seed) if args.w8a8 and rank == 0 else None
     barrier(world)
     sharded = sharded_sweep(world, rank, device, args.seed) if args.sharded else None
     talker = talker_frames(args.seed) if args.talker and rank == 0 else None
@@ -859,6 +928,7 @@ def run_gpu_arm(args) -> None:
             "per_point": per_point,
             "fp8": fp8,
             "fp8_weight_only": fp8w,
+            "int8_w8a8": w8a8,
             "sharded": sharded,
             "talker": talker,
         }
@@ -941,6 +1011,7 @@ def main(argv=None) -> int:
     ap.add_argument("--no-bf16-compare", dest="bf16_compare", action="store_false")
     ap.add_argument("--no-fp8", dest="fp8", action="store_false", help="skip the config-3 fp8 sweep")
     ap.add_argument("--no-fp8w", dest="fp8w", action="store_false", help="skip the fp8 weight-only sweep")
+    ap.add_argument("--no-w8a8", dest="w8a8", action="store_false", help="skip the int8 W8A8 sweep")
     ap.add_argument("--no-talker", dest="talker", action="store_false",
                     help="skip the config-4 talker + code predictor frames/s measurement")
     ap.add_argument("--no-sharded", dest="sharded", action="store_false",

@@ -268,6 +268,27 @@ QTTS_API int qtts_fp8_gemm(const uint8_t* xq, int64_t ldxq, const float* scale_x
  * (with that device current), so make one call before recording a graph. */
 #define QTTS_NOALLOC_MAX_ROWS 1024
 #define QTTS_NOALLOC_MAX_CODES (1 << 20)
+/* ---- int8 W8A8 (Int8Method) --------------------------------------------------
+ * Per-token int8 quantization of the activations of Int8Method.apply
+ * (qtts/quant/int8.py:138-140), each step in the activation dtype as torch
+ * evaluates it on a CUDA tensor: c = max(amax_k |x[m,k]|, 1e-6 rounded to the
+ * dtype); s = dtype(c * fl32(1 / 127)); q[m,k] = clamp(round_half_even(
+ * dtype(x[m,k] / s)), -127, 127). q: [M, K] int8 (ld = K); scale_x: [M] fp32
+ * holding s. Bit-exact with the reference's op sequence on the GPU. */
+QTTS_API int qtts_int8_quant_rows(const void* x, int64_t ldx, int x_dtype, int8_t* q, float* scale_x, int M, int K,
+                                  unsigned flags, void* stream);
+
+/* int8 W8A8 GEMM: replaces torch._int_mm and the scaling of Int8Method.apply
+ * (qtts/quant/int8.py:142-153, no 17-row padding):
+ *   out[m,n] = cast( ((float(sum_k xq[m,k] * wq[n,k]) * scale_x[m]) * scale_w[n]) + bias[n] )
+ * with an exact int32 sum (tcgen05.mma kind::i8) and the reference's fp32
+ * roundings in that order. xq: [M, K] int8; wq: [N, K] int8 (K-major, i.e.
+ * the reference's [K, N] int8_weight transposed); scale_w [N] fp32; bias [N]
+ * of out_dtype or NULL. Variants as for qtts_fp8_gemm. */
+QTTS_API int qtts_i8_gemm(const int8_t* xq, int64_t ldxq, const float* scale_x, const int8_t* wq, int64_t ldw,
+                          const float* scale_w, const void* bias, void* out, int64_t ldo, int out_dtype, int M, int N,
+                          int K, int variant, unsigned flags, void* stream);
+
 QTTS_API int qtts_fp8_linear_noalloc(const void* x, int64_t ldx, int x_dtype,
                             const uint8_t* wq, int64_t ldw, const float* scale_w,
                             const void* bias, void* out, int64_t ldo, int out_dtype,

@@ -22,8 +22,11 @@ from .qtts_ref import (  # noqa: F401
     fp16_round,
     fp8_scaled_mm_reference,
     fp8_weight_only_reference,
+    int8_w8a8_reference,
     naive_dequant_linear,
+    round_to,
     quantize_act_fp8,
+    quantize_act_int8,
     quantize_weight_fp8,
     quantize_weight_per_channel,
     rel_err,

@@ -158,6 +158,28 @@ def quantize_act_fp8(x, dtype: str = "bf16", device: str = "cuda") -> tuple[np.n
     return e4m3_encode(xv / scale[:, None]), scale
 
 
+def quantize_act_int8(x, dtype: str = "bf16", device: str = "cuda") -> tuple[np.ndarray, np.ndarray]:
+    """qtts/quant/int8.py:138-140 -- Int8Method's per-token activation quantization, each
+    step in the activation dtype as torch evaluates it:
+
+    amax (exact), ``clamp_min(1e-6)`` (the bound rounded to the dtype), ``/ 127`` (a
+    tensor / number: on ``device``, rounded to the dtype), ``flat / scale_x`` (tensor /
+    tensor: an IEEE fp32 division rounded to the dtype), ``round()`` half to even,
+    clamp to +-127. Returns (q int8 [M, K], scale fp32 [M] holding the dtype scale).
+    """
+    xv = np.asarray(x, dtype=np.float32)
+    amax = np.abs(xv).max(axis=1)
+    floor = round_to(np.array([1e-6], dtype=np.float32), dtype)[0]
+    c = np.maximum(amax, floor)
+    scale = round_to(div_by_number(c, 127.0, device), dtype)
+    with np.errstate(invalid="ignore", divide="ignore"):
+        v = np.rint(round_to((xv / scale[:, None]).astype(np.float32), dtype))
+    # 0 / 0 (a zero scale from an all-zero fp16 row) stays NaN through round and
+    # clamp and converts to 0 on the GPU.
+    q = np.where(np.isnan(v), 0.0, np.clip(v, -127, 127)).astype(np.int8)
+    return q, scale.astype(np.float32)
+
+
 # ----------------------------------------------------------------------------
 # GEMMs
 
@@ -206,6 +228,20 @@ def fp8_scaled_mm_reference(xq, scale_x, wq, scale_w, bias=None) -> np.ndarray:
     if bias is not None:
         out = out + np.asarray(bias, dtype=np.float64)[None, :]
     return out
+
+
+def int8_w8a8_reference(xq, scale_x, wq, scale_w, bias=None) -> np.ndarray:
+    """qtts/quant/int8.py:142-153 -- ``torch._int_mm`` then ``acc.float() * scale_x *
+    int8_scale (+ bias)``: the exact integer sum converted to fp32, then the two products
+    and the bias each rounded to fp32 in that order. Returns fp32 [M, N] (the caller
+    rounds to the output dtype)."""
+    acc = np.asarray(xq, dtype=np.int64) @ np.asarray(wq, dtype=np.int64).T
+    y = acc.astype(np.float32)
+    y = (y * np.asarray(scale_x, dtype=np.float32).reshape(-1, 1)).astype(np.float32)
+    y = (y * np.asarray(scale_w, dtype=np.float32).reshape(1, -1)).astype(np.float32)
+    if bias is not None:
+        y = (y + np.asarray(bias, dtype=np.float32).reshape(1, -1)).astype(np.float32)
+    return y
 
 
 def rel_err(out, ref) -> float:

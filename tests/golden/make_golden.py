@@ -17,6 +17,10 @@ records, on seeded CPU inputs:
 * the tuning script's ``quantize`` and ``naive_dequant_linear``
   (examples/kernels/tune_w8_gemm.py:73-85) -- the eager dequantize-then-matmul
   the kernels are checked against;
+* ``Int8Method`` (qtts/quant/int8.py:120-155) on bf16, fp16 and fp32 layers
+  with a bias: the int8 weight and scale, the activation codes (captured from
+  ``torch._int_mm``, which runs on the CPU) and the output, including an
+  all-zero row, a row below the 1e-6 floor and a large row;
 * the byte/convert report of ``apply_quantization`` / ``quantize_module``
   (qtts/quant/base.py:74-113, 155-183) with int8 weight-only, calibration
   off, on a small module tree with the reference's layer names.
@@ -118,6 +122,41 @@ def main() -> None:
         y = ref_tune.naive_dequant_linear(x, packed, scale, torch.bfloat16)
         out[f"naive_x_m{m}"] = f32(x)
         out[f"naive_y_m{m}"] = f32(y)
+
+    # -- Int8Method (W8A8): activation codes captured from torch._int_mm, and the output --
+    gi = torch.Generator().manual_seed(7)
+    wi = torch.randn(n, k, generator=gi) * 0.02
+    bi = torch.randn(n, generator=gi)
+    out["w8a8_w"] = f32(wi)
+    out["w8a8_bias"] = f32(bi)
+    seen: dict[str, torch.Tensor] = {}
+    real_int_mm = torch._int_mm
+
+    def int_mm_recorder(a, b):
+        seen["q"] = a
+        return real_int_mm(a, b)
+
+    torch._int_mm = int_mm_recorder
+    try:
+        for name, dtype in (("bf16", torch.bfloat16), ("fp16", torch.float16), ("f32", torch.float32)):
+            method = ref_int8.Int8Method()
+            layer = LinearBase(k, n, bias=True, dtype=dtype)
+            layer.weight.data.copy_(wi.to(dtype))
+            layer.bias.data.copy_(bi.to(dtype))
+            method.process_weights(layer)
+            out[f"w8a8_wq_{name}"] = layer.int8_weight.t().contiguous().numpy()
+            out[f"w8a8_ws_{name}"] = layer.int8_scale.numpy()
+            x = torch.randn(6, k, generator=gi)
+            x[1] = 0.0
+            x[2] = x[2] * 1e-8  # amax below the 1e-6 floor
+            x[3] = x[3] * 300.0
+            x = x.to(dtype)
+            y = method.apply(layer, x, layer.bias)
+            out[f"w8a8_x_{name}"] = f32(x)
+            out[f"w8a8_q_{name}"] = seen["q"][: x.shape[0]].numpy()  # apply pads to 17 rows
+            out[f"w8a8_y_{name}"] = f32(y)
+    finally:
+        torch._int_mm = real_int_mm
 
     np.savez_compressed(HERE / "quant_golden.npz", **out)
 

@@ -125,3 +125,21 @@ def test_quantizers_cuda_form_consistent(golden, src):
         same = sc == sg
         np.testing.assert_array_equal(qc[same], qg[same])
         assert np.all(np.abs(sc.view(np.int32) - sg.view(np.int32)) <= 1)
+
+
+@pytest.mark.parametrize("dtype", ["bf16", "fp16", "f32"])
+def test_int8_w8a8_matches_reference(golden, dtype):
+    """Int8Method (W8A8) through the oracle against the reference run on the CPU: the
+    weight codes, the activation codes captured from torch._int_mm, and the output,
+    bit for bit (the CPU form of ``tensor / number``)."""
+    name = {"bf16": "bf16", "fp16": "fp16", "f32": "f32"}[dtype]
+    w = oracle.round_to(golden["w8a8_w"], dtype)
+    wq, ws = oracle.quantize_weight_per_channel(w, device="cpu")
+    np.testing.assert_array_equal(wq, golden[f"w8a8_wq_{name}"])
+    np.testing.assert_array_equal(ws, golden[f"w8a8_ws_{name}"])
+    x = golden[f"w8a8_x_{name}"]
+    q, sx = oracle.quantize_act_int8(x, dtype, device="cpu")
+    np.testing.assert_array_equal(q, golden[f"w8a8_q_{name}"])
+    bias = oracle.round_to(golden["w8a8_bias"], dtype)
+    y = oracle.round_to(oracle.int8_w8a8_reference(q, sx, wq, ws, bias), dtype)
+    np.testing.assert_array_equal(y, golden[f"w8a8_y_{name}"])

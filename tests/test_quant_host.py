@@ -215,27 +215,22 @@ def test_apply_quantization_routing(monkeypatch):
 def test_build_method_selection():
     with pytest.raises(ValueError):
         build_method(QuantConfig(method="int4"))  # type: ignore[arg-type]
-    assert build_method(QuantConfig(method="int8")).name == "int8"
     if not torch.cuda.is_available():
+        with pytest.raises(RuntimeError, match="sm_100a"):
+            build_method(QuantConfig(method="int8"))
         with pytest.raises(RuntimeError, match="sm_100a"):
             build_method(QuantConfig(method="int8_weight_only"))
         with pytest.raises(RuntimeError, match="fp8 quantization unavailable"):
             build_method(QuantConfig(method="fp8"))
 
 
-def test_int8_w8a8_method_on_cpu():
-    # Int8Method stays on torch._int_mm as in the reference; check its math on CPU.
+def test_int8_w8a8_method_needs_the_library():
+    # Int8Method runs on the sm_100a kernels (no CPU or torch._int_mm fallback).
     from qtts_b200.quant.int8 import Int8Method
 
-    lin = LinearBase(32, 16, dtype=torch.float32)
-    lin.weight.data.normal_(0, 0.05)
-    ref_w = lin.weight.detach().clone()
-    m = Int8Method()
-    m.process_weights(lin)
-    lin.quant_method = m
-    x = torch.randn(3, 32)
-    y = lin(x)
-    assert oracle.rel_err(y.numpy(), (x @ ref_w.T).numpy()) < 3e-2
+    if not torch.cuda.is_available():
+        with pytest.raises(RuntimeError, match="sm_100a"):
+            Int8Method()
 
 
 # ---------------------------------------------------------------- calibration

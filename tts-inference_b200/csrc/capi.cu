@@ -221,6 +221,48 @@ __global__ void __launch_bounds__(256) generic_fp8_kernel(const GenericFp8Args a
   }
 }
 
+// SIMT int8 W8A8 for shapes the tensor-core kernel cannot take: exact int32
+// sums, epilogue in the reference's order (qtts/quant/int8.py:148-153).
+template <typename OT>
+__global__ void __launch_bounds__(256) generic_i8_kernel(const GenericFp8Args a) {
+  pdl_launch_dependents();
+  pdl_wait();
+  const int warp = threadIdx.x >> 5;
+  const int lane = threadIdx.x & 31;
+  const int n = blockIdx.x * 8 + warp;
+  const int m0 = blockIdx.y * 8;
+  if (n >= a.N) return;
+  const int8_t* wr = reinterpret_cast<const int8_t*>(a.wq) + static_cast<int64_t>(n) * a.ldw;
+  const int8_t* xq = reinterpret_cast<const int8_t*>(a.xq);
+  int acc[8];
+#pragma unroll
+  for (int i = 0; i < 8; ++i) acc[i] = 0;
+  for (int k = lane; k < a.K; k += 32) {
+    const int wv = wr[k];
+#pragma unroll
+    for (int i = 0; i < 8; ++i) {
+      if (m0 + i < a.M) acc[i] += static_cast<int>(xq[static_cast<int64_t>(m0 + i) * a.ldxq + k]) * wv;
+    }
+  }
+#pragma unroll
+  for (int i = 0; i < 8; ++i) {
+#pragma unroll
+    for (int o = 16; o > 0; o >>= 1) acc[i] += __shfl_xor_sync(0xffffffffu, acc[i], o);
+  }
+  if (lane == 0) {
+    const float sw = a.scale_w[n];
+    OT* o = static_cast<OT*>(a.out);
+#pragma unroll
+    for (int i = 0; i < 8; ++i) {
+      if (m0 + i < a.M) {
+        float y = __fmul_rn(__fmul_rn(__int2float_rn(acc[i]), a.scale_x[m0 + i]), sw);
+        if (a.bias != nullptr) y = __fadd_rn(y, to_float(static_cast<const OT*>(a.bias)[n]));
+        o[static_cast<int64_t>(m0 + i) * a.ldo + n] = from_float<OT>(y);
+      }
+    }
+  }
+}
+
 // ---- row quantizers ---------------------------------------------------------------------
 template <typename T>
 __device__ __forceinline__ float ld_elem(const void* p, int64_t i) {
@@ -291,6 +333,36 @@ __global__ void __launch_bounds__(256) fp8_quant_rows_kernel(const void* x, int6
   for (int k = threadIdx.x; k < K; k += 256) {
     const float v = ld_elem<T>(x, row + k) / s;
     q[qrow + k] = static_cast<uint8_t>(__nv_cvt_float_to_fp8(v, __NV_SATFINITE, __NV_E4M3));
+  }
+}
+
+// Per-token int8 activation quantization of Int8Method (qtts/quant/int8.py:138-140),
+// every step in the activation dtype T as torch evaluates it on a CUDA tensor:
+//   c  = amax.clamp_min(1e-6)               (T; the bound rounds to T)
+//   s  = T(float(c) * fl32(1 / 127))        (tensor / number: fp32 reciprocal product)
+//   q  = int8(clamp(rne(T(float(x) / float(s))), -127, 127))
+// (x / s is a tensor-tensor division: IEEE fp32, rounded to T, then rounded
+// half-to-even). scale_x receives float(s).
+template <typename T>
+__global__ void __launch_bounds__(256) int8_quant_rows_kernel(const void* x, int64_t ldx, int8_t* q, float* scale_x,
+                                                              int M, int K) {
+  __shared__ float sh[8];
+  pdl_launch_dependents();
+  pdl_wait();
+  const int m = blockIdx.x;
+  const int64_t row = static_cast<int64_t>(m) * ldx;
+  float amax = 0.f;
+  for (int k = threadIdx.x; k < K; k += 256) amax = fmaxf(amax, fabsf(ld_elem<T>(x, row + k)));
+  amax = block_max_256(amax, sh);
+  const float c = fmaxf(amax, to_float(from_float<T>(1e-6f)));
+  const float s = to_float(from_float<T>(c * (1.0f / 127.0f)));
+  if (threadIdx.x == 0) scale_x[m] = s;
+  const int64_t qrow = static_cast<int64_t>(m) * K;
+  for (int k = threadIdx.x; k < K; k += 256) {
+    const float v = rintf(to_float(from_float<T>(__fdiv_rn(ld_elem<T>(x, row + k), s))));
+    // A zero scale (an all-zero fp16 row: 1e-6 / 127 underflows) gives 0 / 0;
+    // torch carries the NaN through round and clamp and converts it to 0.
+    q[qrow + k] = isnan(v) ? static_cast<int8_t>(0) : static_cast<int8_t>(fminf(fmaxf(v, -127.0f), 127.0f));
   }
 }
 
@@ -798,6 +870,99 @@ int qtts_fp8_gemm(const uint8_t* xq, int64_t ldxq, const float* scale_x, const u
       return launch_simple(generic_fp8_kernel<__half>, grid, dim3(256), ga, pdl, s);
     default:
       return launch_simple(generic_fp8_kernel<float>, grid, dim3(256), ga, pdl, s);
+  }
+}
+
+int qtts_int8_quant_rows(const void* x, int64_t ldx, int x_dtype, int8_t* q, float* scale_x, int M, int K,
+                         unsigned flags, void* stream) {
+  if (M < 0 || K < 0) return QTTS_ERR_SHAPE;
+  if (M == 0) return QTTS_OK;
+  if (x == nullptr || q == nullptr || scale_x == nullptr) return QTTS_ERR_NULL;
+  if (ldx < K) return QTTS_ERR_SHAPE;
+  const int dev_ok = check_device();
+  if (dev_ok != QTTS_OK) return dev_ok;
+  cudaLaunchConfig_t cfg = {};
+  cfg.gridDim = dim3(M);
+  cfg.blockDim = dim3(256);
+  cfg.stream = static_cast<cudaStream_t>(stream);
+  cudaLaunchAttribute attr[1];
+  if ((flags & QTTS_FLAG_PDL) != 0) {
+    attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+    attr[0].val.programmaticStreamSerializationAllowed = 1;
+    cfg.attrs = attr;
+    cfg.numAttrs = 1;
+  }
+  cudaError_t e;
+  switch (x_dtype) {
+    case QTTS_BF16:
+      e = cudaLaunchKernelEx(&cfg, int8_quant_rows_kernel<__nv_bfloat16>, x, ldx, q, scale_x, M, K);
+      break;
+    case QTTS_FP16:
+      e = cudaLaunchKernelEx(&cfg, int8_quant_rows_kernel<__half>, x, ldx, q, scale_x, M, K);
+      break;
+    case QTTS_FP32:
+      e = cudaLaunchKernelEx(&cfg, int8_quant_rows_kernel<float>, x, ldx, q, scale_x, M, K);
+      break;
+    default:
+      return QTTS_ERR_DTYPE;
+  }
+  return e == cudaSuccess ? QTTS_OK : QTTS_ERR_LAUNCH;
+}
+
+int qtts_i8_gemm(const int8_t* xq, int64_t ldxq, const float* scale_x, const int8_t* wq, int64_t ldw,
+                 const float* scale_w, const void* bias, void* out, int64_t ldo, int out_dtype, int M, int N, int K,
+                 int variant, unsigned flags, void* stream) {
+  if (M < 0 || N < 0 || K < 0) return QTTS_ERR_SHAPE;
+  if (M == 0 || N == 0) return QTTS_OK;
+  if (xq == nullptr || scale_x == nullptr || wq == nullptr || scale_w == nullptr || out == nullptr)
+    return QTTS_ERR_NULL;
+  if (!is_float_dtype(out_dtype)) return QTTS_ERR_DTYPE;
+  if (ldxq < K || ldw < K || ldo < N) return QTTS_ERR_SHAPE;
+  const int dev_ok = check_device();
+  if (dev_ok != QTTS_OK) return dev_ok;
+  cudaStream_t s = static_cast<cudaStream_t>(stream);
+  const bool pdl = (flags & QTTS_FLAG_PDL) != 0;
+  const bool tc_ok = K % 16 == 0 && aligned16(xq) && aligned16(wq) && ldxq % 16 == 0 && ldw % 16 == 0;
+  const int family = variant == QTTS_VARIANT_AUTO ? (tc_ok ? 0x200 : 0) : (variant & 0xF00);
+  if (family == 0x200) {
+    if (!tc_ok) return QTTS_ERR_ALIGN;
+    const int split = variant == QTTS_VARIANT_AUTO ? 0 : (variant & 0xF);
+    if (!(split == 0 || split == 1 || split == 2 || split == 4) || (variant & 0xF0F0) != 0) return QTTS_ERR_VARIANT;
+    const Fp8Plan plan = plan_fp8(M, N, K, split);
+    if (plan.grid.z > 65535u) return QTTS_ERR_SHAPE;
+    CUtensorMap wmap, xmap;
+    int r = make_tmap_u8_2d(&wmap, wq, static_cast<uint64_t>(N), static_cast<uint64_t>(K), static_cast<uint64_t>(ldw),
+                            128, 128);
+    if (r != QTTS_OK) return r;
+    r = make_tmap_u8_2d(&xmap, xq, static_cast<uint64_t>(M), static_cast<uint64_t>(K), static_cast<uint64_t>(ldxq),
+                        static_cast<uint32_t>(plan.nb), 128);
+    if (r != QTTS_OK) return r;
+    Fp8Args fa{};
+    fa.scale_x = scale_x;
+    fa.scale_w = scale_w;
+    fa.bias = bias;
+    fa.out = out;
+    fa.ldo = ldo;
+    fa.M = M;
+    fa.N = N;
+    fa.K = K;
+    fa.k_per_cta = plan.k_per_cta;
+    fa.stages = plan.stages;
+    fa.wait_ns = current_wait_limit_ns();
+    return launch_fp8_gemm(plan, wmap, xmap, fa, out_dtype, pdl, s, /*int8=*/true);
+  }
+  if (variant != QTTS_VARIANT_AUTO && variant != QTTS_VARIANT_GENERIC) return QTTS_ERR_VARIANT;
+  GenericFp8Args ga{reinterpret_cast<const uint8_t*>(xq), ldxq, scale_x, reinterpret_cast<const uint8_t*>(wq), ldw,
+                    scale_w, bias, out, ldo, M, N, K};
+  const dim3 grid((N + 7) / 8, (M + 7) / 8);
+  if (grid.y > 65535u) return QTTS_ERR_SHAPE;
+  switch (out_dtype) {
+    case QTTS_BF16:
+      return launch_simple(generic_i8_kernel<__nv_bfloat16>, grid, dim3(256), ga, pdl, s);
+    case QTTS_FP16:
+      return launch_simple(generic_i8_kernel<__half>, grid, dim3(256), ga, pdl, s);
+    default:
+      return launch_simple(generic_i8_kernel<float>, grid, dim3(256), ga, pdl, s);
   }
 }
 

@@ -188,6 +188,19 @@ __device__ __forceinline__ void umma_f8_ss(uint32_t d_tmem, uint64_t a_desc, uin
       : "memory");
 }
 
+// D[tmem] (+)= A[smem desc] x B[smem desc], kind::i8 (signed int8 in, int32 accumulate).
+__device__ __forceinline__ void umma_i8_ss(uint32_t d_tmem, uint64_t a_desc, uint64_t b_desc, uint32_t idesc,
+                                           uint32_t accumulate) {
+  asm volatile(
+      "{\n"
+      ".reg .pred p;\n"
+      "setp.ne.b32 p, %4, 0;\n"
+      "tcgen05.mma.cta_group::1.kind::i8 [%0], %1, %2, %3, {%5, %6, %7, %8}, p;\n"
+      "}\n" ::"r"(d_tmem),
+      "l"(a_desc), "l"(b_desc), "r"(idesc), "r"(accumulate), "r"(0u), "r"(0u), "r"(0u), "r"(0u)
+      : "memory");
+}
+
 // Shared-memory matrix descriptor for a K-major operand in the canonical
 // 128-byte-swizzled layout: 8-row x 128-byte atoms, atoms of consecutive row
 // groups 1024 bytes apart (stride byte offset), descriptor version 1 (sm_100).
@@ -200,6 +213,12 @@ __device__ __forceinline__ uint64_t smem_desc_k_sw128(uint32_t saddr) {
 // Instruction descriptor: fp32 accumulator, A/B formats, both K-major, M x N.
 __host__ __device__ constexpr uint32_t umma_idesc(uint32_t a_fmt, uint32_t b_fmt, int m, int n) {
   return (1u << 4) | (a_fmt << 7) | (b_fmt << 10) | (static_cast<uint32_t>(n >> 3) << 17) |
+         (static_cast<uint32_t>(m >> 4) << 24);
+}
+// Instruction descriptor for kind::i8: int32 accumulator (format 2), signed
+// 8-bit A and B (format 1), both K-major, M x N.
+__host__ __device__ constexpr uint32_t umma_idesc_i8(int m, int n) {
+  return (2u << 4) | (1u << 7) | (1u << 10) | (static_cast<uint32_t>(n >> 3) << 17) |
          (static_cast<uint32_t>(m >> 4) << 24);
 }
 

@@ -1,4 +1,4 @@
-// fp8-e4m3 W8A8 GEMM on the 5th-generation tensor cores.
+// fp8-e4m3 (and int8) W8A8 GEMM on the 5th-generation tensor cores.
 //
 // Replaces torch._scaled_mm in Fp8Method.apply (qtts/quant/fp8.py:79-88):
 //   out[m, n] = cast( (sum_k xq[m,k] * wq[n,k]) * scale_x[m] * scale_w[n] + bias[n] )
@@ -18,6 +18,12 @@
 // tcgen05.ld (one row per thread). K can be split over a cluster of up to 4
 // CTAs whose partial sums reach the row owner by st.async. All waits are
 // bounded; tensor memory is always freed.
+//
+// The same kernel with I8 = true is the int8 W8A8 GEMM of Int8Method
+// (qtts/quant/int8.py:120-155, which uses torch._int_mm): tcgen05.mma kind::i8
+// on signed int8 operands with an exact int32 accumulator, the split-K
+// partials added as int32, and the epilogue (float(acc) * scale_x) * scale_w +
+// bias in the reference's order.
 #include "common.cuh"
 #include "kernels.h"
 
@@ -41,13 +47,26 @@ __device__ __forceinline__ void f8_tmem_ld<16>(uint32_t taddr, uint32_t (&r)[16]
       : "r"(taddr));
 }
 
-template <int NB, typename OT>
+// Epilogue value of one accumulator word. e4m3 (I8 false): the fp32 sum scaled
+// and biased. int8 (I8 true, Int8Method, qtts/quant/int8.py:148-153): the
+// int32 sum converted and scaled in the reference's order and roundings,
+// ((float(acc) * sx) * sw) + bias, no fused multiply-add.
+template <bool I8>
+__device__ __forceinline__ float w8a8_out(uint32_t acc_bits, float sx, float sw, float bias, bool has_bias) {
+  if (I8) {
+    float y = __fmul_rn(__fmul_rn(__int2float_rn(static_cast<int>(acc_bits)), sx), sw);
+    return has_bias ? __fadd_rn(y, bias) : y;
+  }
+  return __uint_as_float(acc_bits) * sx * sw + bias;
+}
+
+template <int NB, typename OT, bool I8 = false>
 __global__ void __launch_bounds__(kF8Threads, 1)
     fp8_gemm_kernel(const __grid_constant__ CUtensorMap wmap, const __grid_constant__ CUtensorMap xmap,
                     const Fp8Args a) {
   constexpr int XS = NB * 128;  // activation tile bytes per 128-k stage
   constexpr uint32_t kCols = NB < 32 ? 32 : NB;  // TMEM allocation: power of two >= 32
-  constexpr uint32_t kIdesc = umma_idesc(0u /*E4M3*/, 0u /*E4M3*/, 128, NB);
+  constexpr uint32_t kIdesc = I8 ? umma_idesc_i8(128, NB) : umma_idesc(0u /*E4M3*/, 0u /*E4M3*/, 128, NB);
   extern __shared__ uint8_t smem_raw[];
   uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
   const int split = gridDim.y;
@@ -149,7 +168,11 @@ __global__ void __launch_bounds__(kF8Threads, 1)
         for (int i = 0; i < 4; ++i) {
           const uint64_t adesc = smem_desc_k_sw128(waddr + s * kF8StageW + i * 32);
           const uint64_t bdesc = smem_desc_k_sw128(xaddr + s * XS + i * 32);
-          umma_f8_ss(tmem, adesc, bdesc, kIdesc, (it | i) != 0 ? 1u : 0u);
+          if (I8) {
+            umma_i8_ss(tmem, adesc, bdesc, kIdesc, (it | i) != 0 ? 1u : 0u);
+          } else {
+            umma_f8_ss(tmem, adesc, bdesc, kIdesc, (it | i) != 0 ? 1u : 0u);
+          }
         }
         tc_commit(&sempty[s]);
       }
@@ -184,16 +207,18 @@ __global__ void __launch_bounds__(kF8Threads, 1)
       uint32_t d[16];
       f8_tmem_ld<16>(tmem + lane_base + c0, d);
       tc_wait_ld();
-      float v[16];
+      // Raw accumulator words (fp32 bits, or int32 for I8; zero either way).
+      uint32_t v[16];
 #pragma unroll
-      for (int c = 0; c < 16; ++c) v[c] = (n_iters > 0 && !cta_err) ? __uint_as_float(d[c]) : 0.f;
+      for (int c = 0; c < 16; ++c) v[c] = (n_iters > 0 && !cta_err) ? d[c] : 0u;
       if (split == 1) {
         if (!cta_err && n < a.N) {
 #pragma unroll
           for (int c = 0; c < 16; ++c) {
             const int col = c0 + c;
             if (col < mrows) {
-              og[static_cast<int64_t>(col) * a.ldo + n] = from_float<OT>(v[c] * a.scale_x[m0 + col] * sw + bias);
+              og[static_cast<int64_t>(col) * a.ldo + n] =
+                  from_float<OT>(w8a8_out<I8>(v[c], a.scale_x[m0 + col], sw, bias, a.bias != nullptr));
             }
           }
         }
@@ -205,14 +230,15 @@ __global__ void __launch_bounds__(kF8Threads, 1)
         if (owner == static_cast<int>(crank)) {
 #pragma unroll
           for (int c = 0; c < 16; c += 4)
-            *reinterpret_cast<float4*>(recv + recv_offset(rrow, (c0 + c) >> 2, NB)) =
-                make_float4(v[c], v[c + 1], v[c + 2], v[c + 3]);
+            *reinterpret_cast<uint4*>(recv + recv_offset(rrow, (c0 + c) >> 2, NB)) =
+                make_uint4(v[c], v[c + 1], v[c + 2], v[c + 3]);
         } else {
           const uint32_t rbar = mapa_shared(smem_u32(recv_bar), owner);
 #pragma unroll
           for (int c = 0; c < 16; c += 4) {
             const uint32_t rdst = mapa_shared(smem_u32(recv + recv_offset(rrow, (c0 + c) >> 2, NB)), owner);
-            st_async_f32x4(rdst, v[c], v[c + 1], v[c + 2], v[c + 3], rbar);
+            st_async_f32x4(rdst, __uint_as_float(v[c]), __uint_as_float(v[c + 1]), __uint_as_float(v[c + 2]),
+                           __uint_as_float(v[c + 3]), rbar);
           }
         }
       }
@@ -233,21 +259,25 @@ __global__ void __launch_bounds__(kF8Threads, 1)
           const int lr = i - mq * rpo;
           const int nn = n0 + rbase + lr;
           if (nn < a.N) {
-            float4 r = make_float4(0.f, 0.f, 0.f, 0.f);
+            // Partial sums in rank order: fp32 adds, or exact int32 adds (I8).
+            uint32_t rv[4] = {0u, 0u, 0u, 0u};
             for (int p = 0; p < split; ++p) {
-              const float4 t = *reinterpret_cast<const float4*>(recv + recv_offset(p * rpo + lr, mq, NB));
-              r.x += t.x;
-              r.y += t.y;
-              r.z += t.z;
-              r.w += t.w;
+              const uint4 t = *reinterpret_cast<const uint4*>(recv + recv_offset(p * rpo + lr, mq, NB));
+              const uint32_t tv[4] = {t.x, t.y, t.z, t.w};
+#pragma unroll
+              for (int q = 0; q < 4; ++q) {
+                rv[q] = I8 ? static_cast<uint32_t>(static_cast<int>(rv[q]) + static_cast<int>(tv[q]))
+                           : __float_as_uint(__uint_as_float(rv[q]) + __uint_as_float(tv[q]));
+              }
             }
             const float sw = a.scale_w[nn];
             const float bias = a.bias != nullptr ? to_float(static_cast<const OT*>(a.bias)[nn]) : 0.f;
-            const float rv[4] = {r.x, r.y, r.z, r.w};
 #pragma unroll
             for (int q = 0; q < 4; ++q) {
               const int m = 4 * mq + q;
-              if (m < mrows) og[static_cast<int64_t>(m) * a.ldo + nn] = from_float<OT>(rv[q] * a.scale_x[m0 + m] * sw + bias);
+              if (m < mrows)
+                og[static_cast<int64_t>(m) * a.ldo + nn] =
+                    from_float<OT>(w8a8_out<I8>(rv[q], a.scale_x[m0 + m], sw, bias, a.bias != nullptr));
             }
           }
         }
@@ -276,10 +306,10 @@ __global__ void __launch_bounds__(kF8Threads, 1)
 
 namespace {
 
-template <int NB, typename OT>
+template <int NB, typename OT, bool I8>
 int launch_fp8_t(const CUtensorMap& wmap, const CUtensorMap& xmap, const Fp8Args& args, const Fp8Plan& p,
                  bool pdl, cudaStream_t stream) {
-  auto kern = fp8_gemm_kernel<NB, OT>;
+  auto kern = fp8_gemm_kernel<NB, OT, I8>;
   static int configured[64] = {0};
   int dev = 0;
   cudaGetDevice(&dev);
@@ -313,18 +343,31 @@ int launch_fp8_t(const CUtensorMap& wmap, const CUtensorMap& xmap, const Fp8Args
   return cudaLaunchKernelEx(&cfg, kern, wmap, xmap, args) == cudaSuccess ? QTTS_OK : QTTS_ERR_LAUNCH;
 }
 
-template <typename OT>
+template <typename OT, bool I8>
 int launch_fp8_nb(const CUtensorMap& wmap, const CUtensorMap& xmap, const Fp8Args& args, const Fp8Plan& p, bool pdl,
                   cudaStream_t stream) {
   switch (p.nb) {
     case 16:
-      return launch_fp8_t<16, OT>(wmap, xmap, args, p, pdl, stream);
+      return launch_fp8_t<16, OT, I8>(wmap, xmap, args, p, pdl, stream);
     case 32:
-      return launch_fp8_t<32, OT>(wmap, xmap, args, p, pdl, stream);
+      return launch_fp8_t<32, OT, I8>(wmap, xmap, args, p, pdl, stream);
     case 64:
-      return launch_fp8_t<64, OT>(wmap, xmap, args, p, pdl, stream);
+      return launch_fp8_t<64, OT, I8>(wmap, xmap, args, p, pdl, stream);
     default:
-      return launch_fp8_t<128, OT>(wmap, xmap, args, p, pdl, stream);
+      return launch_fp8_t<128, OT, I8>(wmap, xmap, args, p, pdl, stream);
+  }
+}
+
+template <bool I8>
+int launch_w8a8_out(const CUtensorMap& wmap, const CUtensorMap& xmap, const Fp8Args& args, const Fp8Plan& p,
+                    int out_dtype, bool pdl, cudaStream_t stream) {
+  switch (out_dtype) {
+    case QTTS_BF16:
+      return launch_fp8_nb<__nv_bfloat16, I8>(wmap, xmap, args, p, pdl, stream);
+    case QTTS_FP16:
+      return launch_fp8_nb<__half, I8>(wmap, xmap, args, p, pdl, stream);
+    default:
+      return launch_fp8_nb<float, I8>(wmap, xmap, args, p, pdl, stream);
   }
 }
 
@@ -369,16 +412,10 @@ Fp8Plan plan_fp8(int M, int N, int K, int split_req) {
 }
 
 int launch_fp8_gemm(const Fp8Plan& p, const CUtensorMap& wmap, const CUtensorMap& xmap, const Fp8Args& args,
-                    int out_dtype, bool pdl, cudaStream_t stream) {
+                    int out_dtype, bool pdl, cudaStream_t stream, bool int8) {
   if (p.smem > kMaxDynSmem) return QTTS_ERR_VARIANT;
-  switch (out_dtype) {
-    case QTTS_BF16:
-      return launch_fp8_nb<__nv_bfloat16>(wmap, xmap, args, p, pdl, stream);
-    case QTTS_FP16:
-      return launch_fp8_nb<__half>(wmap, xmap, args, p, pdl, stream);
-    default:
-      return launch_fp8_nb<float>(wmap, xmap, args, p, pdl, stream);
-  }
+  return int8 ? launch_w8a8_out<true>(wmap, xmap, args, p, out_dtype, pdl, stream)
+              : launch_w8a8_out<false>(wmap, xmap, args, p, out_dtype, pdl, stream);
 }
 
 }  // namespace qtts

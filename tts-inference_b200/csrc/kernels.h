@@ -101,8 +101,9 @@ struct Fp8Plan {
 };
 
 Fp8Plan plan_fp8(int M, int N, int K, int split_req);
+// int8 = true: the int8 W8A8 form (signed int8 operands, int32 accumulator).
 int launch_fp8_gemm(const Fp8Plan& p, const CUtensorMap& wmap, const CUtensorMap& xmap, const Fp8Args& args,
-                    int out_dtype, bool pdl, cudaStream_t stream);
+                    int out_dtype, bool pdl, cudaStream_t stream, bool int8 = false);
 
 // ---- tensor maps ---------------------------------------------------------------
 // 2-D uint8 tensor map over a row-major [rows, cols] byte matrix with row pitch

@@ -71,6 +71,12 @@ SIGNATURES: dict[str, tuple[object, list[object]]] = {
         [_c_vp, _c_i64, _c_int, _c_vp, _c_i64, _c_vp, _c_int, _c_vp, _c_vp, _c_i64, _c_int, _c_int, _c_int,
          _c_int, _c_uint, _c_vp],
     ),
+    "qtts_int8_quant_rows": (_c_int, [_c_vp, _c_i64, _c_int, _c_vp, _c_vp, _c_int, _c_int, _c_uint, _c_vp]),
+    "qtts_i8_gemm": (
+        _c_int,
+        [_c_vp, _c_i64, _c_vp, _c_vp, _c_i64, _c_vp, _c_vp, _c_vp, _c_i64, _c_int, _c_int, _c_int, _c_int, _c_int,
+         _c_uint, _c_vp],
+    ),
     "qtts_w8a16_plan": (_c_int, [_c_int, _c_int, _c_int, _c_int, _c_int, _c_vp, _c_vp, _c_vp, _c_vp]),
     "qtts_w8a16_gemm_allgather": (
         _c_int,

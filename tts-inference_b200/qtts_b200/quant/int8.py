@@ -9,8 +9,10 @@ dropped after conversion, and ``apply`` computing
 this package; calibration additionally records which kernel variant is fastest
 for the shape, per batch-row bucket, and ``apply`` passes it along.
 
-:class:`Int8Method` (W8A8 through ``torch._int_mm``, int8.py:120-155) is kept
-unchanged: it is not part of the accelerated path.
+:class:`Int8Method` (W8A8, int8.py:120-155) keeps the reference's contract and
+numbers on the same library: a per-token int8 activation quantizer and a
+tcgen05 kind::i8 GEMM with the reference's epilogue arithmetic replace the
+torch op sequence and ``torch._int_mm``.
 """
 
 from __future__ import annotations
@@ -23,13 +25,11 @@ from ..layers.linear import LinearBase
 from ..utils import get_logger
 from .base import QuantMethodBase
 from .calibrate import choose_variant, lookup_variant, worth_quantizing
-from .kernels import kernel_available, quantize_int8_rows, w8_gemm
+from .kernels import i8_scaled_mm, int8_quant_rows, kernel_available, quantize_int8_rows, w8_gemm
 
 logger = get_logger("quant.int8")
 
 _INT8_MAX = 127.0
-#: torch._int_mm rejects fewer rows than this.
-_INT_MM_MIN_ROWS = 17
 #: Batch-row buckets calibration times separately (the kernels' costs change
 #: with the rows of an 8-wide MMA tile that are real, and between tiles).
 _ROW_BUCKETS = (1, 2, 4, 8, 16, 32, 64)
@@ -156,16 +156,28 @@ class Int8WeightOnlyMethod(QuantMethodBase):
 
 
 class Int8Method(QuantMethodBase):
-    """W8A8: per-token activation scales, per-channel weight scales, int8 GEMM (torch._int_mm)."""
+    """W8A8: per-token activation scales, per-channel weight scales, int8 GEMM.
+
+    Same contract and numbers as the reference (qtts/quant/int8.py:120-155),
+    on the sm_100a library instead of torch._int_mm: one kernel quantizes the
+    activations per token (every step in the activation dtype, as torch does
+    on a CUDA tensor) and one tcgen05 kind::i8 kernel computes the exact int32
+    sums and the scaling ((acc * scale_x) * scale_w + bias, the reference's
+    fp32 roundings). No 17-row padding. Buffers: ``int8_weight`` is the
+    reference's [K, N] int8 layout as the transposed view of the K-major
+    [N, K] array the kernel reads; ``int8_scale`` [N] fp32.
+    """
 
     name = "int8"
 
+    def __init__(self) -> None:
+        available, reason = kernel_available()
+        if not available:
+            raise RuntimeError(f"int8 W8A8 needs the sm_100a kernels of qtts_b200: {reason}")
+
     def process_weights(self, layer: LinearBase) -> None:
-        w = layer.weight.detach().float()
-        scale = w.abs().amax(dim=1).clamp_min(1e-12) / _INT8_MAX
-        q = (w / scale[:, None]).round().clamp_(-_INT8_MAX, _INT8_MAX).to(torch.int8)
-        # _int_mm takes B as [K, N]; the transpose is materialised once here.
-        layer.register_buffer("int8_weight", q.t().contiguous(), persistent=False)
+        q, scale = quantize_weight_per_channel(layer.weight)
+        layer.register_buffer("int8_weight", q.t(), persistent=False)
         layer.register_buffer("int8_scale", scale, persistent=False)
         layer.weight = torch.nn.Parameter(
             torch.empty(0, dtype=layer.weight.dtype, device=layer.weight.device), requires_grad=False
@@ -177,16 +189,8 @@ class Int8Method(QuantMethodBase):
     def apply(self, layer: LinearBase, x: torch.Tensor, bias: torch.Tensor | None) -> torch.Tensor:
         shape = x.shape
         flat = x.reshape(-1, shape[-1])
-        scale_x = flat.abs().amax(dim=1, keepdim=True).clamp_min(1e-6) / _INT8_MAX
-        q = (flat / scale_x).round().clamp_(-_INT8_MAX, _INT8_MAX).to(torch.int8)
-        rows = q.shape[0]
-        padded = rows < _INT_MM_MIN_ROWS
-        if padded:
-            q = torch.cat([q, q.new_zeros(_INT_MM_MIN_ROWS - rows, q.shape[1])], dim=0)
-        acc = torch._int_mm(q, layer.int8_weight)  # type: ignore[attr-defined]
-        if padded:
-            acc = acc[:rows]
-        out = acc.float() * scale_x.float() * layer.int8_scale.reshape(1, -1)  # type: ignore[attr-defined]
-        if bias is not None:
-            out += bias.float()
-        return out.to(x.dtype).reshape(*shape[:-1], layer.out_features)
+        q, scale_x = int8_quant_rows(flat)
+        out = i8_scaled_mm(
+            q, scale_x, layer.int8_weight.t(), layer.int8_scale, bias, x.dtype  # type: ignore[attr-defined]
+        )
+        return out.reshape(*shape[:-1], layer.out_features)

@@ -352,3 +352,58 @@ def fp8_scaled_mm(
     )
     nat.check(code, "qtts_fp8_gemm")
     return out
+
+
+def int8_quant_rows(x: torch.Tensor) -> tuple[torch.Tensor, torch.Tensor]:
+    """Per-token int8 activation quantization of Int8Method (qtts/quant/int8.py:138-140):
+    returns (q [M, K] int8, scale_x [M, 1] fp32 holding the activation-dtype scale)."""
+    device = _require_cuda(x)
+    k = x.shape[-1]
+    a = _rows_view(x, k)
+    m = a.shape[0]
+    q = torch.empty((m, k), device=device, dtype=torch.int8)
+    s = torch.empty((m, 1), device=device, dtype=torch.float32)
+    code = nat.lib().qtts_int8_quant_rows(
+        a.data_ptr(), a.stride(0) if m > 1 else k, nat.dtype_code(a.dtype), q.data_ptr(), s.data_ptr(), m, k,
+        _flags(), nat.stream_ptr(device),
+    )
+    nat.check(code, "qtts_int8_quant_rows")
+    return q, s
+
+
+def i8_scaled_mm(
+    xq: torch.Tensor,
+    scale_x: torch.Tensor,
+    wq: torch.Tensor,
+    scale_w: torch.Tensor,
+    bias: torch.Tensor | None,
+    out_dtype: torch.dtype,
+    *,
+    variant: int = nat.VARIANT_AUTO,
+) -> torch.Tensor:
+    """``((float(xq @ wq.T) * scale_x) * scale_w) + bias`` with int8 operands and an exact
+    int32 sum (torch._int_mm and the scaling of Int8Method.apply, qtts/quant/int8.py:142-153).
+
+    ``xq`` [M, K] int8, ``wq`` [N, K] int8 row-major (``int8_weight.t()`` of the
+    reference's [K, N] layout), scales fp32 ``[M]``/``[N]``.
+    """
+    device = _require_cuda(xq, scale_x, wq, scale_w, bias)
+    if xq.dtype != torch.int8 or wq.dtype != torch.int8:
+        raise ValueError("xq and wq must be int8")
+    m, k = xq.shape
+    n = wq.shape[0]
+    if wq.shape[1] != k or wq.stride(1) != 1 or xq.stride(1) != 1:
+        raise ValueError("xq and wq must be row-major [M, K] and [N, K]")
+    scale_x = scale_x.reshape(-1).to(torch.float32).contiguous()
+    scale_w = scale_w.reshape(-1).to(torch.float32).contiguous()
+    if bias is not None:
+        bias = bias.reshape(-1).to(out_dtype).contiguous()
+    out = torch.empty((m, n), device=device, dtype=out_dtype)
+    code = nat.lib().qtts_i8_gemm(
+        xq.data_ptr(), xq.stride(0) if m > 1 else k, scale_x.data_ptr(),
+        wq.data_ptr(), wq.stride(0), scale_w.data_ptr(),
+        bias.data_ptr() if bias is not None else None,
+        out.data_ptr(), n, nat.dtype_code(out_dtype), m, n, k, variant, _flags(), nat.stream_ptr(device),
+    )
+    nat.check(code, "qtts_i8_gemm")
+    return out
