@@ -451,6 +451,81 @@ def w8a8_sweep(device, seed: int) -> dict:
     }
 
 
+PROLOGUE_ROWS = (1, 8, 16, 64)
+
+
+def prologue_sweep(device, seed: int) -> dict:
+    """Fused activation prologues: the talker's input / post-attention RMSNorm feeding qkv /
+    gate_up, and SiLU·up feeding down_proj (qtts/models/talker.py:249, 271;
+    qtts/layers/activation.py:147), as one library call (qtts_w8a16_gemm_prologue) beside
+    the same prologue as torch ops ahead of the library's plain GEMM, at M in {1, 8, 16,
+    64}. Weights rotate through >= 256 MB per shape."""
+    import torch.nn.functional as F
+
+    from qtts_b200.quant import kernels as qk
+
+    gen = torch.Generator(device=device)
+    gen.manual_seed(seed + 17)
+    cases = [("rmsnorm+qkv", 4096, 2048, "rms"), ("rmsnorm+gate_up", 12288, 2048, "rms"),
+             ("silu_mul+down_proj", 2048, 6144, "silu")]
+    out: dict = {}
+    tot_fused = tot_torch = 0.0
+    for label, n, k, kind in cases:
+        p = pool_size(n, k)
+        qs = torch.empty((p, n, k), dtype=torch.int8, device=device)
+        ss = torch.empty((p, n), dtype=torch.bfloat16, device=device)
+        for i in range(p):
+            q, s_ = qk.quantize_int8_rows(torch.randn((n, k), generator=gen, device=device) * 0.02)
+            qs[i].copy_(q)
+            ss[i].copy_(s_.to(torch.bfloat16))
+            del q, s_
+        nw = (1 + 0.1 * torch.randn(k, generator=gen, device=device)).to(torch.bfloat16)
+        for m in PROLOGUE_ROWS:
+            width = k if kind == "rms" else 2 * k
+            x = torch.randn((m, width), generator=gen, device=device).to(torch.bfloat16)
+            if kind == "rms":
+                def fused(x=x):
+                    for c in range(CALLS_PER_GRAPH):
+                        qk.w8_gemm_rmsnorm(x, nw, 1e-6, qs[c % p], ss[c % p])
+
+                def torch_prologue(x=x):
+                    for c in range(CALLS_PER_GRAPH):
+                        qk.w8_gemm(F.rms_norm(x, (k,), nw, 1e-6), qs[c % p], ss[c % p])
+            else:
+                def fused(x=x):
+                    for c in range(CALLS_PER_GRAPH):
+                        qk.w8_gemm_silu_mul(x, qs[c % p], ss[c % p])
+
+                def torch_prologue(x=x):
+                    for c in range(CALLS_PER_GRAPH):
+                        gate, up = x.chunk(2, dim=-1)
+                        qk.w8_gemm(F.silu(gate) * up, qs[c % p], ss[c % p])
+            xa = x[:, :k].contiguous()
+
+            def gemm_only(xa=xa):
+                for c in range(CALLS_PER_GRAPH):
+                    qk.w8_gemm(xa, qs[c % p], ss[c % p])
+
+            us, us_t, us_g = graph_us_per_call(fused), graph_us_per_call(torch_prologue), graph_us_per_call(gemm_only)
+            out.setdefault(label, {})[str(m)] = {
+                "fused_us": round(us, 3),
+                "torch_prologue_us": round(us_t, 3),
+                "gemm_alone_us": round(us_g, 3),
+                "one_launch": qk.prologue_fused(m, n, k, 1 if kind == "rms" else 2),
+                "speedup": round(us_t / us, 3),
+            }
+            tot_fused += us
+            tot_torch += us_t
+        del qs, ss
+        torch.cuda.empty_cache()
+    return {
+        "workload": "RMSNorm -> qkv / gate_up and SiLU·up -> down_proj (talker shapes) at M in {1,8,16,64}: "
+        "one qtts_w8a16_gemm_prologue call vs the torch prologue + the library's GEMM, in CUDA graphs",
+        "speedup_overall": round(tot_torch / tot_fused, 3),
+        "per_point": out,
+    }
+
+
 def fp8w_sweep(device, seed: int) -> dict:
     """fp8 weight-only (e4m3 weights, bf16 activations, Fp8WeightOnlyMethod.apply) on the
     config-2 grid: the four talker shapes at M in {1..64}, weights rotating through
@@ -636,6 +711,18 @@ class FusedMathFp32:
             acc = acc + bias.float()
         return acc.to(x.dtype)
 
+    # The frame fuses its norms and SiLU·up into the int8 linears: the reference math
+    # takes the same prologues (the library's RMSNorm, torch's SiLU·up, equal to the
+    # library's), so only the GEMM arithmetic differs.
+    def apply_rmsnorm(self, layer, x, norm_weight, eps, bias):
+        from qtts_b200.quant import kernels as qk
+
+        return self.apply(layer, qk.rms_norm(x, norm_weight, eps), bias)
+
+    def apply_silu_mul(self, layer, gate_up, bias):
+        gate, up = gate_up.chunk(2, dim=-1)
+        return self.apply(layer, torch.nn.functional.silu(gate) * up, bias)
+
 
 def talker_frames(seed: int, batch: int = 8) -> dict:
     """Config 4: frames/s of the random-init talker decode step + code predictor at batch 8 in
@@ -643,7 +730,7 @@ def talker_frames(seed: int, batch: int = 8) -> dict:
     and int8 where calibration measures it faster (the reference's default); plus the codes
     of the all-int8 frame against the reference kernel's math in fp32 on the same weights."""
     from qtts_b200.config import QuantConfig
-    from qtts_b200.decode_step import Frame, timed_frames_per_s
+    from qtts_b200.decode_step import Block, Frame, timed_frames_per_s
     from qtts_b200.layers.linear import iter_linears
     from qtts_b200.quant import build_method, quantize_module
 
@@ -659,6 +746,14 @@ def talker_frames(seed: int, batch: int = 8) -> dict:
     torch.cuda.empty_cache()
     fps_int8, ms_int8 = timed_frames_per_s(frame)
     codes = frame.codes.clone()
+    # The same int8 frame with the norms and SiLU·up as separate torch ops.
+    Block.fuse_prologues = False
+    frame.graph = None
+    try:
+        fps_unfused, ms_unfused = timed_frames_per_s(frame)
+    finally:
+        Block.fuse_prologues = True
+        frame.graph = None
     # Same int8 weights through the reference kernel's math in fp32.
     layers = [layer for _, layer in iter_linears(frame.talker)] + [layer for _, layer in iter_linears(frame.predictor)]
     tf32 = torch.backends.cuda.matmul.allow_tf32
@@ -688,6 +783,8 @@ def talker_frames(seed: int, batch: int = 8) -> dict:
         "+ code predictor (5 layers, 15 sequential codebook steps, 15 heads) at batch 8, one CUDA graph per frame",
         "frames_per_s_int8": round(fps_int8, 1),
         "frames_per_s_bf16": round(fps_bf16, 1),
+        "frames_per_s_int8_torch_prologues": round(fps_unfused, 1),
+        "ms_per_step_int8_torch_prologues": round(ms_unfused, 3),
         "speedup_vs_bf16": round(fps_int8 / fps_bf16, 3),
         "ms_per_step_int8": round(ms_int8, 3),
         "ms_per_step_bf16": round(ms_bf16, 3),
@@ -845,6 +942,7 @@ def run_gpu_arm(args) -> None:
     fp8 = fp8_sweep(device, args.seed) if args.fp8 and rank == 0 else None
     fp8w = fp8w_sweep(device, args.seed) if args.fp8w and rank == 0 else None
     w8a8 = w8a8_sweep(device, args.seed) if args.w8a8 and rank == 0 else None
+    prologue = prologue_sweep(device, args.seed) if args.prologue and rank == 0 else None
     barrier(world)
     sharded = sharded_sweep(world, rank, device, args.seed) if args.sharded else None
     talker = talker_frames(args.seed) if args.talker and rank == 0 else None
@@ -929,6 +1027,7 @@ def run_gpu_arm(args) -> None:
             "fp8": fp8,
             "fp8_weight_only": fp8w,
             "int8_w8a8": w8a8,
+            "fused_prologues": prologue,
             "sharded": sharded,
             "talker": talker,
         }
@@ -1012,6 +1111,8 @@ def main(argv=None) -> int:
     ap.add_argument("--no-fp8", dest="fp8", action="store_false", help="skip the config-3 fp8 sweep")
     ap.add_argument("--no-fp8w", dest="fp8w", action="store_false", help="skip the fp8 weight-only sweep")
     ap.add_argument("--no-w8a8", dest="w8a8", action="store_false", help="skip the int8 W8A8 sweep")
+    ap.add_argument("--no-prologue", dest="prologue", action="store_false",
+                    help="skip the fused RMSNorm / SiLU·up sweep")
     ap.add_argument("--no-talker", dest="talker", action="store_false",
                     help="skip the config-4 talker + code predictor frames/s measurement")
     ap.add_argument("--no-sharded", dest="sharded", action="store_false",

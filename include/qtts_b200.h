@@ -164,6 +164,62 @@ QTTS_API int qtts_w8a16_grouped_gemm(const void* x, int64_t group_stride_x, int6
 QTTS_API int qtts_w8a16_plan(int M, int N, int K, int G, int variant, int* kernel, int* split, int* row_tile,
                              int* ctas);
 
+/* ---- activation prologues -------------------------------------------------
+ * RMSNorm and SiLU·up, standalone and fused into the W8A16 GEMM that consumes
+ * them (the decoder layer's input / post-attention norm feeding qkv_proj /
+ * gate_up_proj, qtts/models/talker.py:249, 271; SiLU·up between gate_up_proj
+ * and down_proj, qtts/layers/activation.py:147). Element arithmetic:
+ *   RMSNorm   y = cast( w[k] * (x[k] * inv) ),
+ *             inv = 1 / sqrt( sum_k x[k]^2 / width + eps )   (fp32; the sum
+ *             in the library's fixed order, identical in every form)
+ *   SiLU·up   y = cast( float(cast(g / (1 + exp(-g)))) * float(up) )
+ *             (each step rounded to the activation type, as torch's
+ *             F.silu(gate) * up) */
+#define QTTS_PROLOGUE_NONE 0
+#define QTTS_PROLOGUE_RMSNORM 1
+#define QTTS_PROLOGUE_SILU_MUL 2
+
+/* RMSNorm over the last dimension of x [rows, width] (leading dimension ldx)
+ * with weight [width], into out [rows, width] (ldo); dtype BF16, FP16 or
+ * FP32 for x, weight and out. out may be x (same ld): in place.
+ * Replaces: _rms_norm_kernel and RMSNorm.forward (qtts/layers/norm.py:49-76,
+ * 102-121; the reduction reaches the reference's eager form,
+ * norm.py:123-137, within one bf16 step, as the reference's own fused
+ * kernel does). */
+QTTS_API int qtts_rms_norm(const void* x, int64_t ldx, const void* weight, void* out, int64_t ldo, int dtype,
+                           int rows, int width, float eps, unsigned flags, void* stream);
+
+/* out [rows, width] = silu(gate) * up of gate_up [rows, 2*width] (leading
+ * dimension ld_in >= 2*width; gate = columns [0, width), up = [width,
+ * 2*width), MergedLinear.split order). out may be gate_up (ldo = ld_in).
+ * Replaces: F.silu(gate) * up in GatedMLP.forward (qtts/layers/activation.py:
+ * 143-147); equal bit for bit to torch's two CUDA kernels. */
+QTTS_API int qtts_silu_mul(const void* gate_up, int64_t ld_in, void* out, int64_t ldo, int dtype, int rows,
+                           int width, unsigned flags, void* stream);
+
+/* out = W8A16( prologue(x) ): qtts_w8a16_gemm on the RMSNorm of x [M, K]
+ * (norm_weight [K] of x_dtype, eps), or on SiLU·up of x [M, 2K] (ldx >= 2K;
+ * norm_weight and eps unused). Equal bit for bit to qtts_rms_norm /
+ * qtts_silu_mul followed by qtts_w8a16_gemm with the same variant. Where the
+ * chosen kernel is the split-K or whole-K streaming kernel (int8 weights,
+ * M <= 16, bf16/fp16 activations, 16-byte aligned rows and norm weight) the
+ * prologue runs inside it as the activations are staged: one launch. Otherwise
+ * the prologue kernel writes workspace [M, K] (x_dtype, leading dimension K,
+ * 16-byte aligned for the tensor-core kernels) and the GEMM, launched with
+ * programmatic dependent launch behind it, reads that; workspace may be NULL
+ * only when the call fuses (QTTS_ERR_NULL otherwise;
+ * qtts_w8a16_gemm_prologue_fused tells in advance). Other arguments as for
+ * qtts_w8a16_gemm. */
+QTTS_API int qtts_w8a16_gemm_prologue(const void* x, int64_t ldx, int x_dtype, int prologue,
+                                      const void* norm_weight, float eps, const int8_t* w, int64_t ldw,
+                                      const void* scale, int scale_dtype, const void* bias, void* out, int64_t ldo,
+                                      int M, int N, int K, void* workspace, int variant, unsigned flags,
+                                      void* stream);
+
+/* 1 when qtts_w8a16_gemm_prologue with this shape, prologue and variant runs
+ * as one fused launch (given aligned bf16/fp16 operands), else 0. Host-only. */
+QTTS_API int qtts_w8a16_gemm_prologue_fused(int M, int N, int K, int prologue, int variant);
+
 /* fp8 weight-only GEMM (no counterpart in the reference, which leaves
  * Fp8WeightOnlyMethod unimplemented, qtts/quant/fp8.py:92-122): the W8A16
  * contract with e4m3 weights,

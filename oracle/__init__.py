@@ -19,6 +19,7 @@ from .qtts_ref import (  # noqa: F401
     div_by_number,
     e4m3_decode,
     e4m3_encode,
+    float_steps,
     fp16_round,
     fp8_scaled_mm_reference,
     fp8_weight_only_reference,
@@ -30,6 +31,8 @@ from .qtts_ref import (  # noqa: F401
     quantize_weight_fp8,
     quantize_weight_per_channel,
     rel_err,
+    rms_norm_reference,
+    silu_mul_reference,
     tune_quantize,
     w8a16_reference,
 )

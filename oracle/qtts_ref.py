@@ -244,6 +244,51 @@ def int8_w8a8_reference(xq, scale_x, wq, scale_w, bias=None) -> np.ndarray:
     return y
 
 
+# ----------------------------------------------------------------------------
+# Activation prologues (RMSNorm before a projection, SiLU·up between the MLP's)
+
+
+def rms_norm_reference(x, weight, eps: float = 1e-6, dtype: str = "bf16") -> np.ndarray:
+    """qtts/layers/norm.py:123-137 (RMSNorm, eager form): ``weight * (x * rsqrt(mean(x^2) +
+    eps))``. Computed in float64, the value the reference's fp32 forms both approximate (its
+    own test takes the same float64 answer, tests/test_norm.py:29-32), then rounded to the
+    output dtype."""
+    x64 = np.asarray(x, dtype=np.float64)
+    w64 = np.asarray(weight, dtype=np.float64)
+    inv = 1.0 / np.sqrt((x64 * x64).mean(axis=-1, keepdims=True) + eps)
+    return round_to((w64 * (x64 * inv)).astype(np.float32), dtype)
+
+
+def float_steps(a, b, dtype: str) -> np.ndarray:
+    """How many representable values of ``dtype`` lie between ``a`` and ``b`` (both holding
+    values of that dtype): bit patterns mapped to integers in float order, as the
+    reference's norm test counts them (tests/test_norm.py:40-52)."""
+    def order(v):
+        v = np.asarray(v, dtype=np.float32)
+        if dtype == "bf16":
+            bits = (v.view(np.uint32) >> 16).astype(np.int64)
+            sign, mag = bits >> 15, bits & 0x7FFF
+        elif dtype == "fp16":
+            bits = v.astype(np.float16).view(np.uint16).astype(np.int64)
+            sign, mag = bits >> 15, bits & 0x7FFF
+        else:
+            bits = v.view(np.uint32).astype(np.int64)
+            sign, mag = bits >> 31, bits & 0x7FFFFFFF
+        return np.where(sign == 1, -mag, mag)
+    return np.abs(order(a) - order(b))
+
+
+def silu_mul_reference(gate, up, dtype: str = "bf16") -> np.ndarray:
+    """qtts/layers/activation.py:147 -- ``F.silu(gate) * up`` on tensors of ``dtype``:
+    silu in fp32 (``g / (1 + exp(-g))``) rounded to the dtype, then the product in fp32
+    rounded to the dtype (torch's two elementwise kernels)."""
+    g = np.asarray(gate, dtype=np.float32)
+    with np.errstate(over="ignore"):
+        s = (g / (np.float32(1.0) + np.exp(-g))).astype(np.float32)
+    s = round_to(s, dtype)
+    return round_to((s * np.asarray(up, dtype=np.float32)).astype(np.float32), dtype)
+
+
 def rel_err(out, ref) -> float:
     """examples/kernels/tune_w8_gemm.py:121 -- max|out - ref| / max|ref|."""
     out = np.asarray(out, dtype=np.float64)

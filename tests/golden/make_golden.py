@@ -23,7 +23,13 @@ records, on seeded CPU inputs:
   all-zero row, a row below the 1e-6 floor and a large row;
 * the byte/convert report of ``apply_quantization`` / ``quantize_module``
   (qtts/quant/base.py:74-113, 155-183) with int8 weight-only, calibration
-  off, on a small module tree with the reference's layer names.
+  off, on a small module tree with the reference's layer names;
+* ``RMSNorm`` (qtts/layers/norm.py:123-137, the eager form the CPU runs) on
+  bf16, fp16 and fp32 rows of the model's widths, including an all-zero row
+  and a tiny one (the eps floor);
+* the SwiGLU product ``F.silu(gate) * up`` of ``GatedMLP.forward``
+  (qtts/layers/activation.py:147) on bf16 and fp16 ``[gate | up]`` rows split
+  with ``MergedLinear.split`` (qtts/layers/linear.py:99-100).
 
 The reference is not needed afterwards: tests read only the files written
 here (``quant_golden.npz``, ``quantize_report.json``).
@@ -44,6 +50,7 @@ REF = Path(os.environ.get("QTTS_REFERENCE_DIR", "/root/reference"))
 sys.path.insert(0, str(REF))
 sys.path.insert(0, str(REF / "examples" / "kernels"))
 
+import qtts.layers.norm as ref_norm  # noqa: E402
 import qtts.quant.fp8 as ref_fp8  # noqa: E402
 import qtts.quant.int8 as ref_int8  # noqa: E402
 import tune_w8_gemm as ref_tune  # noqa: E402
@@ -157,6 +164,31 @@ def main() -> None:
             out[f"w8a8_y_{name}"] = f32(y)
     finally:
         torch._int_mm = real_int_mm
+
+    # -- RMSNorm (eager form) and SiLU·up --
+    gn = torch.Generator().manual_seed(11)
+    for name, dtype in (("bf16", torch.bfloat16), ("fp16", torch.float16), ("f32", torch.float32)):
+        for width in (128, 1024, 2048):
+            norm = ref_norm.RMSNorm(width, eps=1e-6, dtype=dtype, backend="eager")
+            norm.weight.data.copy_((1.0 + 0.1 * torch.randn(width, generator=gn)).to(dtype))
+            x = torch.randn(6, width, generator=gn) * 3.0
+            x[1] = 0.0
+            x[2] = x[2] * 1e-5
+            x[4] = x[4] * 200.0
+            x = x.to(dtype)
+            with torch.no_grad():
+                y = norm(x)
+            out[f"rms_x_{name}_{width}"] = f32(x)
+            out[f"rms_w_{name}_{width}"] = f32(norm.weight)
+            out[f"rms_y_{name}_{width}"] = f32(y)
+    merged = MergedLinear(8, [384, 384], bias=False, dtype=torch.float32)
+    for name, dtype in (("bf16", torch.bfloat16), ("fp16", torch.float16)):
+        gate_up = (torch.randn(5, 768, generator=gn) * 4.0).to(dtype)
+        gate_up[0, :8] = torch.tensor([0.0, -0.0, 20.0, -20.0, 90.0, -90.0, 1e-3, -1e-3]).to(dtype)
+        gate, up = merged.split(gate_up)
+        y = torch.nn.functional.silu(gate) * up
+        out[f"silu_gate_up_{name}"] = f32(gate_up)
+        out[f"silu_y_{name}"] = f32(y)
 
     np.savez_compressed(HERE / "quant_golden.npz", **out)
 

@@ -4,7 +4,10 @@ North-star parity for the model: the greedy codebook-0 ids of the random-init
 talker step with the library's kernels equal those of the reference int8
 kernel's math (exact int8 weight, fp32 accumulation, scale after the K loop,
 qtts/quant/kernels.py:114-135) run in torch fp32 on the same int8 weights; and
-the CUDA graph of a frame replays the eager frame exactly.
+the CUDA graph of a frame replays the eager frame exactly. Both with the
+norms and SiLU·up as separate torch ops and with them fused into the int8
+linears (the reference-math side then takes the same norm, from the
+library's standalone kernel, so only the GEMM arithmetic differs).
 """
 
 from __future__ import annotations
@@ -16,7 +19,9 @@ from conftest import require_b200
 from qtts_b200.config import QuantConfig
 from qtts_b200.decode_step import Frame
 from qtts_b200.layers.linear import iter_linears
+from qtts_b200.decode_step import Block
 from qtts_b200.quant import build_method, quantize_module
+from qtts_b200.quant import kernels as qk
 
 pytestmark = pytest.mark.gpu
 
@@ -29,6 +34,26 @@ class FusedMathFp32:
         if bias is not None:
             acc = acc + bias.float()
         return acc.to(x.dtype)
+
+
+class FusedMathFp32Prologues(FusedMathFp32):
+    """The same GEMM math behind the fused-prologue hooks: the library's RMSNorm kernel
+    (the one the int8 GEMMs fuse) and torch's SiLU·up (equal to the library's)."""
+
+    def apply_rmsnorm(self, layer, x, norm_weight, eps, bias):
+        return self.apply(layer, qk.rms_norm(x, norm_weight, eps), bias)
+
+    def apply_silu_mul(self, layer, gate_up, bias):
+        gate, up = gate_up.chunk(2, dim=-1)
+        return self.apply(layer, torch.nn.functional.silu(gate) * up, bias)
+
+
+@pytest.fixture(params=[True, False], ids=["fused_prologues", "torch_prologues"])
+def fuse(request):
+    saved = Block.fuse_prologues
+    Block.fuse_prologues = request.param
+    yield request.param
+    Block.fuse_prologues = saved
 
 
 @pytest.fixture(scope="module")
@@ -45,13 +70,14 @@ def frame():
     return f
 
 
-def test_code0_matches_reference_math(frame):
+def test_code0_matches_reference_math(frame, fuse):
     ours = frame.run().clone()
     layers = [l for _, l in iter_linears(frame.talker)] + [l for _, l in iter_linears(frame.predictor)]
     tf32 = torch.backends.cuda.matmul.allow_tf32
     torch.backends.cuda.matmul.allow_tf32 = False
+    ref_method = FusedMathFp32Prologues() if fuse else FusedMathFp32()
     for layer in layers:
-        layer.quant_method = FusedMathFp32()
+        layer.quant_method = ref_method
     try:
         ref = frame.run().clone()
     finally:
@@ -63,7 +89,7 @@ def test_code0_matches_reference_math(frame):
     # summation order of two fp32 GEMMs decides near-ties; they are not compared.
 
 
-def test_graph_replay_equals_eager(frame):
+def test_graph_replay_equals_eager(frame, fuse):
     eager = frame.run().clone()
     frame.capture()
     frame.codes.zero_()

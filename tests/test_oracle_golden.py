@@ -143,3 +143,32 @@ def test_int8_w8a8_matches_reference(golden, dtype):
     bias = oracle.round_to(golden["w8a8_bias"], dtype)
     y = oracle.round_to(oracle.int8_w8a8_reference(q, sx, wq, ws, bias), dtype)
     np.testing.assert_array_equal(y, golden[f"w8a8_y_{name}"])
+
+
+@pytest.mark.parametrize("dtype", ["bf16", "fp16", "f32"])
+@pytest.mark.parametrize("width", [128, 1024, 2048])
+def test_rms_norm_matches_reference(golden, dtype, width):
+    """RMSNorm through the oracle (float64, rounded once) against the reference's eager
+    RMSNorm run on the CPU: within one representable step for 16-bit outputs (the bar the
+    reference sets for its own fused kernel, tests/test_norm.py:55-72) and within a few
+    ULP in fp32 (its fp32 bar), including an all-zero row and a row under the eps floor."""
+    x, w, y = golden[f"rms_x_{dtype}_{width}"], golden[f"rms_w_{dtype}_{width}"], golden[f"rms_y_{dtype}_{width}"]
+    ref = oracle.rms_norm_reference(x, w, 1e-6, dtype)
+    steps = oracle.float_steps(ref, y, dtype)
+    assert steps.max() <= (1 if dtype != "f32" else 4), f"{steps.max()} steps"
+    assert np.all(y[1] == 0) and np.all(ref[1] == 0)
+
+
+@pytest.mark.parametrize("dtype", ["bf16", "fp16"])
+def test_silu_mul_matches_reference(golden, dtype):
+    """F.silu(gate) * up through the oracle against the reference's expression run on the
+    CPU, bit for bit, including zeros, saturating gates and tiny gates."""
+    gu, y = golden[f"silu_gate_up_{dtype}"], golden[f"silu_y_{dtype}"]
+    w = gu.shape[1] // 2
+    np.testing.assert_array_equal(oracle.silu_mul_reference(gu[:, :w], gu[:, w:], dtype), y)
+
+
+def test_float_steps_counts_representable_values():
+    a = np.array([1.0, -1.0, 0.0, 1.0], dtype=np.float32)
+    b = oracle.bf16_round(np.array([1.0078125, -1.0078125, -0.0, 1.0], dtype=np.float32))
+    np.testing.assert_array_equal(oracle.float_steps(a, b, "bf16"), [1, 1, 0, 0])

@@ -58,3 +58,19 @@ def test_every_split_owns_part_of_k():
                 sw = 128 * (128 // p["row_tile"])  # k per stage: 8 warps / (row tile / 16) k groups
                 kpc = -(-(-(-k // p["split"])) // sw) * sw
                 assert (p["split"] - 1) * kpc < k, (n, k, m, p)
+
+
+@pytest.mark.parametrize("m", [1, 2, 4, 8, 16, 17, 64])
+def test_prologue_fuses_where_the_kernel_stages_activations(m):
+    """RMSNorm / SiLU·up run inside the GEMM exactly when the chosen kernel is one of the
+    two streaming kernels (int8, up to 16 rows); past that the prologue kernel is chained."""
+    lib = nat.lib()
+    for n, k in ((4096, 2048), (12288, 2048), (2048, 6144), (3072, 1024)):
+        for pro in (nat.PROLOGUE_RMSNORM, nat.PROLOGUE_SILU_MUL):
+            fused = lib.qtts_w8a16_gemm_prologue_fused(m, n, k, pro, nat.VARIANT_AUTO)
+            kernel = nat.plan(m, n, k)["kernel"]
+            assert fused == (kernel in ("skinny_w8a16_kernel", "stream_w8a16_kernel")), (n, k, m)
+            assert fused == (m <= 16)
+    assert lib.qtts_w8a16_gemm_prologue_fused(8, 4096, 2048, nat.PROLOGUE_RMSNORM, nat.variant_umma(1)) == 0
+    assert lib.qtts_w8a16_gemm_prologue_fused(8, 4096, 2048, nat.PROLOGUE_RMSNORM, nat.variant_skinny(2)) == 1
+    assert lib.qtts_w8a16_gemm_prologue_fused(8, 4096, 2048, 0, nat.VARIANT_AUTO) == 0

@@ -9,6 +9,7 @@
 
 #include "common.cuh"
 #include "kernels.h"
+#include "prologue.cuh"
 
 namespace qtts {
 
@@ -500,11 +501,24 @@ static int auto_family(int M, int N, int K, int zg, int w_fmt, bool allgather, i
   return family;
 }
 
+// A prologue fused into the skinny or whole-K kernel (qtts_w8a16_gemm_prologue).
+struct FusedPrologue {
+  int kind;
+  const void* weight;
+  float eps;
+};
+
+static void set_prologue(SkinnyArgs& sa, const FusedPrologue* pro) {
+  sa.prologue = pro != nullptr ? pro->kind : kProNone;
+  sa.pro_weight = pro != nullptr ? pro->weight : nullptr;
+  sa.pro_eps = pro != nullptr ? pro->eps : 0.f;
+}
+
 static int w8a16_dispatch(const void* x, int64_t gsx, int64_t ldx, int x_dtype, const int8_t* w, int64_t ldw,
                           const void* scale, int scale_dtype, const void* bias, void* out, int64_t gso,
                           int64_t ldo, int G, int M, int N, int K, const int64_t* group_index, int variant,
                           unsigned flags, void* stream_ptr, int w_fmt = kWInt8,
-                          const AllGatherForm* ag = nullptr) {
+                          const AllGatherForm* ag = nullptr, const FusedPrologue* pro = nullptr) {
   if (M < 0 || N < 0 || K < 0 || G < 1) return QTTS_ERR_SHAPE;
   if (ag != nullptr && N == 0) return QTTS_ERR_SHAPE;  // every rank takes part in the exchange
   if (M == 0 || N == 0) return QTTS_OK;
@@ -533,6 +547,10 @@ static int w8a16_dispatch(const void* x, int64_t gsx, int64_t ldx, int x_dtype, 
     // The all-gather epilogue lives in the split-K and tcgen05 kernels.
     return skinny_ok ? QTTS_ERR_VARIANT : QTTS_ERR_ALIGN;
   }
+  // Fused prologues live in the skinny and whole-K kernels (int8, M <= 16);
+  // the caller has checked that the call lands there.
+  if (pro != nullptr && !(skinny_ok && w_fmt == kWInt8 && M <= 16 && (family == 0x100 || family == 0x300)))
+    return QTTS_ERR_VARIANT;
   if (variant == QTTS_VARIANT_GENERIC || family == 0) {
     if (variant != QTTS_VARIANT_AUTO && variant != QTTS_VARIANT_GENERIC) return QTTS_ERR_VARIANT;
     GenericArgs ga{x, ldx, gsx, w, ldw, scale, scale_dtype, bias, out, ldo, gso, M, N, K, G, group_index, w_fmt};
@@ -574,6 +592,7 @@ static int w8a16_dispatch(const void* x, int64_t gsx, int64_t ldx, int x_dtype, 
     sa.group_index = group_index;
     sa.w_fmt = w_fmt;
     set_allgather(sa, ag);
+    set_prologue(sa, pro);
     sa.wait_ns = current_wait_limit_ns();
     sa.trace_slot = -1;
 #ifdef QTTS_TRACE
@@ -617,6 +636,7 @@ static int w8a16_dispatch(const void* x, int64_t gsx, int64_t ldx, int x_dtype, 
     sa.group_index = group_index;
     sa.w_fmt = w_fmt;
     set_allgather(sa, ag);
+    set_prologue(sa, pro);
     sa.wait_ns = current_wait_limit_ns();
     sa.trace_slot = -1;
 #ifdef QTTS_TRACE
@@ -663,6 +683,7 @@ static int w8a16_dispatch(const void* x, int64_t gsx, int64_t ldx, int x_dtype, 
     sa.group_index = group_index;
     sa.w_fmt = w_fmt;
     set_allgather(sa, ag);
+    set_prologue(sa, pro);
     sa.wait_ns = current_wait_limit_ns();
     sa.trace_slot = -1;
 #ifdef QTTS_TRACE
@@ -686,6 +707,129 @@ int qtts_fp8w_gemm(const void* x, int64_t ldx, int x_dtype, const uint8_t* w, in
                    unsigned flags, void* stream) {
   return w8a16_dispatch(x, 0, ldx, x_dtype, reinterpret_cast<const int8_t*>(w), ldw, scale, scale_dtype, bias, out,
                         0, ldo, 1, M, N, K, nullptr, variant, flags, stream, kWE4M3);
+}
+
+// ---- activation prologues ------------------------------------------------------------
+
+int qtts_rms_norm(const void* x, int64_t ldx, const void* weight, void* out, int64_t ldo, int dtype, int rows,
+                  int width, float eps, unsigned flags, void* stream) {
+  if (rows < 0 || width < 0) return QTTS_ERR_SHAPE;
+  if (rows == 0 || width == 0) return QTTS_OK;
+  if (x == nullptr || weight == nullptr || out == nullptr) return QTTS_ERR_NULL;
+  if (!is_float_dtype(dtype)) return QTTS_ERR_DTYPE;
+  if (ldx < width || ldo < width) return QTTS_ERR_SHAPE;
+  const int dev_ok = check_device();
+  if (dev_ok != QTTS_OK) return dev_ok;
+  const size_t sz = dtype_size(dtype);
+  PrologueArgs pa{};
+  pa.kind = kProRmsNorm;
+  pa.x = x;
+  pa.ldx = ldx;
+  pa.weight = weight;
+  pa.eps = eps;
+  pa.out = out;
+  pa.ldo = ldo;
+  pa.rows = rows;
+  pa.width = width;
+  pa.vec = width % 8 == 0 && aligned16(x) && aligned16(weight) && aligned16(out) && (ldx * sz) % 16 == 0 &&
+           (ldo * sz) % 16 == 0;
+  return launch_prologue(pa, dtype, (flags & QTTS_FLAG_PDL) != 0, static_cast<cudaStream_t>(stream));
+}
+
+int qtts_silu_mul(const void* gate_up, int64_t ld_in, void* out, int64_t ldo, int dtype, int rows, int width,
+                  unsigned flags, void* stream) {
+  if (rows < 0 || width < 0) return QTTS_ERR_SHAPE;
+  if (rows == 0 || width == 0) return QTTS_OK;
+  if (gate_up == nullptr || out == nullptr) return QTTS_ERR_NULL;
+  if (!is_float_dtype(dtype)) return QTTS_ERR_DTYPE;
+  if (ld_in < 2 * static_cast<int64_t>(width) || ldo < width) return QTTS_ERR_SHAPE;
+  const int dev_ok = check_device();
+  if (dev_ok != QTTS_OK) return dev_ok;
+  const size_t sz = dtype_size(dtype);
+  PrologueArgs pa{};
+  pa.kind = kProSiluMul;
+  pa.x = gate_up;
+  pa.ldx = ld_in;
+  pa.out = out;
+  pa.ldo = ldo;
+  pa.rows = rows;
+  pa.width = width;
+  pa.vec = width % 8 == 0 && aligned16(gate_up) && aligned16(out) && (ld_in * sz) % 16 == 0 && (ldo * sz) % 16 == 0;
+  return launch_prologue(pa, dtype, (flags & QTTS_FLAG_PDL) != 0, static_cast<cudaStream_t>(stream));
+}
+
+// Which kernel family the call lands on (the same choice w8a16_dispatch makes).
+static int chosen_family(const void* x, int64_t ldx, int x_dtype, const int8_t* w, int64_t ldw, int M, int N, int K,
+                         int variant) {
+  const size_t xs = dtype_size(x_dtype);
+  const bool skinny_ok = (x_dtype == QTTS_BF16 || x_dtype == QTTS_FP16) && K % 16 == 0 && K > 0 && aligned16(x) &&
+                         aligned16(w) && (ldx * xs) % 16 == 0 && ldw % 16 == 0;
+  if (variant == QTTS_VARIANT_GENERIC) return 0;
+  if (variant != QTTS_VARIANT_AUTO) return skinny_ok ? (variant & 0xF00) : -1;
+  int rgroups = 0;
+  return skinny_ok ? auto_family(M, N, K, 1, kWInt8, false, &rgroups) : 0;
+}
+
+int qtts_w8a16_gemm_prologue(const void* x, int64_t ldx, int x_dtype, int prologue, const void* norm_weight,
+                             float eps, const int8_t* w, int64_t ldw, const void* scale, int scale_dtype,
+                             const void* bias, void* out, int64_t ldo, int M, int N, int K, void* workspace,
+                             int variant, unsigned flags, void* stream) {
+  if (prologue == QTTS_PROLOGUE_NONE) {
+    return w8a16_dispatch(x, 0, ldx, x_dtype, w, ldw, scale, scale_dtype, bias, out, 0, ldo, 1, M, N, K, nullptr,
+                          variant, flags, stream);
+  }
+  if (prologue != QTTS_PROLOGUE_RMSNORM && prologue != QTTS_PROLOGUE_SILU_MUL) return QTTS_ERR_VARIANT;
+  if (M < 0 || N < 0 || K < 0) return QTTS_ERR_SHAPE;
+  if (M == 0 || N == 0) return QTTS_OK;
+  if (x == nullptr || w == nullptr || scale == nullptr || out == nullptr) return QTTS_ERR_NULL;
+  if (prologue == QTTS_PROLOGUE_RMSNORM && norm_weight == nullptr) return QTTS_ERR_NULL;
+  if (!is_float_dtype(x_dtype) || !is_float_dtype(scale_dtype)) return QTTS_ERR_DTYPE;
+  const int64_t x_width = prologue == QTTS_PROLOGUE_SILU_MUL ? 2 * static_cast<int64_t>(K) : K;
+  if (ldx < x_width || ldw < K || ldo < N) return QTTS_ERR_SHAPE;
+  const int family = chosen_family(x, ldx, x_dtype, w, ldw, M, N, K, variant);
+  if (family < 0) return QTTS_ERR_ALIGN;
+  const bool fusable = M <= 16 && (family == 0x100 || family == 0x300) &&
+                       (prologue != QTTS_PROLOGUE_RMSNORM || aligned16(norm_weight));
+  if (fusable) {
+    const FusedPrologue pro{prologue == QTTS_PROLOGUE_RMSNORM ? kProRmsNorm : kProSiluMul, norm_weight, eps};
+    return w8a16_dispatch(x, 0, ldx, x_dtype, w, ldw, scale, scale_dtype, bias, out, 0, ldo, 1, M, N, K, nullptr,
+                          variant, flags, stream, kWInt8, nullptr, &pro);
+  }
+  // Two launches: the prologue writes the activation into the workspace
+  // [M, K] (leading dimension K), then the GEMM reads it. The GEMM launches
+  // with programmatic dependent launch behind the prologue kernel, which
+  // writes no weights.
+  if (workspace == nullptr) return QTTS_ERR_NULL;
+  const int dev_ok = check_device();
+  if (dev_ok != QTTS_OK) return dev_ok;
+  const size_t sz = dtype_size(x_dtype);
+  PrologueArgs pa{};
+  pa.kind = prologue == QTTS_PROLOGUE_RMSNORM ? kProRmsNorm : kProSiluMul;
+  pa.x = x;
+  pa.ldx = ldx;
+  pa.weight = norm_weight;
+  pa.eps = eps;
+  pa.out = workspace;
+  pa.ldo = K;
+  pa.rows = M;
+  pa.width = K;
+  pa.vec = K % 8 == 0 && aligned16(x) && aligned16(workspace) && (ldx * sz) % 16 == 0 && (K * sz) % 16 == 0 &&
+           (pa.kind != kProRmsNorm || aligned16(norm_weight));
+  const int r = launch_prologue(pa, x_dtype, (flags & QTTS_FLAG_PDL) != 0, static_cast<cudaStream_t>(stream));
+  if (r != QTTS_OK) return r;
+  return w8a16_dispatch(workspace, 0, K, x_dtype, w, ldw, scale, scale_dtype, bias, out, 0, ldo, 1, M, N, K, nullptr,
+                        variant, flags | QTTS_FLAG_PDL, stream);
+}
+
+int qtts_w8a16_gemm_prologue_fused(int M, int N, int K, int prologue, int variant) {
+  if (M < 1 || N < 1 || K < 16 || K % 16 != 0) return 0;
+  if (prologue != QTTS_PROLOGUE_RMSNORM && prologue != QTTS_PROLOGUE_SILU_MUL) return 0;
+  int family = variant & 0xF00;
+  if (variant == QTTS_VARIANT_AUTO) {
+    int rgroups = 0;
+    family = auto_family(M, N, K, 1, kWInt8, false, &rgroups);
+  }
+  return (M <= 16 && (family == 0x100 || family == 0x300)) ? 1 : 0;
 }
 
 int qtts_w8a16_plan(int M, int N, int K, int G, int variant, int* kernel, int* split, int* row_tile, int* ctas) {

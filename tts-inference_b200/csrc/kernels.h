@@ -45,6 +45,12 @@ struct SkinnyArgs {
   int64_t col_offset;         // gathered column of this rank's first output channel
   int rank;
   int world;
+  // Fused activation prologue (qtts_w8a16_gemm_prologue, csrc/prologue.cuh):
+  // kProNone, kProRmsNorm (pro_weight = the norm weight [K] of the activation
+  // type, pro_eps) or kProSiluMul (x rows are [gate | up], 2*K wide).
+  int prologue;
+  const void* pro_weight;
+  float pro_eps;
 };
 
 constexpr int kWInt8 = 0;  // int8 weights (W8A16)
@@ -104,6 +110,20 @@ Fp8Plan plan_fp8(int M, int N, int K, int split_req);
 // int8 = true: the int8 W8A8 form (signed int8 operands, int32 accumulator).
 int launch_fp8_gemm(const Fp8Plan& p, const CUtensorMap& wmap, const CUtensorMap& xmap, const Fp8Args& args,
                     int out_dtype, bool pdl, cudaStream_t stream, bool int8 = false);
+
+// ---- standalone activation prologues (csrc/prologue.cu) ------------------------
+struct PrologueArgs {
+  int kind;  // kProRmsNorm or kProSiluMul
+  const void* x;
+  int64_t ldx;
+  const void* weight;  // RMSNorm weight [width], of the activation type
+  float eps;
+  void* out;
+  int64_t ldo;
+  int rows, width;
+  bool vec;  // 16-byte aligned rows and width % 8 == 0: vector loads and stores
+};
+int launch_prologue(const PrologueArgs& p, int dtype, bool pdl, cudaStream_t stream);
 
 // ---- tensor maps ---------------------------------------------------------------
 // 2-D uint8 tensor map over a row-major [rows, cols] byte matrix with row pitch

@@ -38,6 +38,10 @@
 //     (arrive at start, wait before the first remote store) plus one closing
 //     phase, so that a cluster's CTAs leave together, are the only
 //     cluster-wide synchronization.
+//   * Optional activation prologue (template PRO, csrc/prologue.cuh): RMSNorm
+//     of the raw rows (one warp per row forms the row's factor over the whole
+//     of K, in the library's fixed order, before the slice is staged) or
+//     SiLU·up of [gate | up] rows, applied to each chunk as it is staged.
 //   * Every wait is bounded (globaltimer). On expiry the kernel records
 //     QTTS_ERR_TIMEOUT in the device status word, keeps the remote-store
 //     protocol (so no peer waits on it), skips its global stores and drains its
@@ -45,6 +49,7 @@
 #include "allgather.cuh"
 #include "common.cuh"
 #include "kernels.h"
+#include "prologue.cuh"
 
 namespace qtts {
 
@@ -54,7 +59,7 @@ constexpr int kSkThreads = (kSkConsumerWarps + 1) * 32;
 
 __device__ __forceinline__ float pow2f(int e) { return __int_as_float((e + 127) << 23); }
 
-template <int MT, int R, typename XT, bool E4M3 = false, bool AG = false>
+template <int MT, int R, typename XT, bool E4M3 = false, bool AG = false, int PRO = kProNone>
 __global__ void __launch_bounds__(kSkThreads, 2)
     skinny_w8a16_kernel(const __grid_constant__ CUtensorMap wmap, const SkinnyArgs a) {
   constexpr int MB = MT * 8;       // batch rows per CTA (MMA N dimension)
@@ -67,7 +72,8 @@ __global__ void __launch_bounds__(kSkThreads, 2)
   uint8_t* wbuf = smem;
   __half* xs = reinterpret_cast<__half*>(smem + a.stages * kSkStageBytes);  // [MB][x_pitch]
   float* xinv = reinterpret_cast<float*>(xs + MB * a.x_pitch);               // [MB] 2^-scale
-  float* recv = xinv + MB;                                                   // [S][BN/S][MB]
+  float* rinv = xinv + MB;                                                   // [MB] RMSNorm factors
+  float* recv = rinv + MB;                                                   // [S][BN/S][MB]
   const int split = gridDim.y;
   uint64_t* full = reinterpret_cast<uint64_t*>(
       (reinterpret_cast<uintptr_t>(recv + (split > 1 ? BN * MB : 0)) + 15) & ~uintptr_t(15));
@@ -173,6 +179,17 @@ __global__ void __launch_bounds__(kSkThreads, 2)
     }
 #endif
     const int kpad = n_iters * SW;
+    const XT* wnorm = static_cast<const XT*>(a.pro_weight);
+    if constexpr (PRO == kProRmsNorm) {
+      // The norm's factor needs the whole row, not only this CTA's slice.
+      if (valid) {
+        for (int m = warp; m < mrows; m += kSkConsumerWarps) {
+          const float ss = warp_row_sumsq<XT>(xg + static_cast<int64_t>(m) * a.ldx, a.K, true, lane);
+          if (lane == 0) rinv[m] = rms_inv(ss, a.K, a.pro_eps);
+        }
+      }
+      named_bar_sync(1, kSkConsumerWarps * 32);
+    }
     // 1) Activation slice [MB, kpad]: each thread loads 16-byte chunks into
     //    registers (zeros past K and past the last batch row), the per-row
     //    maximum is combined with shared-memory atomics, then every thread
@@ -192,7 +209,8 @@ __global__ void __launch_bounds__(kSkThreads, 2)
         const int kv = (ci - m * cpr) * 8;
         uint4 u = make_uint4(0u, 0u, 0u, 0u);
         if (valid && m < mrows && kv < klen) {
-          u = __ldcg(reinterpret_cast<const uint4*>(xg + static_cast<int64_t>(m) * a.ldx + k0 + kv));
+          u = prologue_chunk<XT, PRO>(xg + static_cast<int64_t>(m) * a.ldx, k0 + kv, a.K, wnorm,
+                                      PRO == kProRmsNorm ? rinv[m] : 0.f);
         }
         const XT* e = reinterpret_cast<const XT*>(&u);
         float mx = 0.f;
@@ -493,10 +511,10 @@ __global__ void __launch_bounds__(kSkThreads, 2)
 
 namespace {
 
-template <int MT, int R, typename XT, bool E4M3, bool AG>
+template <int MT, int R, typename XT, bool E4M3, bool AG, int PRO>
 int launch_skinny_t(const CUtensorMap& map, const SkinnyArgs& args, dim3 grid, int split, size_t smem,
                     bool pdl, cudaStream_t stream) {
-  auto kern = skinny_w8a16_kernel<MT, R, XT, E4M3, AG>;
+  auto kern = skinny_w8a16_kernel<MT, R, XT, E4M3, AG, PRO>;
   static int configured[64] = {0};
   int dev = 0;
   cudaGetDevice(&dev);
@@ -531,18 +549,18 @@ int launch_skinny_t(const CUtensorMap& map, const SkinnyArgs& args, dim3 grid, i
   return e == cudaSuccess ? QTTS_OK : QTTS_ERR_LAUNCH;
 }
 
-template <int MT, typename XT, bool E4M3, bool AG = false>
+template <int MT, typename XT, bool E4M3, bool AG = false, int PRO = kProNone>
 int launch_skinny_r(int r, const CUtensorMap& map, const SkinnyArgs& args, dim3 grid, int split, size_t smem,
                     bool pdl, cudaStream_t stream) {
   switch (r) {
     case 1:
-      return launch_skinny_t<MT, 1, XT, E4M3, AG>(map, args, grid, split, smem, pdl, stream);
+      return launch_skinny_t<MT, 1, XT, E4M3, AG, PRO>(map, args, grid, split, smem, pdl, stream);
     case 2:
-      return launch_skinny_t<MT, 2, XT, E4M3, AG>(map, args, grid, split, smem, pdl, stream);
+      return launch_skinny_t<MT, 2, XT, E4M3, AG, PRO>(map, args, grid, split, smem, pdl, stream);
     case 4:
-      return launch_skinny_t<MT, 4, XT, E4M3, AG>(map, args, grid, split, smem, pdl, stream);
+      return launch_skinny_t<MT, 4, XT, E4M3, AG, PRO>(map, args, grid, split, smem, pdl, stream);
     default:
-      return launch_skinny_t<MT, 8, XT, E4M3, AG>(map, args, grid, split, smem, pdl, stream);
+      return launch_skinny_t<MT, 8, XT, E4M3, AG, PRO>(map, args, grid, split, smem, pdl, stream);
   }
 }
 
@@ -555,6 +573,20 @@ int launch_skinny_mt(const SkinnyPlan& p, const CUtensorMap& map, const SkinnyAr
     if (p.mt == 1) return launch_skinny_r<1, XT, false, true>(p.r, map, args, p.grid, p.split, p.smem, pdl, stream);
     if (p.mt == 2) return launch_skinny_r<2, XT, false, true>(p.r, map, args, p.grid, p.split, p.smem, pdl, stream);
     return QTTS_ERR_VARIANT;
+  }
+  if (args.prologue != kProNone) {
+    // Fused prologues: int8 weights, up to 16 rows (AUTO's range for this kernel).
+    if (args.w_fmt != kWInt8 || p.mt > 2) return QTTS_ERR_VARIANT;
+    if (args.prologue == kProRmsNorm) {
+      return p.mt == 1 ? launch_skinny_r<1, XT, false, false, kProRmsNorm>(p.r, map, args, p.grid, p.split, p.smem,
+                                                                           pdl, stream)
+                       : launch_skinny_r<2, XT, false, false, kProRmsNorm>(p.r, map, args, p.grid, p.split, p.smem,
+                                                                           pdl, stream);
+    }
+    return p.mt == 1 ? launch_skinny_r<1, XT, false, false, kProSiluMul>(p.r, map, args, p.grid, p.split, p.smem, pdl,
+                                                                         stream)
+                     : launch_skinny_r<2, XT, false, false, kProSiluMul>(p.r, map, args, p.grid, p.split, p.smem, pdl,
+                                                                         stream);
   }
   if (args.w_fmt == kWE4M3) {
     // fp8 weight-only takes this kernel up to 16 rows only.
@@ -575,7 +607,7 @@ int launch_skinny_mt(const SkinnyPlan& p, const CUtensorMap& map, const SkinnyAr
 }
 
 size_t skinny_smem(int mb, int bn, int x_pitch, int stages, int split) {
-  const size_t xbytes = static_cast<size_t>(mb) * x_pitch * 2 + mb * 4;
+  const size_t xbytes = static_cast<size_t>(mb) * x_pitch * 2 + mb * 8;  // + row scales, norm factors
   const size_t recv = split > 1 ? static_cast<size_t>(bn) * mb * 4 : 0;
   return 1024 + static_cast<size_t>(stages) * kSkStageBytes + xbytes + recv + 16 + 16 * stages + 48;
 }

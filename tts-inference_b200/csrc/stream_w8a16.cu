@@ -30,10 +30,14 @@
 //     per-row power of two (exact for every element within 2^28 of the row's
 //     largest magnitude), with warp-level reductions before the few shared
 //     atomics.
+//   * Optional activation prologue (template PRO, csrc/prologue.cuh): RMSNorm
+//     (row factors formed first, one warp per row) or SiLU·up of [gate | up]
+//     rows, applied to each chunk as it is loaded.
 //   * Every wait is bounded (globaltimer); on expiry the kernel records
 //     QTTS_ERR_TIMEOUT, skips its stores and drains its own copies in flight.
 #include "common.cuh"
 #include "kernels.h"
+#include "prologue.cuh"
 
 namespace qtts {
 
@@ -112,7 +116,7 @@ __device__ __forceinline__ float convert_x_chunk(const uint4& u, unsigned row_ma
 
 }  // namespace
 
-template <int MT, int R, typename XT>
+template <int MT, int R, typename XT, int PRO = kProNone>
 __global__ void __launch_bounds__(kStThreads, 2)
     stream_w8a16_kernel(const __grid_constant__ CUtensorMap wmap, const SkinnyArgs a) {
   constexpr int KG = kStConsumerWarps / R;  // k groups
@@ -130,8 +134,9 @@ __global__ void __launch_bounds__(kStThreads, 2)
   __half* xs = reinterpret_cast<__half*>(smem + a.stages * kStStageBytes);  // [xrows][x_pitch]
   float* xpart = reinterpret_cast<float*>(xs + xrows * a.x_pitch);  // [warp][MB] partial row sums
   unsigned* xmax = reinterpret_cast<unsigned*>(xpart + kStConsumerWarps * MB);  // [MB] float bits
+  float* rinv = reinterpret_cast<float*>(xmax + MB);                             // [MB] RMSNorm factors
   uint64_t* full = reinterpret_cast<uint64_t*>(
-      (reinterpret_cast<uintptr_t>(xmax + MB) + 15) & ~uintptr_t(15));
+      (reinterpret_cast<uintptr_t>(rinv + MB) + 15) & ~uintptr_t(15));
   uint64_t* empty = full + a.stages;
   int* err_flag = reinterpret_cast<int*>(empty + a.stages);
   float* red = reinterpret_cast<float*>(wbuf);  // [KG][BN][MB], reuses the ring after the loop
@@ -221,6 +226,17 @@ __global__ void __launch_bounds__(kStThreads, 2)
     constexpr int kBatch = 4;
     const bool in_regs = nj <= kBatch;
     uint4 held[kBatch];
+    const XT* wnorm = static_cast<const XT*>(a.pro_weight);
+    if constexpr (PRO == kProRmsNorm) {
+      // The norm's factor of each real row, before any chunk is staged.
+      if (valid) {
+        for (int m = warp; m < mrows; m += kStConsumerWarps) {
+          const float ss = warp_row_sumsq<XT>(xg + static_cast<int64_t>(m) * a.ldx, a.K, true, lane);
+          if (lane == 0) rinv[m] = rms_inv(ss, a.K, a.pro_eps);
+        }
+      }
+      named_bar_sync(1, NT);
+    }
     // 1) Load the real rows (a thread's chunks of one batch in flight at
     //    once), per-row maximum. Past one batch, raw chunks are parked in
     //    shared memory until the maximum is known.
@@ -231,7 +247,13 @@ __global__ void __launch_bounds__(kStThreads, 2)
         const bool act = j0 + b < nj && ci < total;
         const int m = act ? ci / cpr : 0;
         const int kv = act ? (ci - m * cpr) * 8 : 0;
-        held[b] = load_x_chunk<XT>(xg, a.ldx, m, kv, act && kv < a.K);
+        if (PRO == kProNone) {
+          held[b] = load_x_chunk<XT>(xg, a.ldx, m, kv, act && kv < a.K);
+        } else {
+          held[b] = (act && kv < a.K) ? prologue_chunk<XT, PRO>(xg + static_cast<int64_t>(m) * a.ldx, kv, a.K, wnorm,
+                                                                 PRO == kProRmsNorm ? rinv[m] : 0.f)
+                                      : make_uint4(0u, 0u, 0u, 0u);
+        }
       }
 #pragma unroll
       for (int b = 0; b < kBatch; ++b) {
@@ -453,10 +475,10 @@ __global__ void __launch_bounds__(kStThreads, 2)
 
 namespace {
 
-template <int MT, int R, typename XT>
+template <int MT, int R, typename XT, int PRO>
 int launch_stream_t(const CUtensorMap& map, const SkinnyArgs& args, dim3 grid, size_t smem, bool pdl,
                     cudaStream_t stream) {
-  auto kern = stream_w8a16_kernel<MT, R, XT>;
+  auto kern = stream_w8a16_kernel<MT, R, XT, PRO>;
   static int configured[64] = {0};
   int dev = 0;
   cudaGetDevice(&dev);
@@ -484,26 +506,35 @@ int launch_stream_t(const CUtensorMap& map, const SkinnyArgs& args, dim3 grid, s
   return e == cudaSuccess ? QTTS_OK : QTTS_ERR_LAUNCH;
 }
 
-template <int MT, typename XT>
-int launch_stream_r(int r, const CUtensorMap& map, const SkinnyArgs& args, dim3 grid, size_t smem, bool pdl,
-                    cudaStream_t stream) {
+template <int MT, typename XT, int PRO>
+int launch_stream_rp(int r, const CUtensorMap& map, const SkinnyArgs& args, dim3 grid, size_t smem, bool pdl,
+                     cudaStream_t stream) {
   switch (r) {
     case 1:
-      return launch_stream_t<MT, 1, XT>(map, args, grid, smem, pdl, stream);
+      return launch_stream_t<MT, 1, XT, PRO>(map, args, grid, smem, pdl, stream);
     case 2:
-      return launch_stream_t<MT, 2, XT>(map, args, grid, smem, pdl, stream);
+      return launch_stream_t<MT, 2, XT, PRO>(map, args, grid, smem, pdl, stream);
     case 3:
-      return launch_stream_t<MT, 3, XT>(map, args, grid, smem, pdl, stream);
+      return launch_stream_t<MT, 3, XT, PRO>(map, args, grid, smem, pdl, stream);
     case 4:
-      return launch_stream_t<MT, 4, XT>(map, args, grid, smem, pdl, stream);
+      return launch_stream_t<MT, 4, XT, PRO>(map, args, grid, smem, pdl, stream);
     default:
-      return launch_stream_t<MT, 6, XT>(map, args, grid, smem, pdl, stream);
+      return launch_stream_t<MT, 6, XT, PRO>(map, args, grid, smem, pdl, stream);
   }
 }
 
+template <int MT, typename XT>
+int launch_stream_r(int r, const CUtensorMap& map, const SkinnyArgs& args, dim3 grid, size_t smem, bool pdl,
+                    cudaStream_t stream) {
+  if (args.prologue == kProRmsNorm) return launch_stream_rp<MT, XT, kProRmsNorm>(r, map, args, grid, smem, pdl, stream);
+  if (args.prologue == kProSiluMul) return launch_stream_rp<MT, XT, kProSiluMul>(r, map, args, grid, smem, pdl, stream);
+  return launch_stream_rp<MT, XT, kProNone>(r, map, args, grid, smem, pdl, stream);
+}
+
 size_t stream_smem(int mb, int xrows, int x_pitch, int stages) {
+  // xpart [warps][mb], xmax [mb], rinv [mb], then the barriers.
   return 1024 + static_cast<size_t>(stages) * kStStageBytes + static_cast<size_t>(xrows) * x_pitch * 2 +
-         (kStConsumerWarps + 1) * mb * 4 + 16 + 16 * stages + 16;
+         (kStConsumerWarps + 2) * mb * 4 + 16 + 16 * stages + 16;
 }
 
 }  // namespace

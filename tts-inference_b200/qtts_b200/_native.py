@@ -33,6 +33,8 @@ OK = 0
 ERR_TIMEOUT = 8
 
 FLAG_PDL = 0x1
+# activation prologues (QTTS_PROLOGUE_*)
+PROLOGUE_NONE, PROLOGUE_RMSNORM, PROLOGUE_SILU_MUL = 0, 1, 2
 VARIANT_AUTO = 0
 VARIANT_GENERIC = 1
 
@@ -96,6 +98,15 @@ SIGNATURES: dict[str, tuple[object, list[object]]] = {
         [_c_vp, _c_i64, _c_vp, _c_vp, _c_i64, _c_vp, _c_vp, _c_vp, _c_i64, _c_int, _c_int, _c_int, _c_int,
          _c_int, _c_uint, _c_vp],
     ),
+    "qtts_rms_norm": (_c_int, [_c_vp, _c_i64, _c_vp, _c_vp, _c_i64, _c_int, _c_int, _c_int, ctypes.c_float,
+                               _c_uint, _c_vp]),
+    "qtts_silu_mul": (_c_int, [_c_vp, _c_i64, _c_vp, _c_i64, _c_int, _c_int, _c_int, _c_uint, _c_vp]),
+    "qtts_w8a16_gemm_prologue": (
+        _c_int,
+        [_c_vp, _c_i64, _c_int, _c_int, _c_vp, ctypes.c_float, _c_vp, _c_i64, _c_vp, _c_int, _c_vp, _c_vp, _c_i64,
+         _c_int, _c_int, _c_int, _c_vp, _c_int, _c_uint, _c_vp],
+    ),
+    "qtts_w8a16_gemm_prologue_fused": (_c_int, [_c_int, _c_int, _c_int, _c_int, _c_int]),
     "qtts_fp8_linear_noalloc": (
         _c_int,
         [_c_vp, _c_i64, _c_int, _c_vp, _c_i64, _c_vp, _c_vp, _c_vp, _c_i64, _c_int, _c_int, _c_int, _c_int,

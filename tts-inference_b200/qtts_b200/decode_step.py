@@ -69,6 +69,11 @@ def apply_rope(x: torch.Tensor, cos: torch.Tensor, sin: torch.Tensor) -> torch.T
 
 
 class Block(nn.Module):
+    #: Run the input / post-attention norms and SiLU·up inside the quantized
+    #: linears that consume them (LinearBase.forward_rmsnorm / forward_silu_mul;
+    #: a no-op for unquantized layers). False keeps them as separate torch ops.
+    fuse_prologues = True
+
     def __init__(self, d: Dims, dtype: torch.dtype, device) -> None:
         super().__init__()
         self.d = d
@@ -85,7 +90,10 @@ class Block(nn.Module):
     def _qkv(self, x: torch.Tensor, cos, sin):
         b, t, _ = x.shape
         d = self.d
-        qkv = self.qkv_proj(rms_norm(x, self.input_norm))
+        if self.fuse_prologues:
+            qkv = self.qkv_proj.forward_rmsnorm(x, self.input_norm)
+        else:
+            qkv = self.qkv_proj(rms_norm(x, self.input_norm))
         q, k, v = qkv.split([d.heads * d.head_dim, d.kv_heads * d.head_dim, d.kv_heads * d.head_dim], dim=-1)
         q = rms_norm(q.view(b, t, d.heads, d.head_dim), self.q_norm).transpose(1, 2)
         k = rms_norm(k.view(b, t, d.kv_heads, d.head_dim), self.k_norm).transpose(1, 2)
@@ -93,6 +101,9 @@ class Block(nn.Module):
         return apply_rope(q, cos, sin), apply_rope(k, cos, sin), v
 
     def _mlp(self, h: torch.Tensor) -> torch.Tensor:
+        if self.fuse_prologues:
+            gate_up = self.gate_up_proj.forward_rmsnorm(h, self.post_norm)
+            return h + self.down_proj.forward_silu_mul(gate_up)
         gate, up = self.gate_up_proj(rms_norm(h, self.post_norm)).chunk(2, dim=-1)
         return h + self.down_proj(F.silu(gate) * up)
 
@@ -177,8 +188,10 @@ class CodePredictor(nn.Module):
             t = x.shape[1]
             for layer in self.layers:
                 x = layer.prefix(x, self.cos[:t], self.sin[:t])
-            last = rms_norm(x[:, -1], self.norm)
-            code = self.lm_head[s](last).float().argmax(dim=-1)
+            if Block.fuse_prologues:
+                code = self.lm_head[s].forward_rmsnorm(x[:, -1], self.norm).float().argmax(dim=-1)
+            else:
+                code = self.lm_head[s](rms_norm(x[:, -1], self.norm)).float().argmax(dim=-1)
             codes.append(code)
             if s + 1 < self.codebooks:
                 seq.append(self.embed[s + 1][code])

@@ -54,6 +54,24 @@ class LinearBase(nn.Module):
             return self.quant_method.apply(self, x, self.bias)
         return F.linear(x, self.weight, self.bias)
 
+    def forward_rmsnorm(self, x: torch.Tensor, norm_weight: torch.Tensor, eps: float = 1e-6) -> torch.Tensor:
+        """``self(rms_norm(x))``: the decoder layer's input / post-attention norm feeding
+        this projection (qtts/models/talker.py:249, 271). A quant method with
+        ``apply_rmsnorm`` runs the norm inside its GEMM; otherwise the norm runs first."""
+        fused = getattr(self.quant_method, "apply_rmsnorm", None)
+        if fused is not None:
+            return fused(self, x, norm_weight, eps, self.bias)
+        return self(F.rms_norm(x, (x.shape[-1],), norm_weight, eps))
+
+    def forward_silu_mul(self, gate_up: torch.Tensor) -> torch.Tensor:
+        """``self(F.silu(gate) * up)`` of ``gate_up = [gate | up]``: the down projection of a
+        gated MLP (qtts/layers/activation.py:143-147), fused where the quant method can."""
+        fused = getattr(self.quant_method, "apply_silu_mul", None)
+        if fused is not None:
+            return fused(self, gate_up, self.bias)
+        gate, up = gate_up.chunk(2, dim=-1)
+        return self(F.silu(gate) * up)
+
     def extra_repr(self) -> str:
         method = self.quant_method.name if self.quant_method is not None else "none"
         return f"in={self.in_features}, out={self.out_features}, bias={self.bias is not None}, quant={method}"

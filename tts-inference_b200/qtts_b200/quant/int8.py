@@ -25,7 +25,15 @@ from ..layers.linear import LinearBase
 from ..utils import get_logger
 from .base import QuantMethodBase
 from .calibrate import choose_variant, lookup_variant, worth_quantizing
-from .kernels import i8_scaled_mm, int8_quant_rows, kernel_available, quantize_int8_rows, w8_gemm
+from .kernels import (
+    i8_scaled_mm,
+    int8_quant_rows,
+    kernel_available,
+    quantize_int8_rows,
+    w8_gemm,
+    w8_gemm_rmsnorm,
+    w8_gemm_silu_mul,
+)
 
 logger = get_logger("quant.int8")
 
@@ -153,6 +161,23 @@ class Int8WeightOnlyMethod(QuantMethodBase):
         rows = x.numel() // max(1, x.shape[-1])
         variant = self.variant_for(layer.out_features, layer.in_features, rows, x.dtype)
         return w8_gemm(x, layer.int8_weight, layer.int8_scale, bias, variant=variant)  # type: ignore[attr-defined]
+
+    # -- fused activation prologues (LinearBase.forward_rmsnorm / forward_silu_mul) --
+
+    def apply_rmsnorm(self, layer: LinearBase, x: torch.Tensor, norm_weight: torch.Tensor, eps: float,
+                      bias: torch.Tensor | None) -> torch.Tensor:
+        """``apply(layer, rms_norm(x), bias)`` with the norm inside the GEMM's activation staging."""
+        rows = x.numel() // max(1, x.shape[-1])
+        variant = self.variant_for(layer.out_features, layer.in_features, rows, x.dtype)
+        return w8_gemm_rmsnorm(x, norm_weight, eps, layer.int8_weight, layer.int8_scale,  # type: ignore[attr-defined]
+                               bias, variant=variant)
+
+    def apply_silu_mul(self, layer: LinearBase, gate_up: torch.Tensor, bias: torch.Tensor | None) -> torch.Tensor:
+        """``apply(layer, silu(gate) * up, bias)`` of a ``[gate | up]`` input, fused the same way."""
+        rows = gate_up.numel() // max(1, gate_up.shape[-1])
+        variant = self.variant_for(layer.out_features, layer.in_features, rows, gate_up.dtype)
+        return w8_gemm_silu_mul(gate_up, layer.int8_weight, layer.int8_scale, bias,  # type: ignore[attr-defined]
+                                variant=variant)
 
 
 class Int8Method(QuantMethodBase):

@@ -133,6 +133,125 @@ def _weight_only_gemm(x, weight, scale, bias, variant, out, entry: str) -> torch
     return out.reshape(*shape[:-1], n)
 
 
+def rms_norm(x: torch.Tensor, weight: torch.Tensor, eps: float = 1e-6, *,
+             out: torch.Tensor | None = None) -> torch.Tensor:
+    """RMSNorm over the last dimension (qtts/layers/norm.py:49-76, 102-137):
+    ``cast(weight * (x * (1 / sqrt(mean(x^2) + eps))))`` in fp32, the sum of
+    squares in the library's fixed order. ``weight`` is ``[W]``; bf16, fp16 or
+    fp32 like ``x``. ``out`` may be ``x`` itself."""
+    ok, reason = nat.available()
+    if not ok:
+        raise RuntimeError(reason)
+    width = x.shape[-1]
+    if weight.numel() != width:
+        raise ValueError(f"weight has {weight.numel()} elements, expected {width}")
+    device = _require_cuda(x, weight)
+    a = _rows_view(x, width)
+    rows = a.shape[0]
+    weight = weight.reshape(-1)
+    if weight.dtype != x.dtype or weight.stride(0) != 1:
+        weight = weight.to(x.dtype).contiguous()
+    if out is None:
+        out = torch.empty((rows, width), device=device, dtype=x.dtype)
+    else:
+        out = _rows_view(out, width)
+        if out.shape != (rows, width) or out.dtype != x.dtype or out.stride(1) != 1:
+            raise ValueError(f"out must be [{rows}, {width}] {x.dtype} with unit column stride")
+    code = nat.lib().qtts_rms_norm(
+        a.data_ptr(), a.stride(0) if rows > 1 else width, weight.data_ptr(), out.data_ptr(),
+        out.stride(0) if rows > 1 else width, nat.dtype_code(x.dtype), rows, width, float(eps), _flags(),
+        nat.stream_ptr(device))
+    nat.check(code, "qtts_rms_norm")
+    return out.reshape(*x.shape)
+
+
+def silu_mul(gate_up: torch.Tensor, *, out: torch.Tensor | None = None) -> torch.Tensor:
+    """``F.silu(gate) * up`` of ``gate_up = [gate | up]`` (``[..., 2W]`` -> ``[..., W]``;
+    qtts/layers/activation.py:143-147), bit for bit torch's two CUDA kernels."""
+    ok, reason = nat.available()
+    if not ok:
+        raise RuntimeError(reason)
+    two_w = gate_up.shape[-1]
+    if two_w % 2:
+        raise ValueError(f"gate_up last dimension {two_w} is odd")
+    width = two_w // 2
+    device = _require_cuda(gate_up)
+    a = _rows_view(gate_up, two_w)
+    rows = a.shape[0]
+    if out is None:
+        out = torch.empty((rows, width), device=device, dtype=gate_up.dtype)
+    elif out.shape != (rows, width) or out.dtype != gate_up.dtype or out.stride(1) != 1:
+        raise ValueError(f"out must be [{rows}, {width}] {gate_up.dtype} with unit column stride")
+    code = nat.lib().qtts_silu_mul(
+        a.data_ptr(), a.stride(0) if rows > 1 else two_w, out.data_ptr(), out.stride(0) if rows > 1 else width,
+        nat.dtype_code(gate_up.dtype), rows, width, _flags(), nat.stream_ptr(device))
+    nat.check(code, "qtts_silu_mul")
+    return out.reshape(*gate_up.shape[:-1], width)
+
+
+def prologue_fused(m: int, n: int, k: int, prologue: int, variant: int = nat.VARIANT_AUTO) -> bool:
+    """Whether ``w8_gemm_rmsnorm`` / ``w8_gemm_silu_mul`` of this shape runs as one launch."""
+    return bool(nat.lib().qtts_w8a16_gemm_prologue_fused(m, n, k, prologue, variant))
+
+
+def _prologue_gemm(x, prologue, norm_weight, eps, weight, scale, bias, variant) -> torch.Tensor:
+    ok, reason = nat.available()
+    if not ok:
+        raise RuntimeError(reason)
+    if weight.dim() != 2 or weight.dtype != torch.int8:
+        raise ValueError(f"weight must be a 2-D int8 tensor, got {tuple(weight.shape)} {weight.dtype}")
+    n, k = weight.shape
+    width = 2 * k if prologue == nat.PROLOGUE_SILU_MUL else k
+    if x.shape[-1] != width:
+        raise ValueError(f"x has last dimension {x.shape[-1]}, expected {width} for weight [{n}, {k}]")
+    if scale.numel() != n:
+        raise ValueError(f"scale has {scale.numel()} elements, expected {n}")
+    device = _require_cuda(x, weight, scale, bias, norm_weight)
+    a = _rows_view(x, width)
+    rows = a.shape[0]
+    if weight.stride(1) != 1:
+        weight = weight.contiguous()
+    scale = scale.reshape(-1)
+    if scale.stride(0) != 1:
+        scale = scale.contiguous()
+    if bias is not None:
+        bias = bias.reshape(-1)
+        if bias.dtype != x.dtype or bias.stride(0) != 1:
+            bias = bias.to(x.dtype).contiguous()
+    if norm_weight is not None:
+        norm_weight = norm_weight.reshape(-1)
+        if norm_weight.numel() != k:
+            raise ValueError(f"norm weight has {norm_weight.numel()} elements, expected {k}")
+        if norm_weight.dtype != x.dtype or norm_weight.stride(0) != 1:
+            norm_weight = norm_weight.to(x.dtype).contiguous()
+    out = torch.empty((rows, n), device=device, dtype=x.dtype)
+    workspace = None
+    if rows > 0 and not prologue_fused(rows, n, k, prologue, variant):
+        workspace = torch.empty((rows, k), device=device, dtype=x.dtype)
+    code = nat.lib().qtts_w8a16_gemm_prologue(
+        a.data_ptr(), a.stride(0) if rows > 1 else width, nat.dtype_code(a.dtype), prologue,
+        norm_weight.data_ptr() if norm_weight is not None else None, float(eps),
+        weight.data_ptr(), weight.stride(0), scale.data_ptr(), nat.dtype_code(scale.dtype),
+        bias.data_ptr() if bias is not None else None, out.data_ptr(), n, rows, n, k,
+        workspace.data_ptr() if workspace is not None else None, variant, _flags(), nat.stream_ptr(device))
+    nat.check(code, "qtts_w8a16_gemm_prologue")
+    return out.reshape(*x.shape[:-1], n)
+
+
+def w8_gemm_rmsnorm(x: torch.Tensor, norm_weight: torch.Tensor, eps: float, weight: torch.Tensor,
+                    scale: torch.Tensor, bias: torch.Tensor | None = None, *,
+                    variant: int = nat.VARIANT_AUTO) -> torch.Tensor:
+    """``w8_gemm(rms_norm(x, norm_weight, eps), weight, scale, bias)`` -- one launch when the
+    chosen kernel stages activations itself (M <= 16), else the norm kernel chained ahead."""
+    return _prologue_gemm(x, nat.PROLOGUE_RMSNORM, norm_weight, eps, weight, scale, bias, variant)
+
+
+def w8_gemm_silu_mul(gate_up: torch.Tensor, weight: torch.Tensor, scale: torch.Tensor,
+                     bias: torch.Tensor | None = None, *, variant: int = nat.VARIANT_AUTO) -> torch.Tensor:
+    """``w8_gemm(silu_mul(gate_up), weight, scale, bias)`` (the down projection of a gated MLP)."""
+    return _prologue_gemm(gate_up, nat.PROLOGUE_SILU_MUL, None, 0.0, weight, scale, bias, variant)
+
+
 def w8_gemm_allgather(
     x: torch.Tensor,
     weight: torch.Tensor,
