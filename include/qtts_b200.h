@@ -10,7 +10,10 @@
  *     `torch._scaled_mm` of `Fp8Method.apply` (qtts/quant/fp8.py:72-89);
  *   - the load-time quantizers `quantize_weight_per_channel`
  *     (qtts/quant/int8.py:45-56) and `quantize_weight_fp8`
- *     (qtts/quant/fp8.py:45-49).
+ *     (qtts/quant/fp8.py:45-49);
+ *   - int8 W8A8 (`Int8Method.apply`, qtts/quant/int8.py:120-155), fp8
+ *     weight-only, and the RMSNorm / SiLU·up prologues of the decoder layer's
+ *     linears (qtts/layers/norm.py, activation.py:147), standalone or fused.
  *
  * Conventions shared by every entry point:
  *   - All pointers are device pointers owned by the caller; the library never
@@ -171,7 +174,9 @@ QTTS_API int qtts_w8a16_plan(int M, int N, int K, int G, int variant, int* kerne
  * and down_proj, qtts/layers/activation.py:147). Element arithmetic:
  *   RMSNorm   y = cast( w[k] * (x[k] * inv) ),
  *             inv = 1 / sqrt( sum_k x[k]^2 / width + eps )   (fp32; the sum
- *             in the library's fixed order, identical in every form)
+ *             in the library's fixed order, identical in every form: fma
+ *             over each 8-element chunk, a butterfly over each 32 consecutive
+ *             chunks, a stride-halving tree over those group sums)
  *   SiLU·up   y = cast( float(cast(g / (1 + exp(-g)))) * float(up) )
  *             (each step rounded to the activation type, as torch's
  *             F.silu(gate) * up) */
@@ -181,7 +186,8 @@ QTTS_API int qtts_w8a16_plan(int M, int N, int K, int G, int variant, int* kerne
 
 /* RMSNorm over the last dimension of x [rows, width] (leading dimension ldx)
  * with weight [width], into out [rows, width] (ldo); dtype BF16, FP16 or
- * FP32 for x, weight and out. out may be x (same ld): in place.
+ * FP32 for x, weight and out; width <= 65536. out may be x (same ld): in
+ * place.
  * Replaces: _rms_norm_kernel and RMSNorm.forward (qtts/layers/norm.py:49-76,
  * 102-121; the reduction reaches the reference's eager form,
  * norm.py:123-137, within one bf16 step, as the reference's own fused
@@ -202,7 +208,8 @@ QTTS_API int qtts_silu_mul(const void* gate_up, int64_t ld_in, void* out, int64_
  * norm_weight and eps unused). Equal bit for bit to qtts_rms_norm /
  * qtts_silu_mul followed by qtts_w8a16_gemm with the same variant. Where the
  * chosen kernel is the split-K or whole-K streaming kernel (int8 weights,
- * M <= 16, bf16/fp16 activations, 16-byte aligned rows and norm weight) the
+ * M <= 16, bf16/fp16 activations, 16-byte aligned rows and norm weight,
+ * K <= 8192 for RMSNorm) the
  * prologue runs inside it as the activations are staged: one launch. Otherwise
  * the prologue kernel writes workspace [M, K] (x_dtype, leading dimension K,
  * 16-byte aligned for the tensor-core kernels) and the GEMM, launched with

@@ -713,7 +713,7 @@ int qtts_fp8w_gemm(const void* x, int64_t ldx, int x_dtype, const uint8_t* w, in
 
 int qtts_rms_norm(const void* x, int64_t ldx, const void* weight, void* out, int64_t ldo, int dtype, int rows,
                   int width, float eps, unsigned flags, void* stream) {
-  if (rows < 0 || width < 0) return QTTS_ERR_SHAPE;
+  if (rows < 0 || width < 0 || width > 8 * 32 * kMaxNormGroups) return QTTS_ERR_SHAPE;
   if (rows == 0 || width == 0) return QTTS_OK;
   if (x == nullptr || weight == nullptr || out == nullptr) return QTTS_ERR_NULL;
   if (!is_float_dtype(dtype)) return QTTS_ERR_DTYPE;
@@ -789,7 +789,7 @@ int qtts_w8a16_gemm_prologue(const void* x, int64_t ldx, int x_dtype, int prolog
   const int family = chosen_family(x, ldx, x_dtype, w, ldw, M, N, K, variant);
   if (family < 0) return QTTS_ERR_ALIGN;
   const bool fusable = M <= 16 && (family == 0x100 || family == 0x300) &&
-                       (prologue != QTTS_PROLOGUE_RMSNORM || aligned16(norm_weight));
+                       (prologue != QTTS_PROLOGUE_RMSNORM || (aligned16(norm_weight) && K <= 8 * 32 * 32));
   if (fusable) {
     const FusedPrologue pro{prologue == QTTS_PROLOGUE_RMSNORM ? kProRmsNorm : kProSiluMul, norm_weight, eps};
     return w8a16_dispatch(x, 0, ldx, x_dtype, w, ldw, scale, scale_dtype, bias, out, 0, ldo, 1, M, N, K, nullptr,
@@ -800,6 +800,7 @@ int qtts_w8a16_gemm_prologue(const void* x, int64_t ldx, int x_dtype, int prolog
   // with programmatic dependent launch behind the prologue kernel, which
   // writes no weights.
   if (workspace == nullptr) return QTTS_ERR_NULL;
+  if (prologue == QTTS_PROLOGUE_RMSNORM && K > 8 * 32 * kMaxNormGroups) return QTTS_ERR_SHAPE;
   const int dev_ok = check_device();
   if (dev_ok != QTTS_OK) return dev_ok;
   const size_t sz = dtype_size(x_dtype);
@@ -829,6 +830,8 @@ int qtts_w8a16_gemm_prologue_fused(int M, int N, int K, int prologue, int varian
     int rgroups = 0;
     family = auto_family(M, N, K, 1, kWInt8, false, &rgroups);
   }
+  // The fused norm keeps one group sum per 256 columns of a row: K <= 8192.
+  if (prologue == QTTS_PROLOGUE_RMSNORM && K > 8 * 32 * 32) return 0;
   return (M <= 16 && (family == 0x100 || family == 0x300)) ? 1 : 0;
 }
 

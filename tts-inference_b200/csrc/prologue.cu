@@ -7,9 +7,8 @@
 // early (programmatic dependent launch) so its weights stream in meanwhile.
 // The element arithmetic is csrc/prologue.cuh's, shared with the fused forms.
 //
-// RMSNorm: one warp per row (the fixed reduction order is per warp), two
-// passes over the row (sum of squares, then scale and store; the second pass
-// hits L2). SiLU·up: one thread per 8-element chunk, grid-stride.
+// RMSNorm: one warp per row, two passes over the row (sum of squares in the
+// fixed order, then scale and store; the second pass hits L2). SiLU·up: one thread per 8-element chunk, grid-stride.
 #include "kernels.h"
 #include "prologue.cuh"
 
@@ -46,12 +45,14 @@ __global__ void __launch_bounds__(kPrThreads) rms_norm_kernel(const XT* x, int64
                                                               int64_t ldo, int rows, int width, float eps, bool vec) {
   pdl_launch_dependents();
   pdl_wait();
+  __shared__ float wgs[kPrRowsPerCta][kMaxNormGroups];
   const int lane = threadIdx.x & 31;
-  const int row = blockIdx.x * kPrRowsPerCta + (threadIdx.x >> 5);
+  const int warp = threadIdx.x >> 5;
+  const int row = blockIdx.x * kPrRowsPerCta + warp;
   if (row >= rows) return;
   const XT* xr = x + static_cast<int64_t>(row) * ldx;
   XT* orow = out + static_cast<int64_t>(row) * ldo;
-  const float inv = rms_inv(warp_row_sumsq<XT>(xr, width, vec, lane), width, eps);
+  const float inv = rms_inv(warp_row_sumsq<XT>(xr, width, vec, lane, wgs[warp]), width, eps);
   const int chunks = (width + 7) >> 3;
   for (int c = lane; c < chunks; c += 32) {
     const int n = width - 8 * c;

@@ -180,16 +180,6 @@ __global__ void __launch_bounds__(kSkThreads, 2)
 #endif
     const int kpad = n_iters * SW;
     const XT* wnorm = static_cast<const XT*>(a.pro_weight);
-    if constexpr (PRO == kProRmsNorm) {
-      // The norm's factor needs the whole row, not only this CTA's slice.
-      if (valid) {
-        for (int m = warp; m < mrows; m += kSkConsumerWarps) {
-          const float ss = warp_row_sumsq<XT>(xg + static_cast<int64_t>(m) * a.ldx, a.K, true, lane);
-          if (lane == 0) rinv[m] = rms_inv(ss, a.K, a.pro_eps);
-        }
-      }
-      named_bar_sync(1, kSkConsumerWarps * 32);
-    }
     // 1) Activation slice [MB, kpad]: each thread loads 16-byte chunks into
     //    registers (zeros past K and past the last batch row), the per-row
     //    maximum is combined with shared-memory atomics, then every thread
@@ -201,6 +191,37 @@ __global__ void __launch_bounds__(kSkThreads, 2)
       const bool in_regs = total <= kHeld * kSkConsumerWarps * 32;
       uint4 held[kHeld];
       const int nj = in_regs ? kHeld : (total + kSkConsumerWarps * 32 - 1) / (kSkConsumerWarps * 32);
+      if constexpr (PRO == kProRmsNorm) {
+        // The norm's factor needs the whole row, not only this CTA's slice.
+        // When the slice fits in registers its raw chunks and their norm
+        // weights are loaded first, so those loads overlap the norm's; the
+        // factors' scratch aliases the (not yet written) staged slice.
+        uint4 heldw[kHeld];
+        if (in_regs) {
+#pragma unroll
+          for (int j = 0; j < kHeld; ++j) {
+            const int ci = tid + kSkConsumerWarps * 32 * j;
+            const int m = ci / cpr;
+            const int kv = (ci - m * cpr) * 8;
+            held[j] = heldw[j] = make_uint4(0u, 0u, 0u, 0u);
+            if (ci < total && valid && m < mrows && kv < klen) {
+              held[j] = __ldcg(reinterpret_cast<const uint4*>(xg + static_cast<int64_t>(m) * a.ldx + k0 + kv));
+              heldw[j] = __ldg(reinterpret_cast<const uint4*>(wnorm + k0 + kv));
+            }
+          }
+        }
+        cta_norm_factors<XT>(xg, a.ldx, valid ? mrows : 0, a.K, a.pro_eps, reinterpret_cast<float*>(xs), rinv, warp,
+                             lane, kSkConsumerWarps, 1);
+        if (in_regs) {
+#pragma unroll
+          for (int j = 0; j < kHeld; ++j) {
+            const int ci = tid + kSkConsumerWarps * 32 * j;
+            const int m = ci / cpr;
+            const int kv = (ci - m * cpr) * 8;
+            if (ci < total && valid && m < mrows && kv < klen) held[j] = normalize_chunk<XT>(held[j], heldw[j], rinv[m]);
+          }
+        }
+      }
 #pragma unroll 4
       for (int j = 0; j < nj; ++j) {
         const int ci = tid + kSkConsumerWarps * 32 * j;
@@ -208,7 +229,9 @@ __global__ void __launch_bounds__(kSkThreads, 2)
         const int m = ci / cpr;
         const int kv = (ci - m * cpr) * 8;
         uint4 u = make_uint4(0u, 0u, 0u, 0u);
-        if (valid && m < mrows && kv < klen) {
+        if (PRO == kProRmsNorm && in_regs) {
+          u = held[j & (kHeld - 1)];  // normalized above
+        } else if (valid && m < mrows && kv < klen) {
           u = prologue_chunk<XT, PRO>(xg + static_cast<int64_t>(m) * a.ldx, k0 + kv, a.K, wnorm,
                                       PRO == kProRmsNorm ? rinv[m] : 0.f);
         }

@@ -227,15 +227,37 @@ __global__ void __launch_bounds__(kStThreads, 2)
     const bool in_regs = nj <= kBatch;
     uint4 held[kBatch];
     const XT* wnorm = static_cast<const XT*>(a.pro_weight);
+    bool normalized = false;  // held[] already holds normalized chunks
     if constexpr (PRO == kProRmsNorm) {
-      // The norm's factor of each real row, before any chunk is staged.
-      if (valid) {
-        for (int m = warp; m < mrows; m += kStConsumerWarps) {
-          const float ss = warp_row_sumsq<XT>(xg + static_cast<int64_t>(m) * a.ldx, a.K, true, lane);
-          if (lane == 0) rinv[m] = rms_inv(ss, a.K, a.pro_eps);
+      // The norm's factor of each real row before any chunk is staged. When the
+      // rows fit in registers their raw chunks and norm weights are loaded
+      // first, so those loads overlap the norm's; the factors' scratch aliases
+      // the (not yet written) staged rows.
+      uint4 heldw[kBatch];
+      if (in_regs) {
+#pragma unroll
+        for (int b = 0; b < kBatch; ++b) {
+          const int ci = tid + NT * b;
+          const bool act = b < nj && ci < total;
+          const int m = act ? ci / cpr : 0;
+          const int kv = act ? (ci - m * cpr) * 8 : 0;
+          held[b] = load_x_chunk<XT>(xg, a.ldx, m, kv, act && kv < a.K);
+          heldw[b] = (act && kv < a.K) ? __ldg(reinterpret_cast<const uint4*>(wnorm + kv)) : make_uint4(0u, 0u, 0u, 0u);
         }
       }
-      named_bar_sync(1, NT);
+      cta_norm_factors<XT>(xg, a.ldx, valid ? mrows : 0, a.K, a.pro_eps, reinterpret_cast<float*>(xs), rinv, warp,
+                           lane, kStConsumerWarps, 1);
+      if (in_regs) {
+#pragma unroll
+        for (int b = 0; b < kBatch; ++b) {
+          const int ci = tid + NT * b;
+          const bool act = b < nj && ci < total;
+          const int m = act ? ci / cpr : 0;
+          const int kv = act ? (ci - m * cpr) * 8 : 0;
+          if (act && kv < a.K) held[b] = normalize_chunk<XT>(held[b], heldw[b], rinv[m]);
+        }
+        normalized = true;
+      }
     }
     // 1) Load the real rows (a thread's chunks of one batch in flight at
     //    once), per-row maximum. Past one batch, raw chunks are parked in
@@ -249,6 +271,8 @@ __global__ void __launch_bounds__(kStThreads, 2)
         const int kv = act ? (ci - m * cpr) * 8 : 0;
         if (PRO == kProNone) {
           held[b] = load_x_chunk<XT>(xg, a.ldx, m, kv, act && kv < a.K);
+        } else if (normalized) {
+          // loaded and normalized above
         } else {
           held[b] = (act && kv < a.K) ? prologue_chunk<XT, PRO>(xg + static_cast<int64_t>(m) * a.ldx, kv, a.K, wnorm,
                                                                  PRO == kProRmsNorm ? rinv[m] : 0.f)
