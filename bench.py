@@ -1043,11 +1043,33 @@ def run_gpu_arm(args) -> None:
 def run_single(spec: str, calls: int = 3) -> None:
     """One (shape, M) point, `calls` launches with an L2 flush before each:
     a small case for `ncu` captures. spec = "<shape>:<M>[:<variant>]" (W8A16),
-    "fp8:<shape>:<M>" (activation quantization + fp8 GEMM) or "fp8w:<shape>:<M>"
-    (fp8 weight-only)."""
+    "fp8:<shape>:<M>" (activation quantization + fp8 GEMM), "fp8w:<shape>:<M>"
+    (fp8 weight-only) or "rms:<shape>:<M>" / "silu:<shape>:<M>" (W8A16 with its
+    RMSNorm / SiLU·up prologue, qtts_w8a16_gemm_prologue)."""
     from qtts_b200.quant import kernels as qk
 
     parts = spec.split(":")
+    if parts[0] in ("rms", "silu"):
+        label, m = parts[1], int(parts[2])
+        n, k = {lab: (n_, k_) for lab, n_, k_ in SHAPES}[label]
+        torch.cuda.set_device(0)
+        gen = torch.Generator(device="cuda")
+        gen.manual_seed(0)
+        q, s_ = qk.quantize_int8_rows(torch.randn((n, k), generator=gen, device="cuda") * 0.02)
+        s_ = s_.to(torch.bfloat16)
+        width = k if parts[0] == "rms" else 2 * k
+        x = torch.randn((m, width), generator=gen, device="cuda").to(torch.bfloat16)
+        nw = torch.ones(k, dtype=torch.bfloat16, device="cuda")
+        flush = torch.empty(256 << 20, dtype=torch.uint8, device="cuda")
+        for _ in range(calls):
+            flush.zero_()
+            if parts[0] == "rms":
+                qk.w8_gemm_rmsnorm(x, nw, 1e-6, q, s_)
+            else:
+                qk.w8_gemm_silu_mul(x, q, s_)
+        torch.cuda.synchronize()
+        print(json.dumps({"single": spec, "ok": True}))
+        return
     if parts[0] == "fp8w":
         label, m = parts[1], int(parts[2])
         n, k = {lab: (n_, k_) for lab, n_, k_ in SHAPES}[label]

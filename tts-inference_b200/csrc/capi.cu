@@ -607,7 +607,22 @@ static int w8a16_dispatch(const void* x, int64_t gsx, int64_t ldx, int x_dtype, 
     if (!(rgroups == 0 || rgroups == 1 || rgroups == 2 || rgroups == 4 || rgroups == 8)) return QTTS_ERR_VARIANT;
     if ((variant & 0xF000) != 0) return QTTS_ERR_VARIANT;
     const int zg = group_index != nullptr ? 1 : G;
-    const SkinnyPlan plan = plan_skinny(M, N, K, zg, split, rgroups);
+    SkinnyPlan plan = plan_skinny(M, N, K, zg, split, rgroups);
+    FusedPrologue pro_sk{};
+    if (pro != nullptr) {
+      pro_sk = *pro;
+      if (pro->kind == kProRmsNorm) {
+        // Slices aligned to the norm's 256-column groups: each CTA sums its own
+        // slice and the cluster exchanges the group sums ([MB][K / 256] floats
+        // kept past the barriers); otherwise the CTAs load the rows once more.
+        if (K % 256 == 0 && plan.k_per_cta % 256 == 0) {
+          plan.smem += static_cast<size_t>(plan.mt) * 8 * 32 * 4;
+        } else {
+          pro_sk.kind = kProRmsNormRows;
+        }
+      }
+      pro = &pro_sk;
+    }
     if (plan.grid.z > 65535u) return QTTS_ERR_SHAPE;
     if (plan.smem > kMaxDynSmem) return QTTS_ERR_VARIANT;  // activation slice does not fit this split
     CUtensorMap map;

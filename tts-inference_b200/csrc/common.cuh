@@ -123,6 +123,12 @@ __device__ __forceinline__ uint32_t mapa_shared(uint32_t addr, uint32_t rank) {
 
 // Store two floats into a peer CTA's shared memory; completion is counted in
 // bytes on the peer's mbarrier.
+__device__ __forceinline__ void st_async_f32(uint32_t remote_addr, float a, uint32_t remote_bar) {
+  asm volatile("st.async.shared::cluster.mbarrier::complete_tx::bytes.b32 [%0], %1, [%2];" ::"r"(remote_addr),
+               "r"(__float_as_uint(a)), "r"(remote_bar)
+               : "memory");
+}
+
 __device__ __forceinline__ void st_async_f32x2(uint32_t remote_addr, float a, float b, uint32_t remote_bar) {
   asm volatile("st.async.shared::cluster.mbarrier::complete_tx::bytes.v2.f32 [%0], {%1, %2}, [%3];" ::"r"(
                    remote_addr),

@@ -36,6 +36,11 @@ namespace qtts {
 constexpr int kProNone = 0;     // QTTS_PROLOGUE_NONE
 constexpr int kProRmsNorm = 1;  // QTTS_PROLOGUE_RMSNORM
 constexpr int kProSiluMul = 2;  // QTTS_PROLOGUE_SILU_MUL
+// RMSNorm whose CTA loads the whole rows for the factor (the split-K kernel
+// takes it when its slices are not aligned to the norm's 256-column groups).
+constexpr int kProRmsNormRows = 3;
+
+__host__ __device__ constexpr bool is_rms(int pro) { return pro == kProRmsNorm || pro == kProRmsNormRows; }
 
 // Eight elements starting at p as fp32 (zeros past n). `vec`: p is 16-byte
 // aligned (32-byte for fp32) and all eight exist.
@@ -220,7 +225,7 @@ __device__ __forceinline__ uint4 prologue_chunk(const XT* xrow, int k, int width
     const XT* e = reinterpret_cast<const XT*>(&u);
     uint4 o;
     XT* r = reinterpret_cast<XT*>(&o);
-    if constexpr (PRO == kProRmsNorm) {
+    if constexpr (is_rms(PRO)) {
       return normalize_chunk<XT>(u, __ldg(reinterpret_cast<const uint4*>(wnorm + k)), inv);
     } else {
       const uint4 uv = __ldcg(reinterpret_cast<const uint4*>(xrow + width + k));

@@ -38,10 +38,13 @@
 //     (arrive at start, wait before the first remote store) plus one closing
 //     phase, so that a cluster's CTAs leave together, are the only
 //     cluster-wide synchronization.
-//   * Optional activation prologue (template PRO, csrc/prologue.cuh): RMSNorm
-//     of the raw rows (one warp per row forms the row's factor over the whole
-//     of K, in the library's fixed order, before the slice is staged) or
-//     SiLU·up of [gate | up] rows, applied to each chunk as it is staged.
+//   * Optional activation prologue (template PRO, csrc/prologue.cuh): SiLU·up
+//     of [gate | up] rows, applied to each chunk as it is staged, or RMSNorm.
+//     The norm's factor needs the whole row. When K and the slice are
+//     multiples of 256, each warp's 32 staged chunks are exactly one group of
+//     the norm's fixed order, so every CTA sums its own slice and sends the
+//     group sums to its cluster peers (st.async on a bounded mbarrier): no
+//     extra loads. Otherwise all warps load the rows once more.
 //   * Every wait is bounded (globaltimer). On expiry the kernel records
 //     QTTS_ERR_TIMEOUT in the device status word, keeps the remote-store
 //     protocol (so no peer waits on it), skips its global stores and drains its
@@ -79,8 +82,11 @@ __global__ void __launch_bounds__(kSkThreads, 2)
       (reinterpret_cast<uintptr_t>(recv + (split > 1 ? BN * MB : 0)) + 15) & ~uintptr_t(15));
   uint64_t* empty = full + a.stages;
   uint64_t* recv_bar = empty + a.stages;
+  uint64_t* norm_bar = recv_bar + 1;  // RMSNorm prologue: the peers' group sums have landed
   int* err_flag = reinterpret_cast<int*>(recv_bar + 2);
   int* gate_flag = err_flag + 1;  // all-gather form: every rank is ready to receive
+  // RMSNorm prologue: [MB][K / 256] group sums (the launch adds MB * 128 bytes).
+  float* ngs = reinterpret_cast<float*>(recv_bar + 4);
   float* red = reinterpret_cast<float*>(wbuf);  // [KG][BN][MB], reuses the ring after the loop
 
   const int tid = threadIdx.x;
@@ -96,6 +102,9 @@ __global__ void __launch_bounds__(kSkThreads, 2)
   const int k0 = kidx * a.k_per_cta;
   const int klen = max(0, min(a.K - k0, a.k_per_cta));
   int n_iters = (klen + SW - 1) / SW;
+  // RMSNorm from the CTAs' own slices (group-aligned slices, K <= 8192).
+  // (the host picks this form only when K and the slices are multiples of 256).
+  constexpr bool slice_norm = PRO == kProRmsNorm;
 
   if (tid == 0) {
     QTTS_TRACE_STAMP(0);
@@ -104,6 +113,18 @@ __global__ void __launch_bounds__(kSkThreads, 2)
       mbar_init(&empty[s], kSkConsumerWarps);
     }
     mbar_init(recv_bar, 1);
+    if constexpr (slice_norm) {
+      // One arrival now; the phase completes when every peer's group sums
+      // (its slice's groups x the real rows of this m chunk) have landed.
+      mbar_init(norm_bar, 1);
+      uint32_t bytes = 0;
+      for (int p = 0; p < split; ++p) {
+        if (p == kidx) continue;
+        const int len = max(0, min(a.K - p * a.k_per_cta, a.k_per_cta));
+        bytes += static_cast<uint32_t>((len >> 8) * min(MB, a.M - m0) * 4);
+      }
+      mbar_arrive_expect_tx(norm_bar, bytes);
+    }
     for (int i = 0; i < MB; ++i) xinv[i] = 0.f;
     if (split > 1) {
       // The single arrival happens now; the phase completes once every peer's
@@ -191,11 +212,57 @@ __global__ void __launch_bounds__(kSkThreads, 2)
       const bool in_regs = total <= kHeld * kSkConsumerWarps * 32;
       uint4 held[kHeld];
       const int nj = in_regs ? kHeld : (total + kSkConsumerWarps * 32 - 1) / (kSkConsumerWarps * 32);
-      if constexpr (PRO == kProRmsNorm) {
-        // The norm's factor needs the whole row, not only this CTA's slice.
-        // When the slice fits in registers its raw chunks and their norm
-        // weights are loaded first, so those loads overlap the norm's; the
-        // factors' scratch aliases the (not yet written) staged slice.
+      if constexpr (slice_norm) {
+        // Raw chunks (registers, or parked in the staged slice); a warp's 32
+        // consecutive chunks are one row's group g = k / 256: leaf sums and
+        // butterfly, then the group sum goes to this CTA's table and to every
+        // peer's (the cluster wait makes sure the peers' barriers exist).
+        const int groups = a.K >> 8;
+        if (split > 1) cluster_wait();
+#pragma unroll 4
+        for (int j = 0; j < nj; ++j) {
+          const int ci = tid + kSkConsumerWarps * 32 * j;
+          if (ci >= total) break;  // total is a multiple of 32: warp-uniform
+          const int m = ci / cpr;
+          const int kv = (ci - m * cpr) * 8;
+          const bool real = valid && m < mrows && kv < klen;  // warp-uniform
+          uint4 u = make_uint4(0u, 0u, 0u, 0u);
+          if (real) u = __ldcg(reinterpret_cast<const uint4*>(xg + static_cast<int64_t>(m) * a.ldx + k0 + kv));
+          if (in_regs) {
+            held[j & (kHeld - 1)] = u;
+          } else {
+            *reinterpret_cast<uint4*>(xs + m * a.x_pitch + kv) = u;
+          }
+          if (real) {
+            const XT* e = reinterpret_cast<const XT*>(&u);
+            float v[8];
+#pragma unroll
+            for (int q = 0; q < 8; ++q) v[q] = to_float(e[q]);
+            const float gsum = group_butterfly(leaf_sumsq(v));
+            const int idx = m * groups + ((k0 + kv) >> 8);
+            if (lane == 0) ngs[idx] = gsum;
+            if (lane < split && lane != static_cast<int>(crank)) {
+              st_async_f32(mapa_shared(smem_u32(ngs + idx), lane), gsum,
+                           mapa_shared(smem_u32(norm_bar), lane));
+            }
+          }
+        }
+        named_bar_sync(1, kSkConsumerWarps * 32);  // own group sums written
+        if (!mbar_wait_bounded(norm_bar, 0, a.wait_ns)) {
+          if (tid == 0) record_status(QTTS_ERR_TIMEOUT);
+          // Peers always send; keep this CTA's table alive until their stores land.
+          mbar_wait_bounded(norm_bar, 0, 4 * a.wait_ns);
+        }
+        for (int m = warp; m < mrows; m += kSkConsumerWarps) {
+          const float ssq = lanes_stride_tree(lane < groups ? ngs[m * groups + lane] : 0.f, groups);
+          if (lane == 0) rinv[m] = rms_inv(ssq, a.K, a.pro_eps);
+        }
+        named_bar_sync(1, kSkConsumerWarps * 32);
+      } else if constexpr (PRO == kProRmsNormRows) {
+        // The rows are loaded once more, by all warps. When the slice fits in
+        // registers its raw chunks and their norm weights are loaded first,
+        // so those loads overlap the norm's; the factors' scratch aliases the
+        // (not yet written) staged slice.
         uint4 heldw[kHeld];
         if (in_regs) {
 #pragma unroll
@@ -229,11 +296,19 @@ __global__ void __launch_bounds__(kSkThreads, 2)
         const int m = ci / cpr;
         const int kv = (ci - m * cpr) * 8;
         uint4 u = make_uint4(0u, 0u, 0u, 0u);
-        if (PRO == kProRmsNorm && in_regs) {
-          u = held[j & (kHeld - 1)];  // normalized above
-        } else if (valid && m < mrows && kv < klen) {
-          u = prologue_chunk<XT, PRO>(xg + static_cast<int64_t>(m) * a.ldx, k0 + kv, a.K, wnorm,
-                                      PRO == kProRmsNorm ? rinv[m] : 0.f);
+        if constexpr (slice_norm) {
+          // Raw chunk staged above; normalized now that the factors are known.
+          if (valid && m < mrows && kv < klen) {
+            u = in_regs ? held[j & (kHeld - 1)] : *reinterpret_cast<const uint4*>(xs + m * a.x_pitch + kv);
+            u = normalize_chunk<XT>(u, __ldg(reinterpret_cast<const uint4*>(wnorm + k0 + kv)), rinv[m]);
+          }
+        } else {
+          if (PRO == kProRmsNormRows && in_regs) {
+            u = held[j & (kHeld - 1)];  // normalized above
+          } else if (valid && m < mrows && kv < klen) {
+            u = prologue_chunk<XT, PRO>(xg + static_cast<int64_t>(m) * a.ldx, k0 + kv, a.K, wnorm,
+                                        is_rms(PRO) ? rinv[m] : 0.f);
+          }
         }
         const XT* e = reinterpret_cast<const XT*>(&u);
         float mx = 0.f;
@@ -422,7 +497,7 @@ __global__ void __launch_bounds__(kSkThreads, 2)
       //    rank: a plain store for own rows, st.async from registers for a
       //    peer's, counted on the owner's mbarrier. Peers always send, even
       //    after an error, so no owner waits in vain.
-      cluster_wait();  // every peer's receive barrier is initialized
+      if (!slice_norm) cluster_wait();  // every peer's receive barrier is initialized (waited already otherwise)
       constexpr int kCpr = MB / 4;  // 16-byte chunks per row
       const uint32_t own_recv = smem_u32(recv);
       for (int i = tid; i < BN * kCpr; i += kSkConsumerWarps * 32) {
@@ -605,6 +680,12 @@ int launch_skinny_mt(const SkinnyPlan& p, const CUtensorMap& map, const SkinnyAr
                                                                            pdl, stream)
                        : launch_skinny_r<2, XT, false, false, kProRmsNorm>(p.r, map, args, p.grid, p.split, p.smem,
                                                                            pdl, stream);
+    }
+    if (args.prologue == kProRmsNormRows) {
+      return p.mt == 1 ? launch_skinny_r<1, XT, false, false, kProRmsNormRows>(p.r, map, args, p.grid, p.split,
+                                                                               p.smem, pdl, stream)
+                       : launch_skinny_r<2, XT, false, false, kProRmsNormRows>(p.r, map, args, p.grid, p.split,
+                                                                               p.smem, pdl, stream);
     }
     return p.mt == 1 ? launch_skinny_r<1, XT, false, false, kProSiluMul>(p.r, map, args, p.grid, p.split, p.smem, pdl,
                                                                          stream)
