@@ -279,3 +279,25 @@ def test_graph_replays(m):
         torch.cuda.synchronize()
         assert torch.equal(y1, qk.w8_gemm(qk.rms_norm(xs, nw, 1e-6), wq, ws)), f"replay {seed}"
         assert torch.equal(y2, qk.w8_gemm(qk.silu_mul(gu), wd, wsd)), f"replay {seed}"
+
+
+def test_rms_norm_paths_agree_bit_for_bit():
+    """Rows read once into registers (aligned, <= 2048 wide) and rows read twice (here made
+    unaligned by an odd row pitch) give the same bits: one fixed reduction order."""
+    x, w = norm_rows(12, 2048, torch.bfloat16, seed=290)
+    padded = torch.zeros(12, 2049, dtype=torch.bfloat16, device="cuda")
+    padded[:, :2048] = x
+    assert torch.equal(qk.rms_norm(padded[:, :2048], w, 1e-6), qk.rms_norm(x, w, 1e-6))
+
+
+@pytest.mark.parametrize("m", [1, 4, 8, 16])
+@pytest.mark.parametrize("variant", ["auto", "skinny8", "stream"])
+def test_rmsnorm_gemm_full_row_form(m, variant):
+    """K = 1152 is not a multiple of the norm's 256-column groups: the streaming kernels
+    load the rows once more for the factor. Still equal to the two-step form."""
+    n, k = 2048, 1152
+    wq, ws, q, s = gemm_case(n, k, seed=291)
+    x, nw = norm_rows(m, k, torch.bfloat16, seed=292 + m)
+    v = VARIANTS[variant]
+    xn = qk.rms_norm(x, nw, 1e-6)
+    assert torch.equal(qk.w8_gemm_rmsnorm(x, nw, 1e-6, wq, ws, variant=v), qk.w8_gemm(xn, wq, ws, variant=v))

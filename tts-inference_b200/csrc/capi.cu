@@ -563,7 +563,21 @@ static int w8a16_dispatch(const void* x, int64_t gsx, int64_t ldx, int x_dtype, 
     if (!(rgroups == 0 || stream_rows_ok(rgroups))) return QTTS_ERR_VARIANT;
     if ((variant & 0xF00F) != 0) return QTTS_ERR_VARIANT;
     const int zg = group_index != nullptr ? 1 : G;
-    const SkinnyPlan plan = plan_stream(M, N, K, zg, rgroups);
+    SkinnyPlan plan = plan_stream(M, N, K, zg, rgroups);
+    FusedPrologue pro_st{};
+    if (pro != nullptr) {
+      pro_st = *pro;
+      if (pro->kind == kProRmsNorm) {
+        // K a multiple of 256: the factors come from the staged rows ([MB][K / 256]
+        // group sums kept past the barriers); otherwise from one more load of the rows.
+        if (K % 256 == 0) {
+          plan.smem += static_cast<size_t>(plan.mt) * 8 * 32 * 4;
+        } else {
+          pro_st.kind = kProRmsNormRows;
+        }
+      }
+      pro = &pro_st;
+    }
     if (plan.grid.z > 65535u || plan.grid.x > 2147483647u) return QTTS_ERR_SHAPE;
     if (plan.smem > kMaxDynSmem) return QTTS_ERR_VARIANT;
     CUtensorMap map;

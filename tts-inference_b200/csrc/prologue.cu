@@ -40,6 +40,45 @@ __device__ __forceinline__ void store8(XT* p, int n, bool vec, const float (&v)[
   }
 }
 
+// Rows of at most kRegGroups * 256 16-bit elements: each lane keeps its chunks
+// of the row and of the weight in registers, so the row is read once.
+constexpr int kRegGroups = 8;
+
+template <typename XT>
+__device__ __forceinline__ void rms_norm_row_regs(const XT* xr, const XT* w, XT* orow, int width, float eps,
+                                                  int lane, float* wgs) {
+  const int chunks = width >> 3;
+  const int groups = (chunks + 31) >> 5;
+  uint4 xv[kRegGroups], wv[kRegGroups];
+#pragma unroll
+  for (int g = 0; g < kRegGroups; ++g) {
+    const int c = 32 * g + lane;
+    xv[g] = wv[g] = make_uint4(0u, 0u, 0u, 0u);
+    if (c < chunks) {
+      xv[g] = __ldcg(reinterpret_cast<const uint4*>(xr + 8 * c));
+      wv[g] = __ldg(reinterpret_cast<const uint4*>(w + 8 * c));
+    }
+  }
+#pragma unroll
+  for (int g = 0; g < kRegGroups; ++g) {
+    if (g < groups) {
+      const XT* e = reinterpret_cast<const XT*>(&xv[g]);
+      float v[8];
+#pragma unroll
+      for (int q = 0; q < 8; ++q) v[q] = to_float(e[q]);
+      const float s = group_butterfly(leaf_sumsq(v));
+      if (lane == 0) wgs[g] = s;
+    }
+  }
+  __syncwarp();
+  const float inv = rms_inv(lanes_stride_tree(lane < groups ? wgs[lane] : 0.f, groups), width, eps);
+#pragma unroll
+  for (int g = 0; g < kRegGroups; ++g) {
+    const int c = 32 * g + lane;
+    if (c < chunks) *reinterpret_cast<uint4*>(orow + 8 * c) = normalize_chunk<XT>(xv[g], wv[g], inv);
+  }
+}
+
 template <typename XT>
 __global__ void __launch_bounds__(kPrThreads) rms_norm_kernel(const XT* x, int64_t ldx, const XT* w, XT* out,
                                                               int64_t ldo, int rows, int width, float eps, bool vec) {
@@ -52,6 +91,12 @@ __global__ void __launch_bounds__(kPrThreads) rms_norm_kernel(const XT* x, int64
   if (row >= rows) return;
   const XT* xr = x + static_cast<int64_t>(row) * ldx;
   XT* orow = out + static_cast<int64_t>(row) * ldo;
+  if constexpr (sizeof(XT) == 2) {
+    if (vec && width <= 256 * kRegGroups) {
+      rms_norm_row_regs<XT>(xr, w, orow, width, eps, lane, wgs[warp]);
+      return;
+    }
+  }
   const float inv = rms_inv(warp_row_sumsq<XT>(xr, width, vec, lane, wgs[warp]), width, eps);
   const int chunks = (width + 7) >> 3;
   for (int c = lane; c < chunks; c += 32) {

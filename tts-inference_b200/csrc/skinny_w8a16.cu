@@ -212,6 +212,7 @@ __global__ void __launch_bounds__(kSkThreads, 2)
       const bool in_regs = total <= kHeld * kSkConsumerWarps * 32;
       uint4 held[kHeld];
       const int nj = in_regs ? kHeld : (total + kSkConsumerWarps * 32 - 1) / (kSkConsumerWarps * 32);
+      uint4 heldw[kHeld];  // norm weights of the chunks held in registers (slice form)
       if constexpr (slice_norm) {
         // Raw chunks (registers, or parked in the staged slice); a warp's 32
         // consecutive chunks are one row's group g = k / 256: leaf sums and
@@ -230,6 +231,8 @@ __global__ void __launch_bounds__(kSkThreads, 2)
           if (real) u = __ldcg(reinterpret_cast<const uint4*>(xg + static_cast<int64_t>(m) * a.ldx + k0 + kv));
           if (in_regs) {
             held[j & (kHeld - 1)] = u;
+            heldw[j & (kHeld - 1)] =
+                real ? __ldg(reinterpret_cast<const uint4*>(wnorm + k0 + kv)) : make_uint4(0u, 0u, 0u, 0u);
           } else {
             *reinterpret_cast<uint4*>(xs + m * a.x_pitch + kv) = u;
           }
@@ -263,7 +266,6 @@ __global__ void __launch_bounds__(kSkThreads, 2)
         // registers its raw chunks and their norm weights are loaded first,
         // so those loads overlap the norm's; the factors' scratch aliases the
         // (not yet written) staged slice.
-        uint4 heldw[kHeld];
         if (in_regs) {
 #pragma unroll
           for (int j = 0; j < kHeld; ++j) {
@@ -299,8 +301,12 @@ __global__ void __launch_bounds__(kSkThreads, 2)
         if constexpr (slice_norm) {
           // Raw chunk staged above; normalized now that the factors are known.
           if (valid && m < mrows && kv < klen) {
-            u = in_regs ? held[j & (kHeld - 1)] : *reinterpret_cast<const uint4*>(xs + m * a.x_pitch + kv);
-            u = normalize_chunk<XT>(u, __ldg(reinterpret_cast<const uint4*>(wnorm + k0 + kv)), rinv[m]);
+            if (in_regs) {
+              u = normalize_chunk<XT>(held[j & (kHeld - 1)], heldw[j & (kHeld - 1)], rinv[m]);
+            } else {
+              u = normalize_chunk<XT>(*reinterpret_cast<const uint4*>(xs + m * a.x_pitch + kv),
+                                      __ldg(reinterpret_cast<const uint4*>(wnorm + k0 + kv)), rinv[m]);
+            }
           }
         } else {
           if (PRO == kProRmsNormRows && in_regs) {

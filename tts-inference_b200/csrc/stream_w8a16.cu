@@ -30,9 +30,10 @@
 //     per-row power of two (exact for every element within 2^28 of the row's
 //     largest magnitude), with warp-level reductions before the few shared
 //     atomics.
-//   * Optional activation prologue (template PRO, csrc/prologue.cuh): RMSNorm
-//     (row factors formed first, one warp per row) or SiLU·up of [gate | up]
-//     rows, applied to each chunk as it is loaded.
+//   * Optional activation prologue (template PRO, csrc/prologue.cuh): SiLU·up
+//     of [gate | up] rows, applied to each chunk as it is loaded, or RMSNorm,
+//     whose row factors come from the staged rows themselves (K a multiple of
+//     256) or from one more load of the rows by all warps.
 //   * Every wait is bounded (globaltimer); on expiry the kernel records
 //     QTTS_ERR_TIMEOUT, skips its stores and drains its own copies in flight.
 #include "common.cuh"
@@ -139,6 +140,8 @@ __global__ void __launch_bounds__(kStThreads, 2)
       (reinterpret_cast<uintptr_t>(rinv + MB) + 15) & ~uintptr_t(15));
   uint64_t* empty = full + a.stages;
   int* err_flag = reinterpret_cast<int*>(empty + a.stages);
+  // RMSNorm prologue: [MB][K / 256] group sums (the launch adds MB * 128 bytes).
+  float* ngs = reinterpret_cast<float*>(err_flag + 4);
   float* red = reinterpret_cast<float*>(wbuf);  // [KG][BN][MB], reuses the ring after the loop
 
   const int tid = threadIdx.x;
@@ -229,6 +232,58 @@ __global__ void __launch_bounds__(kStThreads, 2)
     const XT* wnorm = static_cast<const XT*>(a.pro_weight);
     bool normalized = false;  // held[] already holds normalized chunks
     if constexpr (PRO == kProRmsNorm) {
+      // The whole of K is staged here and, with K a multiple of 256, a warp's
+      // 32 consecutive chunks are one group of the norm's fixed order: the
+      // group sums come from the raw chunks as they are loaded (norm weights
+      // alongside), the factors from the group sums, then the chunks held in
+      // registers are normalized; past one batch the staging below reloads
+      // and normalizes them.
+      const int groups = a.K >> 8;
+      uint4 heldw[kBatch];
+      for (int j0 = 0; j0 < nj; j0 += kBatch) {
+#pragma unroll
+        for (int b = 0; b < kBatch; ++b) {
+          const int ci = tid + NT * (j0 + b);
+          const bool act = j0 + b < nj && ci < total;
+          const int m = act ? ci / cpr : 0;
+          const int kv = act ? (ci - m * cpr) * 8 : 0;
+          held[b] = load_x_chunk<XT>(xg, a.ldx, m, kv, act && kv < a.K);
+          heldw[b] = (in_regs && act && kv < a.K) ? __ldg(reinterpret_cast<const uint4*>(wnorm + kv))
+                                                  : make_uint4(0u, 0u, 0u, 0u);
+        }
+#pragma unroll
+        for (int b = 0; b < kBatch; ++b) {
+          const int ci = tid + NT * (j0 + b);
+          if (j0 + b < nj && ci < total) {  // warp-uniform: total is a multiple of 32
+            const int m = ci / cpr;
+            const int kv = (ci - m * cpr) * 8;
+            const XT* e = reinterpret_cast<const XT*>(&held[b]);
+            float v[8];
+#pragma unroll
+            for (int q = 0; q < 8; ++q) v[q] = to_float(e[q]);
+            const float gsum = group_butterfly(leaf_sumsq(v));
+            if (lane == 0) ngs[m * groups + (kv >> 8)] = gsum;
+          }
+        }
+      }
+      named_bar_sync(1, NT);
+      for (int m = warp; m < mrows; m += kStConsumerWarps) {
+        const float ssq = lanes_stride_tree(lane < groups ? ngs[m * groups + lane] : 0.f, groups);
+        if (lane == 0) rinv[m] = rms_inv(ssq, a.K, a.pro_eps);
+      }
+      named_bar_sync(1, NT);
+      if (in_regs) {
+#pragma unroll
+        for (int b = 0; b < kBatch; ++b) {
+          const int ci = tid + NT * b;
+          const bool act = b < nj && ci < total;
+          const int m = act ? ci / cpr : 0;
+          const int kv = act ? (ci - m * cpr) * 8 : 0;
+          if (act && kv < a.K) held[b] = normalize_chunk<XT>(held[b], heldw[b], rinv[m]);
+        }
+        normalized = true;
+      }
+    } else if constexpr (PRO == kProRmsNormRows) {
       // The norm's factor of each real row before any chunk is staged. When the
       // rows fit in registers their raw chunks and norm weights are loaded
       // first, so those loads overlap the norm's; the factors' scratch aliases
@@ -275,7 +330,7 @@ __global__ void __launch_bounds__(kStThreads, 2)
           // loaded and normalized above
         } else {
           held[b] = (act && kv < a.K) ? prologue_chunk<XT, PRO>(xg + static_cast<int64_t>(m) * a.ldx, kv, a.K, wnorm,
-                                                                 PRO == kProRmsNorm ? rinv[m] : 0.f)
+                                                                 is_rms(PRO) ? rinv[m] : 0.f)
                                       : make_uint4(0u, 0u, 0u, 0u);
         }
       }
@@ -551,6 +606,9 @@ template <int MT, typename XT>
 int launch_stream_r(int r, const CUtensorMap& map, const SkinnyArgs& args, dim3 grid, size_t smem, bool pdl,
                     cudaStream_t stream) {
   if (args.prologue == kProRmsNorm) return launch_stream_rp<MT, XT, kProRmsNorm>(r, map, args, grid, smem, pdl, stream);
+  if (args.prologue == kProRmsNormRows) {
+    return launch_stream_rp<MT, XT, kProRmsNormRows>(r, map, args, grid, smem, pdl, stream);
+  }
   if (args.prologue == kProSiluMul) return launch_stream_rp<MT, XT, kProSiluMul>(r, map, args, grid, smem, pdl, stream);
   return launch_stream_rp<MT, XT, kProNone>(r, map, args, grid, smem, pdl, stream);
 }
