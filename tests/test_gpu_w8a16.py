@@ -97,7 +97,7 @@ VARIANTS = {
 
 
 @pytest.mark.parametrize("variant", sorted(VARIANTS))
-@pytest.mark.parametrize("m", [1, 8, 16, 33, 64])
+@pytest.mark.parametrize("m", [1, 8, 16, 33, 64, 128])
 def test_every_variant_agrees(variant, m):
     n, k = 2048, 6144
     x, q, s = seeded_case(n, k, m, seed=2)

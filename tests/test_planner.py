@@ -3,7 +3,9 @@
 Pins the rule the B200 measurements chose: up to 16 rows the split-K streaming
 kernel with the most CTAs that run two per SM (ties to the larger row tile,
 every CTA of a split owning part of K); up to 4 rows of int8 the whole-K
-streaming kernel where it reaches more CTAs; past 16 rows the tcgen05 kernel.
+streaming kernel where it reaches more CTAs; past 16 rows the tcgen05 kernel, whose
+batch tile grows to 128 columns past 64 rows only when 64-column tiles would not fit
+one CTA per SM.
 """
 
 from __future__ import annotations
@@ -29,6 +31,9 @@ def _lib():
         (2048, 6144, 4, "skinny_w8a16_kernel", 8, 64, 256),  # down_proj
         (4096, 2048, 32, "umma_w8a16_kernel", 4, 128, 128),
         (12288, 2048, 64, "umma_w8a16_kernel", 1, 128, 96),
+        # past 64 rows: one 128-column tile when 64-column tiles would overflow a wave
+        (12288, 2048, 128, "umma_w8a16_kernel", 1, 128, 96),
+        (4096, 1024, 128, "umma_w8a16_kernel", 2, 128, 128),
         # code predictor down: every 256-CTA plan would leave a split CTA without K
         (1024, 3072, 8, "skinny_w8a16_kernel", 2, 16, 128),
     ],

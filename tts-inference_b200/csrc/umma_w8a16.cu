@@ -43,7 +43,7 @@ constexpr int kUmDqWarps = 8;
 constexpr int kUmProducerWarp = 8;
 constexpr int kUmMmaWarp = 9;
 constexpr int kUmThreads = (kUmDqWarps + 2) * 32;
-constexpr uint32_t kUmTmemCols = 256;  // A: 3 x 64 columns, D: up to 64 columns
+constexpr uint32_t kUmTmemCols = 256;  // A ring + D: 192 + up to 64 columns, or 128 + 128 (NB = 128)
 
 __device__ __forceinline__ void tmem_st_x32(uint32_t taddr, const uint32_t (&r)[32]) {
   asm volatile(
@@ -95,8 +95,11 @@ __global__ void __launch_bounds__(kUmThreads, 1)
   constexpr int HALF = NB / 2;      // accumulator columns per dequant warpgroup
   constexpr int XS = NB * 256;      // activation tile bytes per 128-k stage
   constexpr int kSlotCols = 32;     // tensor-memory columns per 64-k A slot
-  constexpr int kNA = 192 / kSlotCols;  // A slots
-  constexpr uint32_t kDCol = 192;
+  // NB = 128 (M = 65..128 in one tile: an MMA costs the same for any N) keeps
+  // four A slots so that the accumulator's 128 columns fit the 256 allocated.
+  constexpr int kACols = NB > 64 ? 128 : 192;
+  constexpr int kNA = kACols / kSlotCols;  // A slots
+  constexpr uint32_t kDCol = kACols;
   constexpr uint32_t kIdesc = umma_idesc(kFmt, kFmt, 128, NB);
   extern __shared__ uint8_t smem_raw[];
   uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
@@ -341,7 +344,14 @@ __global__ void __launch_bounds__(kUmThreads, 1)
     if (tid == 0) QTTS_TRACE_STAMP(6);
     tc_fence_after();
     uint32_t d[HALF];
-    tmem_ld<HALF>(tmem + lane_base + kDCol + HALF * half, d);
+    if constexpr (HALF <= 32) {
+      tmem_ld<HALF>(tmem + lane_base + kDCol + HALF * half, d);
+    } else {
+      uint32_t (&d0)[32] = *reinterpret_cast<uint32_t(*)[32]>(d);
+      uint32_t (&d1)[32] = *reinterpret_cast<uint32_t(*)[32]>(d + 32);
+      tmem_ld<32>(tmem + lane_base + kDCol + HALF * half, d0);
+      tmem_ld<32>(tmem + lane_base + kDCol + HALF * half + 32, d1);
+    }
     tc_wait_ld();
     const bool cta_err = *verr != 0;
     float v[HALF];
@@ -498,8 +508,10 @@ int launch_umma_w(const CUtensorMap& map, const CUtensorMap& xmap, const SkinnyA
       return launch_umma_t<16, XT, E4M3, AG>(map, xmap, args, p, pdl, stream);
     case 4:
       return launch_umma_t<32, XT, E4M3, AG>(map, xmap, args, p, pdl, stream);
-    default:
+    case 8:
       return launch_umma_t<64, XT, E4M3, AG>(map, xmap, args, p, pdl, stream);
+    default:
+      return launch_umma_t<128, XT, E4M3, AG>(map, xmap, args, p, pdl, stream);
   }
 }
 
@@ -523,11 +535,20 @@ size_t umma_smem(int nb, int wstages, int xstages, int split) {
 
 SkinnyPlan plan_umma(int M, int N, int K, int G, int split_req) {
   SkinnyPlan p{};
-  const int nb = M <= 16 ? 16 : (M <= 32 ? 32 : 64);
+  const int n_tiles = (N + 127) / 128;
+  // Batch columns per tile. Past 64 rows, 64-column tiles give more CTAs (each
+  // redoing the dequantization and the MMAs of its weight tile: a 128-row
+  // tcgen05.mma costs the same for any N), which pays while they fit one CTA
+  // per SM; beyond that two tiles share an SM's tensor core and one
+  // 128-column tile is faster. Measured on B200 at M = 128: talker gate_up
+  // (96 weight tiles) 34.2 us as 64-column tiles, 18.9 us as one; the code
+  // predictor's 1024-wide matrices (8..48 tiles) 8.0-10.5 us as 64-column
+  // tiles, 10-20 % slower as one.
+  int nb = M <= 16 ? 16 : (M <= 32 ? 32 : 64);
+  if (M > 64 && static_cast<long long>(n_tiles) * G * ((M + 63) / 64) > kNumSMs) nb = 128;
   p.mt = nb / 8;
   p.r = 8;
   p.m_chunks = (M + nb - 1) / nb;
-  const int n_tiles = (N + 127) / 128;
   const int ctas_base = n_tiles * G * p.m_chunks;
   auto kpc_for = [&](int s) { return ((K + s - 1) / s + 127) / 128 * 128; };
   int split = split_req;
@@ -550,7 +571,8 @@ SkinnyPlan plan_umma(int M, int N, int K, int G, int split_req) {
   // deeper ring does not help: the dequant warps run at most three stages
   // ahead of the MMAs, which are bound by the ~115-cycle cost of each
   // 128-row tcgen05.mma.)
-  int xstages = n_iters < 4 ? n_iters : 4;
+  const int xmax = nb > 64 ? 2 : 4;  // 32 KiB activation tiles at NB = 128
+  int xstages = n_iters < xmax ? n_iters : xmax;
   xstages = xstages < 1 ? 1 : xstages;
   const size_t fixed = umma_smem(nb, 0, xstages, split);
   const size_t budget = 100 * 1024;
