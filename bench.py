@@ -451,6 +451,81 @@ def w8a8_sweep(device, seed: int) -> dict:
     }
 
 
+HEADS, HEAD_N, HEAD_K, HEAD_ROWS = 15, 2048, 1024, 8
+
+
+def grouped_heads(device, seed: int) -> dict:
+    """Config 5's second part: the code predictor's 15 codebook heads (lm_head[i] 1024 -> 2048,
+    qtts/models/code_predictor.py:159-161, 235) as int8 W8A16 at M = 8 rows per head: one
+    grouped launch (qtts_w8a16_grouped_gemm) against 15 separate library calls and against
+    cuBLAS bf16 (torch.bmm over the stacked heads, and 15 F.linear calls); plus the engine's
+    form, one head per call chosen by a device index (the heads run one per sequential step,
+    so a graph of one step serves every step). Stacked weights rotate through >= 256 MB."""
+    import torch.nn.functional as F
+
+    from qtts_b200.quant import kernels as qk
+
+    gen = torch.Generator(device=device)
+    gen.manual_seed(seed + 19)
+    g_, n, k, m = HEADS, HEAD_N, HEAD_K, HEAD_ROWS
+    p = pool_size(g_ * n, k)
+    wq = torch.empty((p, g_ * n, k), dtype=torch.int8, device=device)
+    ws = torch.empty((p, g_ * n), dtype=torch.bfloat16, device=device)
+    wb = torch.empty((p, g_, n, k), dtype=torch.bfloat16, device=device)
+    for i in range(p):
+        w = torch.randn((g_ * n, k), generator=gen, device=device) * 0.02
+        q, s_ = qk.quantize_int8_rows(w)
+        wq[i].copy_(q)
+        ws[i].copy_(s_.to(torch.bfloat16))
+        wb[i].copy_(w.view(g_, n, k).to(torch.bfloat16))
+        del w, q, s_
+    x = torch.randn((g_, m, k), generator=gen, device=device).to(torch.bfloat16)
+    index = torch.full((1,), 7, dtype=torch.int64, device=device)
+
+    def grouped():
+        for c in range(CALLS_PER_GRAPH):
+            qk.w8_grouped_gemm(x, wq[c % p], ws[c % p])
+
+    def separate():
+        for c in range(CALLS_PER_GRAPH):
+            for h in range(g_):
+                qk.w8_gemm(x[h], wq[c % p, h * n:(h + 1) * n], ws[c % p, h * n:(h + 1) * n])
+
+    def indexed():
+        for c in range(CALLS_PER_GRAPH):
+            qk.w8_indexed_gemm(x[0], wq[c % p], ws[c % p], index, g_)
+
+    def bf16_bmm():
+        for c in range(CALLS_PER_GRAPH):
+            torch.bmm(x, wb[c % p].transpose(1, 2))
+
+    def bf16_separate():
+        for c in range(CALLS_PER_GRAPH):
+            for h in range(g_):
+                F.linear(x[h], wb[c % p, h])
+
+    us = {name: graph_us_per_call(fn) for name, fn in (("grouped", grouped), ("separate", separate),
+                                                       ("indexed", indexed), ("bf16_bmm", bf16_bmm),
+                                                       ("bf16_separate", bf16_separate))}
+    all_bytes = g_ * n * k + 2 * g_ * n + 2 * g_ * m * k + 2 * g_ * m * n
+    one_bytes = n * k + 2 * n + 2 * m * k + 2 * m * n
+    del wq, ws, wb
+    torch.cuda.empty_cache()
+    return {
+        "workload": f"{g_} codebook heads {n}x{k} int8 W8A16, M = {m} rows per head; weights rotate through "
+        ">= 256 MB",
+        "grouped_us": round(us["grouped"], 3),
+        "grouped_gbs": round(all_bytes / (us["grouped"] * 1e-6) / 1e9, 1),
+        "separate_us": round(us["separate"], 3),
+        "bf16_bmm_us": round(us["bf16_bmm"], 3),
+        "bf16_separate_us": round(us["bf16_separate"], 3),
+        "speedup_vs_separate": round(us["separate"] / us["grouped"], 3),
+        "speedup_vs_bf16_bmm": round(us["bf16_bmm"] / us["grouped"], 3),
+        "indexed_one_head_us": round(us["indexed"], 3),
+        "indexed_one_head_gbs": round(one_bytes / (us["indexed"] * 1e-6) / 1e9, 1),
+    }
+
+
 PROLOGUE_ROWS = (1, 8, 16, 64)
 
 
@@ -943,6 +1018,7 @@ def run_gpu_arm(args) -> None:
     fp8w = fp8w_sweep(device, args.seed) if args.fp8w and rank == 0 else None
     w8a8 = w8a8_sweep(device, args.seed) if args.w8a8 and rank == 0 else None
     prologue = prologue_sweep(device, args.seed) if args.prologue and rank == 0 else None
+    heads = grouped_heads(device, args.seed) if args.heads and rank == 0 else None
     barrier(world)
     sharded = sharded_sweep(world, rank, device, args.seed) if args.sharded else None
     talker = talker_frames(args.seed) if args.talker and rank == 0 else None
@@ -1028,6 +1104,7 @@ def run_gpu_arm(args) -> None:
             "fp8_weight_only": fp8w,
             "int8_w8a8": w8a8,
             "fused_prologues": prologue,
+            "grouped_heads": heads,
             "sharded": sharded,
             "talker": talker,
         }
@@ -1135,6 +1212,8 @@ def main(argv=None) -> int:
     ap.add_argument("--no-w8a8", dest="w8a8", action="store_false", help="skip the int8 W8A8 sweep")
     ap.add_argument("--no-prologue", dest="prologue", action="store_false",
                     help="skip the fused RMSNorm / SiLU·up sweep")
+    ap.add_argument("--no-heads", dest="heads", action="store_false",
+                    help="skip the grouped 15-codebook-head measurement")
     ap.add_argument("--no-talker", dest="talker", action="store_false",
                     help="skip the config-4 talker + code predictor frames/s measurement")
     ap.add_argument("--no-sharded", dest="sharded", action="store_false",
