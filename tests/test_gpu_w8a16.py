@@ -129,7 +129,8 @@ def test_ragged_shapes(n, k, m):
     assert_close_to_oracle(out, ref, f"N={n} K={k} M={m}")
 
 
-@pytest.mark.parametrize("n,k,m", [(80, 272, 3), (300, 2048, 130), (4096, 2048, 17), (12288, 2048, 64), (1, 16, 9)])
+@pytest.mark.parametrize("n,k,m", [(80, 272, 3), (300, 2048, 130), (4096, 2048, 17), (12288, 2048, 64), (1, 16, 9),
+                                   (1024, 2048, 64), (1024, 3072, 32), (12288, 2048, 128)])
 def test_umma_ragged_shapes(n, k, m):
     x, q, s = seeded_case(n, k, m, seed=13)
     ref = oracle.w8a16_reference(x.float().numpy(), q, scale_values(s, torch.bfloat16))

@@ -31,6 +31,10 @@ def _lib():
         (2048, 6144, 4, "skinny_w8a16_kernel", 8, 64, 256),  # down_proj
         (4096, 2048, 32, "umma_w8a16_kernel", 4, 128, 128),
         (12288, 2048, 64, "umma_w8a16_kernel", 1, 128, 96),
+        # code predictor o_proj / down_proj: 8 weight tiles, clusters of 8 (64 CTAs)
+        (1024, 2048, 64, "umma_w8a16_kernel", 8, 128, 64),
+        (1024, 3072, 32, "umma_w8a16_kernel", 8, 128, 64),
+        (2048, 2048, 64, "umma_w8a16_kernel", 4, 128, 64),
         # past 64 rows: one 128-column tile when 64-column tiles would overflow a wave
         (12288, 2048, 128, "umma_w8a16_kernel", 1, 128, 96),
         (4096, 1024, 128, "umma_w8a16_kernel", 2, 128, 128),
