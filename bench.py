@@ -855,7 +855,8 @@ def talker_frames(seed: int, batch: int = 8) -> dict:
     torch.cuda.empty_cache()
     return {
         "workload": "config 4: random-init talker decode step (28 layers, 512-token KV cache, masked codec head) "
-        "+ code predictor (5 layers, 15 sequential codebook steps, 15 heads) at batch 8, one CUDA graph per frame",
+        "+ code predictor (5 layers, 15 sequential codebook steps, 15 heads) at batch 8, one CUDA graph per frame; "
+        "median of 5 windows of 20 replays",
         "frames_per_s_int8": round(fps_int8, 1),
         "frames_per_s_bf16": round(fps_bf16, 1),
         "frames_per_s_int8_torch_prologues": round(fps_unfused, 1),

@@ -263,18 +263,23 @@ class Frame:
             self.predictor.small_to_mtp_projection)
 
 
-def timed_frames_per_s(frame: Frame, reps: int = 20) -> tuple[float, float]:
-    """(frames/s, ms per frame step) over ``reps`` graph replays; frames/s = batch / step time."""
+def timed_frames_per_s(frame: Frame, reps: int = 20, windows: int = 5) -> tuple[float, float]:
+    """(frames/s, ms per frame step): the median over ``windows`` timing windows of ``reps``
+    graph replays each (one window alone has read 10-15 % fast or slow on a shared box);
+    frames/s = batch / step time."""
     if frame.graph is None:
         frame.capture()
     stream = torch.cuda.current_stream()
     frame.graph.replay()
     torch.cuda.synchronize()
-    e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
-    e0.record(stream)
-    for _ in range(reps):
-        frame.graph.replay()
-    e1.record(stream)
-    torch.cuda.synchronize()
-    ms = e0.elapsed_time(e1) / reps
+    times = []
+    for _ in range(windows):
+        e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        e0.record(stream)
+        for _ in range(reps):
+            frame.graph.replay()
+        e1.record(stream)
+        torch.cuda.synchronize()
+        times.append(e0.elapsed_time(e1) / reps)
+    ms = sorted(times)[len(times) // 2]
     return frame.batch / (ms * 1e-3), ms
