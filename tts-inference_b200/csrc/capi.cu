@@ -818,7 +818,7 @@ int qtts_w8a16_gemm_prologue(const void* x, int64_t ldx, int x_dtype, int prolog
   const int family = chosen_family(x, ldx, x_dtype, w, ldw, M, N, K, variant);
   if (family < 0) return QTTS_ERR_ALIGN;
   const bool fusable = M <= 16 && (family == 0x100 || family == 0x300) &&
-                       (prologue != QTTS_PROLOGUE_RMSNORM || (aligned16(norm_weight) && K <= 8 * 32 * 32));
+                       (prologue != QTTS_PROLOGUE_RMSNORM || (aligned16(norm_weight) && K <= 8 * 32 * kMaxFusedNormGroups));
   if (fusable) {
     const FusedPrologue pro{prologue == QTTS_PROLOGUE_RMSNORM ? kProRmsNorm : kProSiluMul, norm_weight, eps};
     return w8a16_dispatch(x, 0, ldx, x_dtype, w, ldw, scale, scale_dtype, bias, out, 0, ldo, 1, M, N, K, nullptr,
@@ -860,7 +860,7 @@ int qtts_w8a16_gemm_prologue_fused(int M, int N, int K, int prologue, int varian
     family = auto_family(M, N, K, 1, kWInt8, false, &rgroups);
   }
   // The fused norm keeps one group sum per 256 columns of a row: K <= 8192.
-  if (prologue == QTTS_PROLOGUE_RMSNORM && K > 8 * 32 * 32) return 0;
+  if (prologue == QTTS_PROLOGUE_RMSNORM && K > 8 * 32 * kMaxFusedNormGroups) return 0;
   return (M <= 16 && (family == 0x100 || family == 0x300)) ? 1 : 0;
 }
 
