@@ -104,3 +104,35 @@ def test_library_has_no_torch_dependency():
     out = subprocess.run(["ldd", str(LIB_PATH)], capture_output=True, text=True).stdout
     assert "torch" not in out and "libc10" not in out
     assert ctypes.CDLL(str(LIB_PATH)).qtts_abi_version() == 1
+
+
+def test_prologue_entry_points_validate(lib):
+    """The activation prologues reject bad arguments on the host, before any device call
+    (so no GPU is needed to see it); valid arguments reach the device check."""
+    bf16, f1 = nat.BF16, ctypes.c_float(1e-6)
+    # qtts_rms_norm(x, ldx, weight, out, ldo, dtype, rows, width, eps, flags, stream)
+    assert lib.qtts_rms_norm(16, 64, 16, 16, 64, bf16, -1, 64, f1, 0, None) == 2
+    assert lib.qtts_rms_norm(16, 64, 16, 16, 64, bf16, 0, 64, f1, 0, None) == 0  # no rows: no-op
+    assert lib.qtts_rms_norm(None, 64, 16, 16, 64, bf16, 4, 64, f1, 0, None) == 1
+    assert lib.qtts_rms_norm(16, 32, 16, 16, 64, bf16, 4, 64, f1, 0, None) == 2  # ldx < width
+    assert lib.qtts_rms_norm(16, 1 << 17, 16, 16, 1 << 17, bf16, 4, 65544, f1, 0, None) == 2  # too wide
+    assert lib.qtts_rms_norm(16, 64, 16, 16, 64, 9, 4, 64, f1, 0, None) == 4
+    assert lib.qtts_rms_norm(16, 64, 16, 16, 64, bf16, 4, 64, f1, 0, None) == 5  # no sm_100 device
+    # qtts_silu_mul(gate_up, ld_in, out, ldo, dtype, rows, width, flags, stream)
+    assert lib.qtts_silu_mul(16, 64, 16, 64, bf16, 4, 64, 0, None) == 2  # ld_in < 2 * width
+    assert lib.qtts_silu_mul(None, 128, 16, 64, bf16, 4, 64, 0, None) == 1
+    assert lib.qtts_silu_mul(16, 128, 16, 64, bf16, 4, 64, 0, None) == 5
+
+    # qtts_w8a16_gemm_prologue(x, ldx, x_dtype, prologue, norm_weight, eps, w, ldw, scale,
+    #   scale_dtype, bias, out, ldo, M, N, K, workspace, variant, flags, stream)
+    def call(prologue=nat.PROLOGUE_RMSNORM, ldx=256, norm=16, m=8, variant=0, workspace=None):
+        return lib.qtts_w8a16_gemm_prologue(16, ldx, bf16, prologue, norm, f1, 16, 256, 16, bf16, None, 16, 128,
+                                            m, 128, 256, workspace, variant, 0, None)
+
+    assert call(prologue=9) == 7
+    assert call(norm=None) == 1
+    assert call(prologue=nat.PROLOGUE_SILU_MUL, ldx=256) == 2  # [gate | up] rows need ldx >= 2K
+    assert call(m=0) == 0
+    assert call(m=40) == 1  # not fused at M > 16: the workspace is required
+    assert call(m=40, workspace=16) == 5  # chained form, valid: reaches the device check
+    assert call() == 5  # fused form, valid
