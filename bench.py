@@ -1122,11 +1122,35 @@ def run_single(spec: str, calls: int = 3) -> None:
     """One (shape, M) point, `calls` launches with an L2 flush before each:
     a small case for `ncu` captures. spec = "<shape>:<M>[:<variant>]" (W8A16),
     "fp8:<shape>:<M>" (activation quantization + fp8 GEMM), "fp8w:<shape>:<M>"
-    (fp8 weight-only) or "rms:<shape>:<M>" / "silu:<shape>:<M>" (W8A16 with its
-    RMSNorm / SiLU·up prologue, qtts_w8a16_gemm_prologue)."""
+    (fp8 weight-only), "rms:<shape>:<M>" / "silu:<shape>:<M>" (W8A16 with its
+    RMSNorm / SiLU·up prologue, qtts_w8a16_gemm_prologue) or "frame" (one eager
+    config-4 frame inside a CUDA profiler range)."""
     from qtts_b200.quant import kernels as qk
 
     parts = spec.split(":")
+    if parts[0] == "frame":
+        # One eager config-4 frame (batch 8, all linears int8 with the fused prologues), with
+        # the CUDA profiler range opened around it only (ncu --profile-from-start off).
+        from qtts_b200.config import QuantConfig
+        from qtts_b200.decode_step import Frame
+        from qtts_b200.quant import build_method, quantize_module
+
+        torch.cuda.set_device(0)
+        frame = Frame(8, seed=0)
+        cfg = QuantConfig(method="int8_weight_only", targets=("talker", "code_predictor"), exclude_substrings=(),
+                          calibrate=False)
+        method = build_method(cfg)
+        quantize_module(frame.talker, method, cfg, "talker")
+        quantize_module(frame.predictor, method, cfg, "code_predictor")
+        with torch.no_grad():
+            frame.run()
+            torch.cuda.synchronize()
+            torch.cuda.profiler.start()
+            frame.run()
+            torch.cuda.synchronize()
+            torch.cuda.profiler.stop()
+        print(json.dumps({"single": spec, "ok": True}))
+        return
     if parts[0] in ("rms", "silu"):
         label, m = parts[1], int(parts[2])
         n, k = {lab: (n_, k_) for lab, n_, k_ in SHAPES}[label]
