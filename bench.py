@@ -16,9 +16,8 @@ reads a different copy of the weight: per shape a pool of at least 256 MB
 weights from HBM.
 
 ``value`` = algorithmic bytes of all calls (int8 W + bf16 scale + bf16 x +
-bf16 out) / device time, aggregated over ranks; ``e2e`` adds, per point, the
-host->device copy of x from pinned memory and the device->host copy of the
-output. ``--impl reference`` times the reference's eager CPU path
+bf16 out) / device time, aggregated over ranks; ``e2e`` is the same sweep with
+every call copying its x in from pinned host memory and its output back out. ``--impl reference`` times the reference's eager CPU path
 (``F.linear(x, q.to(bf16) * scale)``, restated in ``oracle/``) on the host
 cores instead.
 
@@ -53,7 +52,7 @@ REPLAYS_PER_POINT = 9  # 9 x 224 = 2016 calls per point (--replays)
 POOL_MIN_BYTES = 256 << 20
 METRIC = "int8 W8A16 GEMM HBM GB/s (talker linear sweep, M=1..64)"
 # DRAM bytes per launch of the dominant kernel (skinny_w8a16_kernel, down_proj
-# M=1) from one `ncu --set full` capture (profiles/skinny_w8a16_down_proj_m1.md):
+# M=1) from one `ncu --set full` capture of that launch:
 # dram__bytes_read.sum + dram__bytes_write.sum, against its algorithmic bytes.
 NCU_TRAFFIC = {"case": "down_proj 2048x6144, M=1", "bytes_per_launch": 12666624, "algorithmic_bytes": 12603392}
 
@@ -253,6 +252,7 @@ class Point:
         self.label, self.n, self.k, self.m = label, n, k, m
         self.bytes = algo_bytes(n, k, m)
         self.graph = None
+        self.e2e_graph = None
         self.bf16_graph = None
 
 
@@ -875,6 +875,131 @@ def talker_frames(seed: int, batch: int = 8) -> dict:
     }
 
 
+def triton_sweep(points, xs, outs, pools, per_point, stream) -> str:
+    """Time the reference's Triton ``w8_gemm`` (qtts/quant/kernels.py:89-177, installed
+    unmodified under baseline/_ref) at every config-2 point: the same x, the same rotating
+    weight pool and the same CUDA-graph form as the library's calls. Adds ``triton_us`` and
+    ``speedup_vs_triton`` per point; returns "ok" or why the reference could not run."""
+    try:
+        from baseline import ref_frame as rf
+
+        ref_gemm = rf.qtts().quant.kernels.w8_gemm
+        for pt in points:
+            x, out = xs[(pt.label, pt.m)], outs[(pt.label, pt.m)]
+            qs, ss = pools[pt.label]
+            check = ref_gemm(x, qs[0], ss[0])
+
+            def tcalls(x=x, qs=qs, ss=ss):
+                p = qs.shape[0]
+                for c in range(CALLS_PER_GRAPH):
+                    ref_gemm(x, qs[c % p], ss[c % p])
+
+            us = graph_us_per_call(tcalls)
+            d = per_point[pt.label][str(pt.m)]
+            d["triton_us"] = round(us, 3)
+            d["speedup_vs_triton"] = round(us / d["us"], 3)
+            torch.cuda.synchronize()
+            from qtts_b200.quant import kernels as qk
+
+            mine = qk.w8_gemm(x, qs[0], ss[0])
+            d["rel_err_vs_triton"] = float(((mine.float() - check.float()).abs().max()
+                                            / check.float().abs().max().clamp_min(1e-30)).item())
+        torch.cuda.empty_cache()
+        return "ok"
+    except Exception as exc:  # the comparison arm is optional; the library's numbers stand alone
+        torch.cuda.synchronize()
+        return f"unavailable: {type(exc).__name__}: {str(exc).splitlines()[0] if str(exc) else ''}"
+
+
+def reference_model_frames(seed: int, batch: int = 8) -> dict:
+    """Config 4 on the reference's own model (baseline/ref_frame.py): its Qwen3TTSTalker and
+    CodePredictor, quantized by its apply_quantization (every linear, exclude_substrings=())
+    and replayed through its TalkerDecodeGraphs / CodePredictorGraphs, one frame as its
+    TalkerRunner.decode_step runs it (greedy). Arms: bf16; int8 on the reference's Triton
+    kernel; int8 on this library (the one-file kernel swap), both uncalibrated on the same
+    weights and calibrated (--quant-calibrate, each arm's kernel timed against F.linear);
+    plus the greedy code-0 ids of one talker step, library against the reference's eager
+    dequantize-then-matmul and Triton paths, with the top-1/top-2 logit margins."""
+    import gc
+
+    try:
+        from baseline import ref_frame as rf
+
+        rf.qtts()
+    except Exception as exc:
+        return {"unavailable": f"{type(exc).__name__}: {exc}"}
+    out: dict = {"workload": "reference Qwen3TTSTalker + CodePredictor (baseline/_ref, unmodified) at batch 8, "
+                 "512 prior tokens (key length bucketed to 768), its own CUDA graphs, greedy; frames/s = batch / "
+                 "median frame time of 5 windows of 20 frames", "errors": {}}
+
+    def release():
+        gc.collect()
+        torch.cuda.synchronize()
+        torch.cuda.empty_cache()
+
+    def timed(key, talker, predictor):
+        try:
+            fr = rf.RefFrame(talker, predictor, batch, seed)
+            fps, ms = fr.frames_per_s()
+            out[f"frames_per_s_{key}"] = round(fps, 1)
+            out[f"ms_per_frame_{key}"] = round(ms, 3)
+            del fr
+        except Exception as exc:
+            out["errors"][key] = f"{type(exc).__name__}: {str(exc).splitlines()[0] if str(exc) else ''}"
+        release()
+
+    talker, predictor, _ = rf.build_models(batch=batch, quant=None, seed=seed)
+    timed("ref_bf16", talker, predictor)
+    del talker, predictor
+    release()
+
+    talker, predictor, rep = rf.build_models(batch=batch, quant="int8_weight_only", calibrate=False,
+                                             kernels="library", seed=seed)
+    out["layers_int8"] = {k: v.get("converted") for k, v in rep.items()}
+    for kind, key in (("triton", "ref_triton"), ("library", "ref_model_with_library")):
+        rf.set_kernels(kind)
+        timed(key, talker, predictor)
+    # code-0 parity on one talker step (same int8 buffers, three GEMMs)
+    try:
+        _, embeds = rf.initial_state(batch, seed)
+        logits = {}
+        for kind in ("library", "eager", "triton"):
+            rf.set_kernels(kind)
+            logits[kind] = rf.talker_step_logits(talker, embeds.clone()).float()
+        top2 = logits["eager"].topk(2, dim=-1).values
+        finite = torch.isfinite(logits["eager"])
+        ids = {k: v.argmax(-1) for k, v in logits.items()}
+        out["code0_library_vs_ref_eager"] = float((ids["library"] == ids["eager"]).float().mean().item())
+        out["code0_library_vs_ref_triton"] = float((ids["library"] == ids["triton"]).float().mean().item())
+        out["code0_top1_top2_margins"] = [round(v, 4) for v in (top2[:, 0] - top2[:, 1]).tolist()]
+        out["logit_max_abs_diff_library_vs_eager"] = round((logits["library"] - logits["eager"])[finite].abs().max().item(), 5)
+        out["logit_max_abs_diff_triton_vs_eager"] = round((logits["triton"] - logits["eager"])[finite].abs().max().item(), 5)
+    except Exception as exc:
+        out["errors"]["code0"] = f"{type(exc).__name__}: {str(exc).splitlines()[0] if str(exc) else ''}"
+    rf.set_kernels("library")
+    del talker, predictor
+    release()
+
+    for kind, key in (("triton", "ref_triton_calibrated"), ("library", "ref_model_with_library_calibrated")):
+        try:
+            talker, predictor, rep = rf.build_models(batch=batch, quant="int8_weight_only", calibrate=True,
+                                                     kernels=kind, seed=seed)
+            out[f"layers_int8_{key}"] = {k: {"converted": v.get("converted"), "declined": v.get("declined")}
+                                         for k, v in rep.items()}
+            timed(key, talker, predictor)
+            del talker, predictor
+        except Exception as exc:
+            out["errors"][key] = f"{type(exc).__name__}: {str(exc).splitlines()[0] if str(exc) else ''}"
+        release()
+    rf.set_kernels("library")
+    if "frames_per_s_ref_triton" in out and "frames_per_s_ref_model_with_library" in out:
+        out["speedup_library_vs_triton"] = round(out["frames_per_s_ref_model_with_library"]
+                                                 / out["frames_per_s_ref_triton"], 3)
+    if not out["errors"]:
+        del out["errors"]
+    return out
+
+
 def auto_kernel(m: int, n: int, k: int) -> str:
     """The kernel the library's automatic choice launches (asked of the library's planner)."""
     from qtts_b200 import _native as nat
@@ -932,7 +1057,8 @@ def run_gpu_arm(args) -> None:
     torch.cuda.synchronize()
     barrier(world)
 
-    sampler = ClockSampler(local, ROOT / "gpurun_out" / "bench_clocks.csv" if (ROOT / "gpurun_out").is_dir() else None)
+    sampler = ClockSampler(local, Path(os.environ["QTTS_BENCH_CLOCKS_LOG"]) if "QTTS_BENCH_CLOCKS_LOG" in os.environ
+                           else None)
     sampler.start()
     time.sleep(0.3)
     torch.cuda.synchronize()
@@ -1011,6 +1137,11 @@ def run_gpu_arm(args) -> None:
         del bf16_pools
         torch.cuda.empty_cache()
 
+    # ---- the reference's own Triton kernel on the same points (outside the timed region)
+    triton_status = None
+    if args.triton_compare:
+        triton_status = triton_sweep(points, xs, outs, pools, per_point, stream)
+
     torch.cuda.synchronize()
     status_sweep = nat.device_status()  # before the sections (the sharded one resets the word)
 
@@ -1023,19 +1154,34 @@ def run_gpu_arm(args) -> None:
     barrier(world)
     sharded = sharded_sweep(world, rank, device, args.seed) if args.sharded else None
     talker = talker_frames(args.seed) if args.talker and rank == 0 else None
+    if talker is not None and args.ref_model:
+        talker["reference_model"] = reference_model_frames(args.seed)
     barrier(world)
 
-    # ---- end to end: host buffers in, results out, through the public API
-    h2d = sum(pt.m * pt.k * 2 for pt in points)
-    d2h = sum(pt.m * pt.n * 2 for pt in points)
+    # ---- end to end through the public API with host buffers: every call copies its x in
+    # from pinned host memory and its output back out (both copies captured with the call).
+    calls_per_step = CALLS_PER_GRAPH * REPLAYS_PER_POINT
+    h2d = sum(pt.m * pt.k * 2 for pt in points) * calls_per_step
+    d2h = sum(pt.m * pt.n * 2 for pt in points) * calls_per_step
+    variant = nat.VARIANT_AUTO if args.variant is None else int(args.variant, 0)
+    for pt in points:
+        key = (pt.label, pt.m)
+        qs, ss = pools[pt.label]
+
+        def e2e_calls(x=xs[key], out=outs[key], xh=xs_host[key], oh=outs_host[key], qs=qs, ss=ss):
+            p = qs.shape[0]
+            for c in range(CALLS_PER_GRAPH):
+                x.copy_(xh, non_blocking=True)
+                qk.w8_gemm(x, qs[c % p], ss[c % p], None, out=out, variant=variant)
+                oh.copy_(out, non_blocking=True)
+
+        pt.graph = None
+        pt.e2e_graph = capture(e2e_calls)
 
     def e2e_step():
         for pt in points:
-            key = (pt.label, pt.m)
-            xs[key].copy_(xs_host[key], non_blocking=True)
             for _ in range(REPLAYS_PER_POINT):
-                pt.graph.replay()
-            outs_host[key].copy_(outs[key], non_blocking=True)
+                pt.e2e_graph.replay()
 
     for _ in range(max(1, args.warmup)):
         e2e_step()
@@ -1100,6 +1246,7 @@ def run_gpu_arm(args) -> None:
             "clocks": clocks,
             "gpu_launches": launches_per_step * args.steps,
             "device_status": status,
+            "triton_compare": triton_status,
             "per_point": per_point,
             "fp8": fp8,
             "fp8_weight_only": fp8w,
@@ -1115,6 +1262,7 @@ def run_gpu_arm(args) -> None:
 
         for pt in points:
             pt.graph = None
+            pt.e2e_graph = None
         dist.destroy_process_group()
 
 
@@ -1243,6 +1391,10 @@ def main(argv=None) -> int:
                     help="skip the config-4 talker + code predictor frames/s measurement")
     ap.add_argument("--no-sharded", dest="sharded", action="store_false",
                     help="skip the config-5 N-sharded GEMM + all-gather sweep")
+    ap.add_argument("--no-triton-compare", dest="triton_compare", action="store_false",
+                    help="skip timing the reference's Triton w8_gemm per point")
+    ap.add_argument("--no-ref-model", dest="ref_model", action="store_false",
+                    help="skip the config-4 frame on the reference's own model")
     ap.add_argument("--no-cpu-baseline", action="store_true")
     ap.add_argument("--cpu-seconds", type=float, default=15.0)
     ap.add_argument("--replays", type=int, default=REPLAYS_PER_POINT,
