@@ -304,33 +304,19 @@ QTTS_API int qtts_fp8_quant_rows(const void* x, int64_t ldx, int x_dtype,
 
 /* Scaled e4m3 GEMM, the torch._scaled_mm call of Fp8Method.apply
  * (qtts/quant/fp8.py:79-88):
- *   out[m,n] = cast_out( (sum_k xq[m,k] * wq[n,k]) * scale_x[m] * scale_w[n]
- *                        + float(bias[n]) )
- * xq: [M, K] e4m3 (ld ldxq); wq: [N, K] e4m3 (ld ldw); out: [M, N] of out_dtype
- * (BF16/FP16/FP32) with leading dim ldo; bias [N] of out_dtype or NULL.
- * Needs K % 16 == 0 and 16-byte aligned rows. */
+ *   y[m,n]   = cast_out( (sum_k xq[m,k] * wq[n,k]) * scale_x[m] * scale_w[n] )
+ *   out[m,n] = bias ? cast_out( float(y[m,n]) + float(bias[n]) ) : y[m,n]
+ * i.e. _scaled_mm(out_dtype) rounded first and the bias added in the output
+ * dtype, as the reference does. xq: [M, K] e4m3 (ld ldxq); wq: [N, K] e4m3
+ * (ld ldw); out: [M, N] of out_dtype (BF16/FP16/FP32) with leading dim ldo;
+ * bias [N] of out_dtype or NULL. The tcgen05 variants need K % 16 == 0 and
+ * 16-byte aligned rows; AUTO takes a SIMT kernel (QTTS_VARIANT_GENERIC, any
+ * K and stride) for shapes they cannot. */
 QTTS_API int qtts_fp8_gemm(const uint8_t* xq, int64_t ldxq, const float* scale_x,
                   const uint8_t* wq, int64_t ldw, const float* scale_w,
                   const void* bias, void* out, int64_t ldo, int out_dtype,
                   int M, int N, int K, int variant, unsigned flags, void* stream);
 
-/* ---- fp8 linear without caller-provided scratch ----------------------------
- * No counterpart in the reference. qtts_fp8_quant_rows followed by
- * qtts_fp8_gemm (variant AUTO) -- the whole of Fp8Method.apply -- with the
- * intermediate e4m3 codes and row scales kept in one fixed device array of the
- * library instead of memory the caller allocates, for callers with no device
- * allocator of their own. Nothing is allocated by the call.
- *   out[m,n] = same value as the two-step sequence on the same inputs.
- * x: [M, K] (BF16/FP16/FP32, ld ldx); wq: [N, K] e4m3 (ld ldw); scale_w: [N]
- * fp32; bias [N] of out_dtype or NULL; out: [M, N] of out_dtype (ld ldo).
- * Limits: M <= QTTS_NOALLOC_MAX_ROWS and M * K <= QTTS_NOALLOC_MAX_CODES, else
- * QTTS_ERR_SHAPE and nothing is launched. The array is shared by every call on
- * a device: calls that may run at the same time on one device (different
- * streams) race on it; calls ordered on one stream are safe. Nothing in it
- * needs to start at zero. The first call on each device looks its address up
- * (with that device current), so make one call before recording a graph. */
-#define QTTS_NOALLOC_MAX_ROWS 1024
-#define QTTS_NOALLOC_MAX_CODES (1 << 20)
 /* ---- int8 W8A8 (Int8Method) --------------------------------------------------
  * Per-token int8 quantization of the activations of Int8Method.apply
  * (qtts/quant/int8.py:138-140), each step in the activation dtype as torch
@@ -352,6 +338,23 @@ QTTS_API int qtts_i8_gemm(const int8_t* xq, int64_t ldxq, const float* scale_x, 
                           const float* scale_w, const void* bias, void* out, int64_t ldo, int out_dtype, int M, int N,
                           int K, int variant, unsigned flags, void* stream);
 
+/* ---- fp8 linear without caller-provided scratch ----------------------------
+ * No counterpart in the reference. qtts_fp8_quant_rows followed by
+ * qtts_fp8_gemm (variant AUTO) -- the whole of Fp8Method.apply -- with the
+ * intermediate e4m3 codes and row scales kept in one fixed device array of the
+ * library instead of memory the caller allocates, for callers with no device
+ * allocator of their own. Nothing is allocated by the call.
+ *   out[m,n] = same value as the two-step sequence on the same inputs.
+ * x: [M, K] (BF16/FP16/FP32, ld ldx); wq: [N, K] e4m3 (ld ldw); scale_w: [N]
+ * fp32; bias [N] of out_dtype or NULL; out: [M, N] of out_dtype (ld ldo).
+ * Limits: M <= QTTS_NOALLOC_MAX_ROWS and M * K <= QTTS_NOALLOC_MAX_CODES, else
+ * QTTS_ERR_SHAPE and nothing is launched. The array is shared by every call on
+ * a device: calls that may run at the same time on one device (different
+ * streams) race on it; calls ordered on one stream are safe. Nothing in it
+ * needs to start at zero. The first call on each device looks its address up
+ * (with that device current), so make one call before recording a graph. */
+#define QTTS_NOALLOC_MAX_ROWS 1024
+#define QTTS_NOALLOC_MAX_CODES (1 << 20)
 QTTS_API int qtts_fp8_linear_noalloc(const void* x, int64_t ldx, int x_dtype,
                             const uint8_t* wq, int64_t ldw, const float* scale_w,
                             const void* bias, void* out, int64_t ldo, int out_dtype,

@@ -81,6 +81,24 @@ def test_no_device_reports_arch_error(lib):
     assert _w8a16(lib) == 5  # QTTS_ERR_ARCH: valid arguments, no sm_100 device
 
 
+def test_noalloc_error_order(lib):
+    """The scratch-free fp8 linear validates like the others: argument errors first, then
+    QTTS_ERR_ARCH on a machine without an sm_100 device (before its scratch look-up)."""
+    import torch
+
+    def call(x=16, wq=16, sw=16, out=16, M=4, N=64, K=128, x_dtype=nat.BF16):
+        return lib.qtts_fp8_linear_noalloc(x, K, x_dtype, wq, K, sw, None, out, N, nat.BF16, M, N, K, 0, None)
+
+    assert call(M=-1) == 2
+    assert call(x=None) == 1
+    assert call(x_dtype=nat.INT8) == 4
+    assert call(M=1025) == 2  # beyond QTTS_NOALLOC_MAX_ROWS
+    assert call(M=1024, K=1025) == 2  # beyond QTTS_NOALLOC_MAX_CODES
+    assert call(M=0, x=None) == 0
+    if not torch.cuda.is_available():
+        assert call() == 5  # QTTS_ERR_ARCH, not a CUDA error from the symbol look-up
+
+
 def test_other_entry_points_validate(lib):
     assert lib.qtts_fp8_quant_rows(None, 16, nat.BF16, 16, 16, 2, 16, 0, None) == 1
     assert lib.qtts_fp8_quant_rows(16, 8, nat.BF16, 16, 16, 2, 16, 0, None) == 2

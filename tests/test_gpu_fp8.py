@@ -145,6 +145,10 @@ def test_variants_dtypes_bias(variant, out_dtype):
     out = qk.fp8_scaled_mm(xq, xs, wq, ws, bias.to(out_dtype).cuda(), out_dtype, variant=v)
     assert out.dtype == out_dtype
     check_close(out, ref, f"{variant} {out_dtype}", out_dtype)
+    # The bias is added as the reference adds it: to the GEMM's output already rounded to the
+    # output dtype, in that dtype (fp8.py:79-88) -- equal bit for bit to torch's add.
+    plain = qk.fp8_scaled_mm(xq, xs, wq, ws, None, out_dtype, variant=v)
+    assert torch.equal(out, plain + bias.to(out_dtype).cuda())
 
 
 @pytest.mark.parametrize("n,k,m", [(80, 272, 3), (300, 2048, 130), (1, 16, 1), (33, 1000, 5)])

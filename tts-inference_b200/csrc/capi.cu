@@ -216,7 +216,10 @@ __global__ void __launch_bounds__(256) generic_fp8_kernel(const GenericFp8Args a
 #pragma unroll
     for (int i = 0; i < 8; ++i) {
       if (m0 + i < a.M) {
-        o[static_cast<int64_t>(m0 + i) * a.ldo + n] = from_float<OT>(acc[i] * a.scale_x[m0 + i] * sw + b);
+        // _scaled_mm's output in the output dtype, then + bias in that dtype (qtts/quant/fp8.py:79-88).
+        const float y = acc[i] * a.scale_x[m0 + i] * sw;
+        o[static_cast<int64_t>(m0 + i) * a.ldo + n] =
+            from_float<OT>(a.bias != nullptr ? __fadd_rn(to_float(from_float<OT>(y)), b) : y);
       }
     }
   }

@@ -47,17 +47,22 @@ __device__ __forceinline__ void f8_tmem_ld<16>(uint32_t taddr, uint32_t (&r)[16]
       : "r"(taddr));
 }
 
-// Epilogue value of one accumulator word. e4m3 (I8 false): the fp32 sum scaled
-// and biased. int8 (I8 true, Int8Method, qtts/quant/int8.py:148-153): the
-// int32 sum converted and scaled in the reference's order and roundings,
-// ((float(acc) * sx) * sw) + bias, no fused multiply-add.
-template <bool I8>
+// Epilogue value of one accumulator word, before the final cast to OT.
+// e4m3 (I8 false, Fp8Method, qtts/quant/fp8.py:79-88): the fp32 sum scaled,
+// rounded to the output dtype as _scaled_mm(out_dtype=x.dtype) returns it, and
+// the bias then added as torch adds two tensors of that dtype (in fp32, one
+// rounding by the caller's cast). int8 (I8 true, Int8Method,
+// qtts/quant/int8.py:148-153): the int32 sum converted and scaled in the
+// reference's order and roundings, ((float(acc) * sx) * sw) + bias in fp32, no
+// fused multiply-add.
+template <bool I8, typename OT>
 __device__ __forceinline__ float w8a8_out(uint32_t acc_bits, float sx, float sw, float bias, bool has_bias) {
   if (I8) {
     float y = __fmul_rn(__fmul_rn(__int2float_rn(static_cast<int>(acc_bits)), sx), sw);
     return has_bias ? __fadd_rn(y, bias) : y;
   }
-  return __uint_as_float(acc_bits) * sx * sw + bias;
+  const float y = __uint_as_float(acc_bits) * sx * sw;
+  return has_bias ? __fadd_rn(to_float(from_float<OT>(y)), bias) : y;
 }
 
 template <int NB, typename OT, bool I8 = false>
@@ -218,7 +223,7 @@ __global__ void __launch_bounds__(kF8Threads, 1)
             const int col = c0 + c;
             if (col < mrows) {
               og[static_cast<int64_t>(col) * a.ldo + n] =
-                  from_float<OT>(w8a8_out<I8>(v[c], a.scale_x[m0 + col], sw, bias, a.bias != nullptr));
+                  from_float<OT>(w8a8_out<I8, OT>(v[c], a.scale_x[m0 + col], sw, bias, a.bias != nullptr));
             }
           }
         }
@@ -277,7 +282,7 @@ __global__ void __launch_bounds__(kF8Threads, 1)
               const int m = 4 * mq + q;
               if (m < mrows)
                 og[static_cast<int64_t>(m) * a.ldo + nn] =
-                    from_float<OT>(w8a8_out<I8>(rv[q], a.scale_x[m0 + m], sw, bias, a.bias != nullptr));
+                    from_float<OT>(w8a8_out<I8, OT>(rv[q], a.scale_x[m0 + m], sw, bias, a.bias != nullptr));
             }
           }
         }

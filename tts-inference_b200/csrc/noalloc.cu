@@ -25,15 +25,18 @@
 //     ordering between their streams) race on it. Calls ordered on one stream
 //     are safe.
 //   * the address is looked up with cudaGetSymbolAddress the first time the
-//     entry point runs on a device, with that device current, and cached; a
-//     caller that records its launches into a CUDA graph should make one call
-//     on each device before the capture starts, so the look-up (which may load
-//     the module) happens outside it.
+//     entry point runs on a device, with that device current, and cached
+//     together with the device's current context; a call under another context
+//     (after cudaDeviceReset the primary context, and with it the module, is
+//     created anew) looks it up again. A caller that records its launches into
+//     a CUDA graph should make one call on each device before the capture
+//     starts, so the look-up (which may load the module) happens outside it.
 
-#include <atomic>
-#include <cstdint>
-
+#include <cuda.h>
 #include <cuda_runtime.h>
+
+#include <cstdint>
+#include <mutex>
 
 #include "qtts_b200.h"
 
@@ -48,24 +51,76 @@ constexpr int kMaxDevices = 64;
 static_assert(kMaxCodes % 256 == 0, "the scale block must stay aligned");
 static __device__ __align__(256) unsigned char g_noalloc_scratch[kMaxCodes + 4 * kMaxRows];
 
-std::atomic<unsigned char*> g_scratch_addr[kMaxDevices];
+struct ScratchEntry {
+  CUcontext ctx = nullptr;
+  unsigned char* addr = nullptr;
+};
+ScratchEntry g_scratch[kMaxDevices];
+int g_cc_major[kMaxDevices] = {0};
+std::mutex g_scratch_mu;
 
-// The array's device address on the current device, looked up once per device.
-int scratch_address(unsigned char** out) {
+using CtxGetCurrentFn = CUresult (*)(CUcontext*);
+
+// cuCtxGetCurrent through the runtime's driver entry point (the library links
+// no driver library directly).
+CtxGetCurrentFn ctx_get_current() {
+  static CtxGetCurrentFn fn = [] {
+    void* p = nullptr;
+    cudaDriverEntryPointQueryResult q{};
+    if (cudaGetDriverEntryPoint("cuCtxGetCurrent", &p, cudaEnableDefault, &q) != cudaSuccess ||
+        q != cudaDriverEntryPointSuccess) {
+      (void)cudaGetLastError();
+      return static_cast<CtxGetCurrentFn>(nullptr);
+    }
+    return reinterpret_cast<CtxGetCurrentFn>(p);
+  }();
+  return fn;
+}
+
+CUcontext current_context() {
+  CtxGetCurrentFn fn = ctx_get_current();
+  CUcontext ctx = nullptr;
+  if (fn == nullptr || fn(&ctx) != CUDA_SUCCESS) return nullptr;
+  return ctx;
+}
+
+// The current device is an sm_100 part (QTTS_ERR_ARCH otherwise, as every
+// other entry point answers), checked before anything loads the module.
+int check_arch(int* dev_out) {
   int dev = -1;
-  if (cudaGetDevice(&dev) != cudaSuccess) return QTTS_ERR_CUDA;
-  if (dev < 0 || dev >= kMaxDevices) return QTTS_ERR_CUDA;
-  unsigned char* p = g_scratch_addr[dev].load(std::memory_order_acquire);
-  if (p == nullptr) {
+  if (cudaGetDevice(&dev) != cudaSuccess || dev < 0 || dev >= kMaxDevices) {
+    (void)cudaGetLastError();
+    return QTTS_ERR_ARCH;
+  }
+  std::lock_guard<std::mutex> lock(g_scratch_mu);
+  if (g_cc_major[dev] == 0) {
+    int major = 0;
+    if (cudaDeviceGetAttribute(&major, cudaDevAttrComputeCapabilityMajor, dev) != cudaSuccess) {
+      (void)cudaGetLastError();
+      return QTTS_ERR_ARCH;
+    }
+    g_cc_major[dev] = major;
+  }
+  *dev_out = dev;
+  return g_cc_major[dev] == 10 ? QTTS_OK : QTTS_ERR_ARCH;
+}
+
+// The array's device address under the current device's context, looked up
+// once per device and context.
+int scratch_address(int dev, unsigned char** out) {
+  std::lock_guard<std::mutex> lock(g_scratch_mu);
+  ScratchEntry& e = g_scratch[dev];
+  CUcontext ctx = current_context();
+  if (e.addr == nullptr || ctx == nullptr || ctx != e.ctx) {
     void* addr = nullptr;
     if (cudaGetSymbolAddress(&addr, g_noalloc_scratch) != cudaSuccess || addr == nullptr) {
       (void)cudaGetLastError();
       return QTTS_ERR_CUDA;
     }
-    p = static_cast<unsigned char*>(addr);
-    g_scratch_addr[dev].store(p, std::memory_order_release);
+    e.addr = static_cast<unsigned char*>(addr);
+    e.ctx = current_context();  // the look-up makes the primary context current
   }
-  *out = p;
+  *out = e.addr;
   return QTTS_OK;
 }
 
@@ -86,8 +141,11 @@ int qtts_fp8_linear_noalloc(const void* x, int64_t ldx, int x_dtype, const uint8
   if (!is_act_dtype(x_dtype) || !is_act_dtype(out_dtype)) return QTTS_ERR_DTYPE;
   if (ldx < K || ldw < K || ldo < N) return QTTS_ERR_SHAPE;
   if (M > kMaxRows || static_cast<int64_t>(M) * K > kMaxCodes) return QTTS_ERR_SHAPE;
+  int dev = -1;
+  const int arch = check_arch(&dev);
+  if (arch != QTTS_OK) return arch;
   unsigned char* scratch = nullptr;
-  const int r = scratch_address(&scratch);
+  const int r = scratch_address(dev, &scratch);
   if (r != QTTS_OK) return r;
   uint8_t* xq = scratch;
   float* scale_x = reinterpret_cast<float*>(scratch + kMaxCodes);

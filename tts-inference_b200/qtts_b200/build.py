@@ -60,20 +60,7 @@ def _stale() -> bool:
     return any(p.stat().st_mtime > built for p in deps)
 
 
-def build(force: bool = False, verbose: bool = False, extra_flags: list[str] | None = None) -> Path:
-    """Compile the library if any source is newer than it. Returns its path."""
-    if not force and not _stale():
-        return LIB_PATH
-    LIB_DIR.mkdir(parents=True, exist_ok=True)
-    tmp = LIB_PATH.with_suffix(".so.tmp")
-    cmd = (
-        [nvcc_path()]
-        + ARCH_FLAGS
-        + NVCC_FLAGS
-        + (extra_flags or [])
-        + ["-I", str(INCLUDE_DIR), "-I", str(SRC_DIR), "-shared", "-o", str(tmp)]
-        + [str(s) for s in sources()]
-    )
+def _run(cmd: list[str], verbose: bool) -> None:
     if verbose:
         print(" ".join(cmd), file=sys.stderr)
     proc = subprocess.run(cmd, capture_output=True, text=True)
@@ -81,6 +68,31 @@ def build(force: bool = False, verbose: bool = False, extra_flags: list[str] | N
         raise RuntimeError(f"nvcc failed ({proc.returncode}):\n{proc.stdout}\n{proc.stderr}")
     if verbose and (proc.stdout or proc.stderr):
         print(proc.stdout + proc.stderr, file=sys.stderr)
+
+
+def build(force: bool = False, verbose: bool = False, extra_flags: list[str] | None = None) -> Path:
+    """Compile the library if any source is newer than it. Returns its path.
+
+    Each source compiles to a relocatable object in parallel (``_build/``, one
+    nvcc per file), then one nvcc call device-links and links them into the
+    shared library."""
+    if not force and not _stale():
+        return LIB_PATH
+    from concurrent.futures import ThreadPoolExecutor
+
+    LIB_DIR.mkdir(parents=True, exist_ok=True)
+    obj_dir = PKG_DIR.parent / "_build"
+    obj_dir.mkdir(exist_ok=True)
+    flags = ARCH_FLAGS + NVCC_FLAGS + (extra_flags or []) + ["-I", str(INCLUDE_DIR), "-I", str(SRC_DIR)]
+    srcs = sources()
+    objs = [obj_dir / (s.stem + ".o") for s in srcs]
+    jobs = [[nvcc_path()] + flags + ["-c", str(s), "-o", str(o)] for s, o in zip(srcs, objs)]
+    with ThreadPoolExecutor(max_workers=max(1, min(len(jobs), os.cpu_count() or 1))) as pool:
+        for fut in [pool.submit(_run, cmd, verbose) for cmd in jobs]:
+            fut.result()
+    tmp = LIB_PATH.with_suffix(".so.tmp")
+    _run([nvcc_path()] + ARCH_FLAGS + ["-shared", "-Xcompiler", "-fPIC", "-o", str(tmp)] + [str(o) for o in objs],
+         verbose)
     os.replace(tmp, LIB_PATH)
     return LIB_PATH
 
