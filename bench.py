@@ -355,11 +355,26 @@ def fp8_sweep(device, seed: int) -> dict:
                     torch._scaled_mm(xq, wt[c % p], scale_a=sx, scale_b=ws[c % p].reshape(1, -1),
                                      bias=None, out_dtype=torch.bfloat16)
 
+            # The GEMM alone on the same quantized activations: the library's scaled GEMM
+            # against torch._scaled_mm (cuBLASLt), the call Fp8Method.apply makes.
+            xq0, sx0 = qk.fp8_quant_rows(x)
+
+            def ours_gemm(xq0=xq0, sx0=sx0):
+                for c in range(CALLS_PER_GRAPH):
+                    qk.fp8_scaled_mm(xq0, sx0, wq[c % p], ws[c % p], None, torch.bfloat16)
+
+            def scaled_mm_gemm(xq0=xq0, sx0=sx0):
+                for c in range(CALLS_PER_GRAPH):
+                    torch._scaled_mm(xq0, wt[c % p], scale_a=sx0.reshape(-1, 1), scale_b=ws[c % p].reshape(1, -1),
+                                     bias=None, out_dtype=torch.bfloat16)
+
             us = timed(ours)
+            gemm_us = timed(ours_gemm)
             try:
                 ref_us = timed(reference)
+                smm_us = timed(scaled_mm_gemm)
             except Exception as exc:  # _scaled_mm unavailable for this layout/build
-                ref_us = None
+                ref_us = smm_us = None
                 print(f"torch._scaled_mm reference failed: {exc}", file=sys.stderr)
             b = fp8_algo_bytes(n, k, m)
             out.setdefault(label, {})[str(m)] = {
@@ -368,6 +383,9 @@ def fp8_sweep(device, seed: int) -> dict:
                 "tflops": round(2 * m * n * k / (us * 1e-6) / 1e12, 1),
                 "torch_us": round(ref_us, 3) if ref_us else None,
                 "speedup_vs_torch": round(ref_us / us, 3) if ref_us else None,
+                "gemm_us": round(gemm_us, 3),
+                "scaled_mm_us": round(smm_us, 3) if smm_us else None,
+                "speedup_vs_scaled_mm": round(smm_us / gemm_us, 3) if smm_us else None,
             }
             tot_bytes += b
             tot_us += us
@@ -662,14 +680,48 @@ def fp8w_sweep(device, seed: int) -> dict:
 
 SHARD_POINTS = [(k, n, m) for k in (2048, 6144) for n in (12288, 49152) for m in (1, 8, 64)]
 SHARD_CALLS = 32
+SHARD_PARITY_POINTS = [(2048, 12288, 1), (6144, 12288, 8), (2048, 49152, 64), (6144, 49152, 1)]
+
+
+def sharded_parity(world: int, rank: int, device, seed: int, k: int, n: int, m: int) -> float:
+    """Max relative error (max over ranks, of both the NCCL all-gather form and the fused
+    peer-store form) of the gathered [M, N] output against the unsharded library GEMM on the
+    same seeded weights; -1.0 when a form failed to run."""
+    from qtts_b200.quant import kernels as qk
+    from qtts_b200.sharded import FusedAllGatherW8Linear, ShardedW8Linear, shard_rows
+
+    gen = torch.Generator(device=device)
+    gen.manual_seed(seed + 101)  # the same full weight on every rank
+    w = torch.randint(-127, 128, (n, k), dtype=torch.int8, device=device, generator=gen)
+    sc = (torch.rand(n, device=device, generator=gen) * 1e-3).to(torch.bfloat16)
+    x = torch.randn((m, k), generator=gen, device=device).to(torch.bfloat16)
+    full = qk.w8_gemm(x, w, sc).float()
+    start, stop = shard_rows(n, world, rank)
+    errs = []
+    try:
+        nccl = ShardedW8Linear(w[start:stop].contiguous(), sc[start:stop].contiguous(), n)(x).float()
+        fused = FusedAllGatherW8Linear(w[start:stop].contiguous(), sc[start:stop].contiguous(), n, max_rows=m)
+        got = fused(x).float()
+        torch.cuda.synchronize()
+        scale = full.abs().max().clamp_min(1e-30)
+        errs = [((nccl - full).abs().max() / scale).item(), ((got - full).abs().max() / scale).item()]
+        del fused
+    except Exception:
+        errs = [-1.0]
+    barrier(world)
+    err = max(errs) if errs and min(errs) >= 0 else -1.0
+    worst = max_over_ranks(world, err if err >= 0 else 1e9)
+    return -1.0 if worst >= 1e9 else worst
 
 
 def sharded_sweep(world: int, rank: int, device, seed: int) -> dict:
     """Config 5: one int8 weight-only GEMM split along N over the ranks (each rank holds
-    ceil(N / world) rows of W and scale), outputs all-gathered over NCCL. The local GEMM is
-    timed in a CUDA graph, the all-gather of its [M, ceil(N/g)] block in an eager loop (no
-    collective is captured into a graph), each as the max over ranks of CUDA-event time;
-    GEMM + all-gather is their sum."""
+    ceil(N / world) rows of W and scale), outputs all-gathered over NCCL. The local GEMM and
+    the GEMM followed by NCCL's all-gather are each timed in a CUDA graph (and the all-gather
+    alone in an eager loop, host launch cost included, for reference), as the max over ranks
+    of CUDA-event time; the fused form is one kernel per rank per call. Each point also times
+    the unsharded GEMM on one GPU, so ``sharded_efficiency`` = t(1 GPU) / (g x best sharded
+    time), and every point's gathered output is checked against the unsharded GEMM."""
     from qtts_b200 import _native as nat
     from qtts_b200.sharded import FusedAllGatherW8Linear, ShardedW8Linear, shard_rows
 
@@ -735,8 +787,30 @@ def sharded_sweep(world: int, rank: int, device, seed: int) -> dict:
             for c in range(SHARD_CALLS):
                 fused[c % copies](x)
 
+        def gemm_gather():
+            for c in range(SHARD_CALLS):
+                lins[0].gather(lins[c % copies].local(x, block), gathered)
+
         gemm_us = time_graph(gemm_only)
         gather_us = time_eager(gather_only) if world > 1 else 0.0  # one GPU: the block is the output
+        # GEMM + NCCL all-gather captured together (every rank captures the same collectives).
+        gemm_gather_graph_us = time_graph(gemm_gather) if world > 1 else gemm_us
+        # The unsharded GEMM on this GPU alone: the strong-scaling baseline.
+        wfull = torch.randint(-127, 128, (n, k), dtype=torch.int8, device=device, generator=gen)
+        sfull = (torch.rand(n, device=device, generator=gen) * 1e-3).to(torch.bfloat16)
+        ofull = torch.empty((m, n), dtype=torch.bfloat16, device=device)
+        fcopies = max(1, min(8, -(-POOL_MIN_BYTES // (n * k))))
+        wl_full = [wfull] + [torch.randint(-127, 128, (n, k), dtype=torch.int8, device=device, generator=gen)
+                             for _ in range(fcopies - 1)]
+
+        def full_gemm():
+            from qtts_b200.quant import kernels as qk
+
+            for c in range(SHARD_CALLS):
+                qk.w8_gemm(x, wl_full[c % fcopies], sfull, None, out=ofull)
+
+        single_us = time_graph(full_gemm)
+        del wl_full, wfull, sfull, ofull
         if fused_ok:
             # One checked call first: a failed exchange (bounded waits, recorded in the
             # device status) must not turn every timed call into a wait-limit expiry.
@@ -748,10 +822,14 @@ def sharded_sweep(world: int, rank: int, device, seed: int) -> dict:
                 fused_error = f"device status after the first fused call at K={k} N={n} M={m}"
         fused_us = time_graph(fused_calls) if fused_ok else None
         total_us = gemm_us + gather_us
+        best_us = min(v for v in (gemm_gather_graph_us, fused_us) if v)
         res[f"K{k}_N{n}_M{m}"] = {
             "gemm_us": round(gemm_us, 3),
             "allgather_us": round(gather_us, 3),
             "gemm_allgather_us": round(total_us, 3),
+            "gemm_allgather_graph_us": round(gemm_gather_graph_us, 3),
+            "single_gpu_unsharded_us": round(single_us, 3),
+            "sharded_efficiency": round(single_us / (world * best_us), 4),
             "fused_gemm_allgather_us": round(fused_us, 3) if fused_us else None,
             "fused_speedup": round(total_us / fused_us, 3) if fused_us else None,
             "agg_weight_gbs": round(n * k / (total_us * 1e-6) / 1e9, 1),
@@ -761,14 +839,24 @@ def sharded_sweep(world: int, rank: int, device, seed: int) -> dict:
         }
         del ws, ss, lins, fused, x, block, gathered
         torch.cuda.empty_cache()
+    # Parity of the gathered output at every rank against the unsharded GEMM.
+    parity = {}
+    for k, n, m in SHARD_PARITY_POINTS:
+        parity[f"K{k}_N{n}_M{m}"] = round(sharded_parity(world, rank, device, seed, k, n, m), 6)
+        torch.cuda.empty_cache()
+    parity_ok = all(0 <= v <= 1e-2 for v in parity.values())
     return {
         "workload": "config 5: int8 W8A16 GEMM sharded along N over the ranks (ceil(N/g) rows each), bf16 "
         "outputs all-gathered over NCCL (gemm_allgather_us) or by the GEMM kernel itself over peer memory "
         "(fused_gemm_allgather_us); K in {2048,6144}, N in {12288,49152}, M in {1,8,64}",
         "scaling": "strong",
         "n_gpus": world,
-        "allgather_timed": "eager loop, CUDA events" if world > 1 else "single GPU: no exchange",
+        "allgather_timed": "allgather_us: eager loop, CUDA events; gemm_allgather_graph_us: GEMM + NCCL all-gather "
+        "captured in one CUDA graph" if world > 1 else "single GPU: no exchange",
         "fused_error": fused_error,
+        "sharded_parity_ok": parity_ok,
+        "sharded_max_rel_err": parity,
+        "sharded_efficiency": {key: v["sharded_efficiency"] for key, v in res.items() if key.startswith("K6144_N49152")},
         "per_point": res,
     }
 

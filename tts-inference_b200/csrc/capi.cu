@@ -1036,6 +1036,10 @@ int qtts_fp8_gemm(const uint8_t* xq, int64_t ldxq, const float* scale_x, const u
     fa.k_per_cta = plan.k_per_cta;
     fa.stages = plan.stages;
     fa.wait_ns = current_wait_limit_ns();
+    fa.trace_slot = -1;
+#ifdef QTTS_TRACE
+    fa.trace_slot = qtts_trace_next_slot();
+#endif
     return launch_fp8_gemm(plan, wmap, xmap, fa, out_dtype, pdl, s);
   }
   if (variant != QTTS_VARIANT_AUTO && variant != QTTS_VARIANT_GENERIC) return QTTS_ERR_VARIANT;
@@ -1128,6 +1132,10 @@ int qtts_i8_gemm(const int8_t* xq, int64_t ldxq, const float* scale_x, const int
     fa.k_per_cta = plan.k_per_cta;
     fa.stages = plan.stages;
     fa.wait_ns = current_wait_limit_ns();
+    fa.trace_slot = -1;
+#ifdef QTTS_TRACE
+    fa.trace_slot = qtts_trace_next_slot();
+#endif
     return launch_fp8_gemm(plan, wmap, xmap, fa, out_dtype, pdl, s, /*int8=*/true);
   }
   if (variant != QTTS_VARIANT_AUTO && variant != QTTS_VARIANT_GENERIC) return QTTS_ERR_VARIANT;

@@ -88,6 +88,9 @@ __global__ void __launch_bounds__(kF8Threads, 1)
   uint64_t* recv_bar = dfull + 1;
   uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(recv_bar + 1);
   int* err_flag = reinterpret_cast<int*>(tmem_slot + 1);
+  // The tile's activation row scales, staged once by the epilogue warps and
+  // read into registers a group at a time ahead of the group's output stores.
+  float* sx_s = reinterpret_cast<float*>((reinterpret_cast<uintptr_t>(err_flag + 2) + 15) & ~uintptr_t(15));
 
   const int tid = threadIdx.x;
   const int warp = tid >> 5;
@@ -103,6 +106,7 @@ __global__ void __launch_bounds__(kF8Threads, 1)
   const int mrows = min(NB, a.M - m0);
 
   if (tid == 0) {
+    QTTS_TRACE_STAMP(0);
     for (int s = 0; s < S; ++s) {
       mbar_init(&wfull[s], 1);
       mbar_init(&xfull[s], 1);
@@ -111,7 +115,7 @@ __global__ void __launch_bounds__(kF8Threads, 1)
     mbar_init(dfull, 1);
     mbar_init(recv_bar, 1);
     if (split > 1) mbar_arrive_expect_tx(recv_bar, static_cast<uint32_t>((split - 1) * rpo * NB * 4));
-    *err_flag = 0;
+    err_flag[0] = 0;
     fence_mbarrier_init();
   }
   if (warp == kF8MmaWarp) {
@@ -138,6 +142,7 @@ __global__ void __launch_bounds__(kF8Threads, 1)
       }
       w_issued = pre;
       pdl_wait();
+      QTTS_TRACE_STAMP(1);
       for (int it = 0; it < n_iters; ++it) {
         const int s = it % S;
         if (it >= S) {
@@ -146,6 +151,7 @@ __global__ void __launch_bounds__(kF8Threads, 1)
             *verr = 1;
             break;
           }
+          QTTS_TRACE_DETAIL(2, it);
           mbar_arrive_expect_tx(&wfull[s], kF8StageW);
           tma_load_2d(wbuf + s * kF8StageW, &wmap, k0 + it * 128, n0, &wfull[s]);
           w_issued = it + 1;
@@ -164,10 +170,16 @@ __global__ void __launch_bounds__(kF8Threads, 1)
       for (int it = 0; ok && it < n_iters; ++it) {
         const int s = it % S;
         const uint32_t ph = (it / S) & 1;
-        if (!mbar_wait_bounded(&wfull[s], ph, a.wait_ns) || !mbar_wait_bounded(&xfull[s], ph, a.wait_ns)) {
+        if (!mbar_wait_bounded(&wfull[s], ph, a.wait_ns)) {
           ok = false;
           break;
         }
+        QTTS_TRACE_DETAIL(3, it);
+        if (!mbar_wait_bounded(&xfull[s], ph, a.wait_ns)) {
+          ok = false;
+          break;
+        }
+        QTTS_TRACE_DETAIL(0, it);
         tc_fence_after();
 #pragma unroll
         for (int i = 0; i < 4; ++i) {
@@ -180,20 +192,26 @@ __global__ void __launch_bounds__(kF8Threads, 1)
           }
         }
         tc_commit(&sempty[s]);
+        QTTS_TRACE_DETAIL(1, it);
       }
       if (!ok) {
         record_status(QTTS_ERR_TIMEOUT);
         *verr = 1;
       }
+      QTTS_TRACE_STAMP(2);
       tc_commit(dfull);
     }
     __syncwarp();
   } else {
     // ---------------- epilogue warps 0..3: one accumulator row per thread ----------------
     pdl_wait();
+    if (tid == 0) QTTS_TRACE_STAMP(5);
     const int row = warp * 32 + lane;
     const uint32_t lane_base = static_cast<uint32_t>(warp * 32) << 16;
+    for (int c = tid; c < NB; c += kF8EpiWarps * 32) sx_s[c] = (m0 + c < a.M) ? a.scale_x[m0 + c] : 0.f;
+    named_bar_sync(1, kF8EpiWarps * 32);
     const bool dready = mbar_wait_bounded(dfull, 0, a.wait_ns);
+    if (tid == 0) QTTS_TRACE_STAMP(6);
     if (!dready) {
       if (lane == 0) record_status(QTTS_ERR_TIMEOUT);
       *verr = 1;
@@ -207,15 +225,37 @@ __global__ void __launch_bounds__(kF8Threads, 1)
       if (a.bias != nullptr) bias = to_float(static_cast<const OT*>(a.bias)[n]);
     }
     OT* og = static_cast<OT*>(a.out) + static_cast<int64_t>(m0) * a.ldo;
+    // Accumulator columns 16 at a time (one TMEM load and wait per group).
+    constexpr int kGrp = 16;
+#pragma unroll 1
+    for (int g0 = 0; g0 < NB; g0 += kGrp) {
+    uint32_t dg[kGrp];
+    f8_tmem_ld<16>(tmem + lane_base + g0, dg);
+    tc_wait_ld();
+    if (tid == 0) QTTS_TRACE_DETAIL(4, g0 / kGrp);
+    // The loaded registers are only valid after the wait: tie them to it so no
+    // use is scheduled above it.
 #pragma unroll
-    for (int c0 = 0; c0 < NB; c0 += 16) {
-      uint32_t d[16];
-      f8_tmem_ld<16>(tmem + lane_base + c0, d);
-      tc_wait_ld();
+    for (int q = 0; q < kGrp; ++q) asm volatile("" : "+r"(dg[q]));
+    {
+      const int c0 = g0;
+      // The group's activation scales into registers before any output store:
+      // read between stores, each load waited for the previous store (the
+      // compiler cannot tell the output from the scales apart), a serial
+      // chain of load latencies.
+      float sxv[16];
+#pragma unroll
+      for (int q = 0; q < 4; ++q) {
+        const uint4 t = lds128(smem_u32(sx_s + c0 + 4 * q));
+        sxv[4 * q] = __uint_as_float(t.x);
+        sxv[4 * q + 1] = __uint_as_float(t.y);
+        sxv[4 * q + 2] = __uint_as_float(t.z);
+        sxv[4 * q + 3] = __uint_as_float(t.w);
+      }
       // Raw accumulator words (fp32 bits, or int32 for I8; zero either way).
       uint32_t v[16];
 #pragma unroll
-      for (int c = 0; c < 16; ++c) v[c] = (n_iters > 0 && !cta_err) ? d[c] : 0u;
+      for (int c = 0; c < 16; ++c) v[c] = (n_iters > 0 && !cta_err) ? dg[c0 - g0 + c] : 0u;
       if (split == 1) {
         if (!cta_err && n < a.N) {
 #pragma unroll
@@ -223,7 +263,7 @@ __global__ void __launch_bounds__(kF8Threads, 1)
             const int col = c0 + c;
             if (col < mrows) {
               og[static_cast<int64_t>(col) * a.ldo + n] =
-                  from_float<OT>(w8a8_out<I8, OT>(v[c], a.scale_x[m0 + col], sw, bias, a.bias != nullptr));
+                  from_float<OT>(w8a8_out<I8, OT>(v[c], sxv[c], sw, bias, a.bias != nullptr));
             }
           }
         }
@@ -247,6 +287,8 @@ __global__ void __launch_bounds__(kF8Threads, 1)
           }
         }
       }
+    }
+    if (tid == 0) QTTS_TRACE_DETAIL(5, g0 / kGrp);
     }
     if (split > 1) {
       named_bar_sync(1, kF8EpiWarps * 32);
@@ -277,12 +319,15 @@ __global__ void __launch_bounds__(kF8Threads, 1)
             }
             const float sw = a.scale_w[nn];
             const float bias = a.bias != nullptr ? to_float(static_cast<const OT*>(a.bias)[nn]) : 0.f;
+            float sxq[4];
+#pragma unroll
+            for (int q = 0; q < 4; ++q) sxq[q] = sx_s[min(4 * mq + q, NB - 1)];
 #pragma unroll
             for (int q = 0; q < 4; ++q) {
               const int m = 4 * mq + q;
               if (m < mrows)
                 og[static_cast<int64_t>(m) * a.ldo + nn] =
-                    from_float<OT>(w8a8_out<I8, OT>(rv[q], a.scale_x[m0 + m], sw, bias, a.bias != nullptr));
+                    from_float<OT>(w8a8_out<I8, OT>(rv[q], sxq[q], sw, bias, a.bias != nullptr));
             }
           }
         }
@@ -292,6 +337,7 @@ __global__ void __launch_bounds__(kF8Threads, 1)
 
   tc_fence_before();
   __syncthreads();
+  if (tid == 0) QTTS_TRACE_STAMP(7);
   if (warp == kF8MmaWarp) {
     tc_fence_after();
     tmem_dealloc(tmem, kCols);
@@ -378,7 +424,8 @@ int launch_w8a8_out(const CUtensorMap& wmap, const CUtensorMap& xmap, const Fp8A
 
 size_t fp8_smem(int nb, int stages, int split) {
   return 1024 + static_cast<size_t>(stages) * (kF8StageW + static_cast<size_t>(nb) * 128) +
-         (split > 1 ? static_cast<size_t>(128) * nb * 4 : 0) + 16 + 24 * stages + 16 + 32;
+         (split > 1 ? static_cast<size_t>(128) * nb * 4 : 0) + 16 + 24 * stages + 16 + 32 + 16 +
+         static_cast<size_t>(nb) * 4;
 }
 
 }  // namespace

@@ -95,6 +95,7 @@ struct Fp8Args {
   int k_per_cta;
   int stages;
   uint64_t wait_ns;
+  int trace_slot;  // timeline probe slot (-1: off); only read in -DQTTS_TRACE builds
 };
 
 struct Fp8Plan {

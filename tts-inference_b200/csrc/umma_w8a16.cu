@@ -154,7 +154,7 @@ __global__ void __launch_bounds__(kUmThreads, 1)
     mbar_init(dfull, 1);
     mbar_init(recv_bar, 1);
     if (split > 1) mbar_arrive_expect_tx(recv_bar, static_cast<uint32_t>((split - 1) * rpo * NB * 4));
-    *err_flag = 0;
+    err_flag[0] = 0;
     fence_mbarrier_init();
   }
   if (warp == kUmMmaWarp) {
@@ -353,6 +353,9 @@ __global__ void __launch_bounds__(kUmThreads, 1)
       tmem_ld<32>(tmem + lane_base + kDCol + HALF * half + 32, d1);
     }
     tc_wait_ld();
+    // The loaded registers are only valid after the wait: tie them to it.
+#pragma unroll
+    for (int c = 0; c < HALF; ++c) asm volatile("" : "+r"(d[c]));
     const bool cta_err = *verr != 0;
     float v[HALF];
 #pragma unroll
