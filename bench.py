@@ -909,6 +909,17 @@ def talker_frames(seed: int, batch: int = 8) -> dict:
     torch.cuda.empty_cache()
     fps_int8, ms_int8 = timed_frames_per_s(frame)
     codes = frame.codes.clone()
+    # The same int8 frame with the code predictor's heads, argmax and next-embedding lookup
+    # as separate ops instead of the library's fused head.
+    from qtts_b200.decode_step import CodePredictor as _CP
+
+    _CP.fuse_heads = False
+    frame.graph = None
+    try:
+        fps_sep_heads, ms_sep_heads = timed_frames_per_s(frame)
+    finally:
+        _CP.fuse_heads = True
+        frame.graph = None
     # The same int8 frame with the norms and SiLU·up as separate torch ops.
     Block.fuse_prologues = False
     frame.graph = None
@@ -947,6 +958,8 @@ def talker_frames(seed: int, batch: int = 8) -> dict:
         "median of 5 windows of 20 replays",
         "frames_per_s_int8": round(fps_int8, 1),
         "frames_per_s_bf16": round(fps_bf16, 1),
+        "frames_per_s_int8_separate_heads": round(fps_sep_heads, 1),
+        "ms_per_step_int8_separate_heads": round(ms_sep_heads, 3),
         "frames_per_s_int8_torch_prologues": round(fps_unfused, 1),
         "ms_per_step_int8_torch_prologues": round(ms_unfused, 3),
         "speedup_vs_bf16": round(fps_int8 / fps_bf16, 3),

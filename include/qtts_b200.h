@@ -317,6 +317,32 @@ QTTS_API int qtts_fp8_gemm(const uint8_t* xq, int64_t ldxq, const float* scale_x
                   const void* bias, void* out, int64_t ldo, int out_dtype,
                   int M, int N, int K, int variant, unsigned flags, void* stream);
 
+/* ---- fused codebook head -------------------------------------------------------
+ * The end of one greedy decode step in one launch: the code predictor's
+ *   logits = lm_head[step](norm(hidden)); code = logits.argmax(-1);
+ *   next = codec_embedding[step](code)
+ * (qtts/models/code_predictor.py:229-242) and the talker's masked codec head
+ * (qtts/models/talker.py:354-356):
+ *   y[m]     = norm_weight ? RMSNorm(x[m]) (the library's element, as
+ *              qtts_rms_norm) : x[m]
+ *   l[m, n]  = float(cast_x( (sum_k y[m,k] * w[n,k]) * scale[n] )) + logit_bias[n]
+ *   codes[m] = the first n with the largest l[m, n] (torch.argmax)
+ *   embed_out[m, 0:E] = embed[codes[m], 0:E]   (when embed is not NULL)
+ * x: [M, K] BF16/FP16 (ld ldx, 16-byte aligned rows); norm_weight: [K] of x's
+ * dtype or NULL; w: [N, K] int8 (ld ldw, 4-byte aligned rows); scale: [N] of
+ * scale_dtype; logit_bias: [N] fp32 or NULL (0 keeps a logit, -inf masks it);
+ * codes: [M] int64; embed: [vocab, E] of x's dtype or NULL, embed_out [M, E].
+ * state: M + 1 zeroed uint64 words of device memory the caller owns (the
+ * per-row best candidates and a CTA counter); the call leaves them zero, so
+ * one state array serves every call ordered on a stream (calls that may run
+ * at the same time need separate arrays). M <= 16, K % 128 == 0, K <= 2048,
+ * E % 8 == 0. Replaces lm_head[step] + argmax + the embedding lookup. */
+QTTS_API int qtts_w8a16_head_argmax(const void* x, int64_t ldx, int x_dtype, const void* norm_weight, float eps,
+                                    const int8_t* w, int64_t ldw, const void* scale, int scale_dtype,
+                                    const float* logit_bias, int64_t* codes, const void* embed, int64_t lde,
+                                    int vocab, void* embed_out, int64_t ldeo, int E, uint64_t* state, int M, int N,
+                                    int K, unsigned flags, void* stream);
+
 /* ---- int8 W8A8 (Int8Method) --------------------------------------------------
  * Per-token int8 quantization of the activations of Int8Method.apply
  * (qtts/quant/int8.py:138-140), each step in the activation dtype as torch

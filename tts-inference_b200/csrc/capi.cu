@@ -790,6 +790,54 @@ int qtts_silu_mul(const void* gate_up, int64_t ld_in, void* out, int64_t ldo, in
   return launch_prologue(pa, dtype, (flags & QTTS_FLAG_PDL) != 0, static_cast<cudaStream_t>(stream));
 }
 
+int qtts_w8a16_head_argmax(const void* x, int64_t ldx, int x_dtype, const void* norm_weight, float eps,
+                           const int8_t* w, int64_t ldw, const void* scale, int scale_dtype, const float* logit_bias,
+                           int64_t* codes, const void* embed, int64_t lde, int vocab, void* embed_out, int64_t ldeo,
+                           int E, uint64_t* state, int M, int N, int K, unsigned flags, void* stream) {
+  if (M < 0 || N < 0 || K < 0 || E < 0 || vocab < 0) return QTTS_ERR_SHAPE;
+  if (M == 0) return QTTS_OK;
+  if (x == nullptr || w == nullptr || scale == nullptr || codes == nullptr || state == nullptr) return QTTS_ERR_NULL;
+  if (embed != nullptr && embed_out == nullptr) return QTTS_ERR_NULL;
+  if (x_dtype != QTTS_BF16 && x_dtype != QTTS_FP16) return QTTS_ERR_DTYPE;
+  if (!is_float_dtype(scale_dtype)) return QTTS_ERR_DTYPE;
+  if (M > 16 || N < 1 || K < 128 || K > 2048 || K % 128 != 0) return QTTS_ERR_SHAPE;
+  if (ldx < K || ldw < K) return QTTS_ERR_SHAPE;
+  if (embed != nullptr && (E < 8 || E % 8 != 0 || lde < E || ldeo < E || vocab < 1)) return QTTS_ERR_SHAPE;
+  if (!aligned16(x) || (ldx * 2) % 16 != 0 || (norm_weight != nullptr && !aligned16(norm_weight))) {
+    return QTTS_ERR_ALIGN;
+  }
+  if ((reinterpret_cast<uintptr_t>(w) & 3u) != 0 || ldw % 4 != 0) return QTTS_ERR_ALIGN;
+  if ((reinterpret_cast<uintptr_t>(state) & 7u) != 0) return QTTS_ERR_ALIGN;
+  if (embed != nullptr && (!aligned16(embed) || !aligned16(embed_out) || (lde * 2) % 16 != 0 || (ldeo * 2) % 16 != 0)) {
+    return QTTS_ERR_ALIGN;
+  }
+  if (head_argmax_smem(M, K) + 1024 > kMaxDynSmem) return QTTS_ERR_SHAPE;
+  const int dev_ok = check_device();
+  if (dev_ok != QTTS_OK) return dev_ok;
+  HeadArgs ha{};
+  ha.x = x;
+  ha.ldx = ldx;
+  ha.norm_weight = norm_weight;
+  ha.eps = eps;
+  ha.w = w;
+  ha.ldw = ldw;
+  ha.scale = scale;
+  ha.scale_dtype = scale_dtype;
+  ha.logit_bias = logit_bias;
+  ha.codes = codes;
+  ha.embed = embed;
+  ha.lde = lde;
+  ha.embed_out = embed_out;
+  ha.ldeo = ldeo;
+  ha.E = E;
+  ha.vocab = vocab;
+  ha.state = reinterpret_cast<unsigned long long*>(state);
+  ha.M = M;
+  ha.N = N;
+  ha.K = K;
+  return launch_head_argmax(ha, x_dtype, (flags & QTTS_FLAG_PDL) != 0, static_cast<cudaStream_t>(stream));
+}
+
 // Which kernel family the call lands on (the same choice w8a16_dispatch makes).
 static int chosen_family(const void* x, int64_t ldx, int x_dtype, const int8_t* w, int64_t ldw, int M, int N, int K,
                          int variant) {

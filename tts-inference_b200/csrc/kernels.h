@@ -107,6 +107,30 @@ struct Fp8Plan {
   dim3 grid;
 };
 
+// ---- fused codebook head (csrc/head_argmax.cu) --------------------------------
+struct HeadArgs {
+  const void* x;  // [M, K] activations (pre-norm), 16-bit
+  int64_t ldx;
+  const void* norm_weight;  // [K] of the activation type, or nullptr (no norm)
+  float eps;
+  const int8_t* w;  // [N, K] int8
+  int64_t ldw;
+  const void* scale;  // [N]
+  int scale_dtype;
+  const float* logit_bias;  // [N] fp32 added to the rounded logits, or nullptr
+  int64_t* codes;           // [M]
+  const void* embed;        // [vocab, E] of the activation type, or nullptr
+  int64_t lde;
+  void* embed_out;  // [M, E]
+  int64_t ldeo;
+  int E;
+  int vocab;
+  unsigned long long* state;  // [M + 1], zero before the first call; left zero
+  int M, N, K;
+};
+size_t head_argmax_smem(int M, int K);
+int launch_head_argmax(const HeadArgs& a, int x_dtype, bool pdl, cudaStream_t stream);
+
 Fp8Plan plan_fp8(int M, int N, int K, int split_req);
 // int8 = true: the int8 W8A8 form (signed int8 operands, int32 accumulator).
 int launch_fp8_gemm(const Fp8Plan& p, const CUtensorMap& wmap, const CUtensorMap& xmap, const Fp8Args& args,

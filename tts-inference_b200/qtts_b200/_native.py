@@ -101,6 +101,9 @@ SIGNATURES: dict[str, tuple[object, list[object]]] = {
     "qtts_rms_norm": (_c_int, [_c_vp, _c_i64, _c_vp, _c_vp, _c_i64, _c_int, _c_int, _c_int, ctypes.c_float,
                                _c_uint, _c_vp]),
     "qtts_silu_mul": (_c_int, [_c_vp, _c_i64, _c_vp, _c_i64, _c_int, _c_int, _c_int, _c_uint, _c_vp]),
+    "qtts_w8a16_head_argmax": (_c_int, [_c_vp, _c_i64, _c_int, _c_vp, ctypes.c_float, _c_vp, _c_i64, _c_vp, _c_int,
+                                        _c_vp, _c_vp, _c_vp, _c_i64, _c_int, _c_vp, _c_i64, _c_int, _c_vp, _c_int,
+                                        _c_int, _c_int, _c_uint, _c_vp]),
     "qtts_w8a16_gemm_prologue": (
         _c_int,
         [_c_vp, _c_i64, _c_int, _c_int, _c_vp, ctypes.c_float, _c_vp, _c_i64, _c_vp, _c_int, _c_vp, _c_vp, _c_i64,

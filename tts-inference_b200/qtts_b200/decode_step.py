@@ -158,7 +158,20 @@ class Talker(nn.Module):
         return h, logits.argmax(dim=-1)
 
 
+def _fused_head_ok(head: LinearBase, k: int) -> bool:
+    """Whether a codebook head runs as the library's fused head (norm, int8 head, argmax and
+    the next step's embedding in one launch): an int8 weight-only head of a width it takes."""
+    from .quant.int8 import Int8WeightOnlyMethod
+
+    return isinstance(head.quant_method, Int8WeightOnlyMethod) and k % 128 == 0 and k <= 2048
+
+
 class CodePredictor(nn.Module):
+    #: End each codebook step with the library's fused head (qtts_w8a16_head_argmax: the
+    #: final norm, the int8 head, the greedy argmax and the next step's embedding row in one
+    #: launch) when the head is int8; False keeps head, argmax and lookup as separate ops.
+    fuse_heads = True
+
     def __init__(self, dtype=torch.bfloat16, device="cuda", layers: int = PREDICTOR.layers,
                  codebooks: int = CODEBOOKS - 1, seed: int = 0) -> None:
         super().__init__()
@@ -188,6 +201,17 @@ class CodePredictor(nn.Module):
             t = x.shape[1]
             for layer in self.layers:
                 x = layer.prefix(x, self.cos[:t], self.sin[:t])
+            head = self.lm_head[s]
+            if self.fuse_heads and _fused_head_ok(head, x.shape[-1]):
+                from .quant import kernels as qk
+
+                nxt = self.embed[s + 1] if s + 1 < self.codebooks else None
+                code, emb = qk.w8_head_argmax(x[:, -1], head.int8_weight, head.int8_scale, norm_weight=self.norm,
+                                              embed=nxt)
+                codes.append(code)
+                if emb is not None:
+                    seq.append(emb)
+                continue
             if Block.fuse_prologues:
                 code = self.lm_head[s].forward_rmsnorm(x[:, -1], self.norm).float().argmax(dim=-1)
             else:

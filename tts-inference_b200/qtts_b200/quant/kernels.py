@@ -189,6 +189,78 @@ def silu_mul(gate_up: torch.Tensor, *, out: torch.Tensor | None = None) -> torch
     return out.reshape(*gate_up.shape[:-1], width)
 
 
+_HEAD_STATE: dict[int, torch.Tensor] = {}
+
+
+def _head_state(device: torch.device) -> torch.Tensor:
+    """The zeroed uint64 state words of ``qtts_w8a16_head_argmax`` on ``device`` (17: up to 16
+    rows + a CTA counter). Every call leaves them zero, so calls ordered on one stream share
+    them; allocated on the first call (make one before capturing a CUDA graph)."""
+    idx = device.index if device.index is not None else torch.cuda.current_device()
+    st = _HEAD_STATE.get(idx)
+    if st is None:
+        st = torch.zeros(17, dtype=torch.int64, device=device)
+        _HEAD_STATE[idx] = st
+    return st
+
+
+def w8_head_argmax(
+    x: torch.Tensor,
+    weight: torch.Tensor,
+    scale: torch.Tensor,
+    *,
+    norm_weight: torch.Tensor | None = None,
+    eps: float = 1e-6,
+    logit_bias: torch.Tensor | None = None,
+    embed: torch.Tensor | None = None,
+    codes: torch.Tensor | None = None,
+    embed_out: torch.Tensor | None = None,
+) -> tuple[torch.Tensor, torch.Tensor | None]:
+    """The end of a greedy decode step in one launch (``qtts_w8a16_head_argmax``):
+    ``codes = (rms_norm(x) @ (weight * scale).T (+ logit_bias)).argmax(-1)`` with the logits
+    rounded to x's dtype as the head's output is, and ``embed[codes]`` gathered when ``embed``
+    is given (the next step's input row). x ``[M, K]`` (M <= 16, K % 128 == 0, K <= 2048),
+    weight ``[N, K]`` int8, scale ``[N]``, logit_bias ``[N]`` fp32 (0 / -inf mask), embed
+    ``[vocab, E]`` in x's dtype. Returns ``(codes [M] int64, embed rows [M, E] or None)``."""
+    ok, reason = nat.available()
+    if not ok:
+        raise RuntimeError(reason)
+    if x.dim() != 2 or weight.dim() != 2 or weight.shape[1] != x.shape[1]:
+        raise ValueError(f"x {tuple(x.shape)} and weight {tuple(weight.shape)} do not agree")
+    m, k = x.shape
+    n = weight.shape[0]
+    device = _require_cuda(x, weight, scale, norm_weight, logit_bias, embed)
+    if x.stride(1) != 1:
+        x = x.contiguous()
+    if weight.stride(1) != 1:
+        weight = weight.contiguous()
+    scale = scale.reshape(-1).contiguous()
+    if norm_weight is not None:
+        norm_weight = norm_weight.reshape(-1).to(x.dtype).contiguous()
+    if logit_bias is not None:
+        logit_bias = logit_bias.reshape(-1).to(torch.float32).contiguous()
+    if codes is None:
+        codes = torch.empty(m, dtype=torch.int64, device=device)
+    e = vocab = 0
+    if embed is not None:
+        if embed.dim() != 2 or embed.dtype != x.dtype or embed.stride(1) != 1:
+            raise ValueError("embed must be a [vocab, E] table of x's dtype with unit column stride")
+        vocab, e = embed.shape
+        if embed_out is None:
+            embed_out = torch.empty((m, e), dtype=x.dtype, device=device)
+    state = _head_state(device)
+    code = nat.lib().qtts_w8a16_head_argmax(
+        x.data_ptr(), x.stride(0) if m > 1 else k, nat.dtype_code(x.dtype),
+        norm_weight.data_ptr() if norm_weight is not None else None, float(eps),
+        weight.data_ptr(), weight.stride(0) if n > 1 else k, scale.data_ptr(), nat.dtype_code(scale.dtype),
+        logit_bias.data_ptr() if logit_bias is not None else None, codes.data_ptr(),
+        embed.data_ptr() if embed is not None else None, embed.stride(0) if embed is not None else 0, vocab,
+        embed_out.data_ptr() if embed is not None else None, embed_out.stride(0) if embed is not None else 0, e,
+        state.data_ptr(), m, n, k, _flags(), nat.stream_ptr(device))
+    nat.check(code, "qtts_w8a16_head_argmax")
+    return codes, (embed_out if embed is not None else None)
+
+
 def prologue_fused(m: int, n: int, k: int, prologue: int, variant: int = nat.VARIANT_AUTO) -> bool:
     """Whether ``w8_gemm_rmsnorm`` / ``w8_gemm_silu_mul`` of this shape runs as one launch."""
     return bool(nat.lib().qtts_w8a16_gemm_prologue_fused(m, n, k, prologue, variant))
