@@ -22,11 +22,16 @@
 //     lanes x 32 columns = 64 k each). They run ahead of the previous
 //     kernel's completion; only the epilogue waits for it. One MMA per 16 k
 //     for either type: at decode N the tensor core is bound by instruction
-//     count (~150 cycles per 128-row MMA whatever N is), not by FLOPs;
-//   * warp 9 (MMA) issues tcgen05.mma kind::f16, A from tensor memory, B from
-//     shared memory, fp32 accumulator [128 x NB] in tensor memory;
-//     tcgen05.commit releases A slots and activation tiles as they are used.
-// The epilogue reads the accumulator with tcgen05.ld. K can be split over a
+//     issue, not by FLOPs (a 128-row MMA takes ~45 cycles back to back for
+//     N <= 64, but a single issuing thread that also waits and commits gets
+//     one out every ~60-150 cycles);
+//   * warps 9 and 10 (MMA) issue tcgen05.mma kind::f16, A from tensor memory,
+//     B from shared memory: warp 9 the first 64-k half of every 128-k stage,
+//     warp 10 the second, each into its own fp32 accumulator [128 x NB] in
+//     tensor memory (two issuing threads keep the tensor core at ~32 cycles
+//     per MMA, measured); tcgen05.commit releases A slots and activation tiles
+//     as they are used.
+// The epilogue reads both accumulators with tcgen05.ld and adds them. K can be split over a
 // cluster of CTAs whose partial sums reach the row owner through st.async, as
 // in the skinny kernel. All waits are bounded; tensor memory is always
 // released.
@@ -41,9 +46,18 @@ namespace qtts {
 constexpr int kUmStageBytes = 16384;  // 128 rows x 128 k
 constexpr int kUmDqWarps = 8;
 constexpr int kUmProducerWarp = 8;
-constexpr int kUmMmaWarp = 9;
-constexpr int kUmThreads = (kUmDqWarps + 2) * 32;
-constexpr uint32_t kUmTmemCols = 256;  // A ring + D: 192 + up to 64 columns, or 128 + 128 (NB = 128)
+constexpr int kUmMmaWarp = 9;    // first MMA issuer (also allocates tensor memory)
+constexpr int kUmMmaWarp2 = 10;  // second MMA issuer
+constexpr int kUmThreads = (kUmDqWarps + 3) * 32;
+// Tensor-memory columns: the A ring (192, or 128 at NB = 128) and two
+// accumulators of NB columns, rounded up to a power of two.
+__host__ __device__ constexpr uint32_t umma_tmem_cols(int nb) {
+  return ((nb > 64 ? 128 : 192) + 2 * nb) <= 256 ? 256u : 512u;
+}
+// A grid that takes all 512 columns also takes more than half of an SM's
+// shared memory, so that no two of its CTAs share an SM (the second would wait
+// in tcgen05.alloc for the first, which may wait on a cluster peer).
+constexpr size_t kUmFullTmemMinSmem = 116 * 1024;
 
 __device__ __forceinline__ void tmem_st_x32(uint32_t taddr, const uint32_t (&r)[32]) {
   asm volatile(
@@ -95,12 +109,13 @@ __global__ void __launch_bounds__(kUmThreads, 1)
   constexpr int HALF = NB / 2;      // accumulator columns per dequant warpgroup
   constexpr int XS = NB * 256;      // activation tile bytes per 128-k stage
   constexpr int kSlotCols = 32;     // tensor-memory columns per 64-k A slot
-  // NB = 128 (M = 65..128 in one tile: an MMA costs the same for any N) keeps
-  // four A slots so that the accumulator's 128 columns fit the 256 allocated.
+  // NB = 128 (M = 65..128 in one tile) keeps four A slots so that the two
+  // accumulators' 2 x 128 columns fit beside them.
   constexpr int kACols = NB > 64 ? 128 : 192;
   constexpr int kNA = kACols / kSlotCols;  // A slots
   constexpr uint32_t kDCol = kACols;
   constexpr uint32_t kIdesc = umma_idesc(kFmt, kFmt, 128, NB);
+  constexpr uint32_t kTmemCols = umma_tmem_cols(NB);
   extern __shared__ uint8_t smem_raw[];
   uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
   const int split = gridDim.y;
@@ -145,20 +160,20 @@ __global__ void __launch_bounds__(kUmThreads, 1)
     }
     for (int s = 0; s < XD; ++s) {
       mbar_init(&xfull[s], 1);
-      mbar_init(&xempty[s], 1);
+      mbar_init(&xempty[s], 2);  // one commit from each MMA issuer
     }
     for (int b = 0; b < kNA; ++b) {
       mbar_init(&afull[b], kUmDqWarps / 2);
       mbar_init(&aempty[b], 1);
     }
-    mbar_init(dfull, 1);
+    mbar_init(dfull, 2);  // one commit from each MMA issuer
     mbar_init(recv_bar, 1);
     if (split > 1) mbar_arrive_expect_tx(recv_bar, static_cast<uint32_t>((split - 1) * rpo * NB * 4));
     err_flag[0] = 0;
     fence_mbarrier_init();
   }
   if (warp == kUmMmaWarp) {
-    tmem_alloc(tmem_slot, kUmTmemCols);
+    tmem_alloc(tmem_slot, kTmemCols);
     tmem_relinquish();
   }
   tc_fence_before();
@@ -233,10 +248,12 @@ __global__ void __launch_bounds__(kUmThreads, 1)
       }
     }
     __syncwarp();
-  } else if (warp == kUmMmaWarp) {
-    // ---------------- MMA issuer ----------------
+  } else if (warp == kUmMmaWarp || warp == kUmMmaWarp2) {
+    // ---------------- MMA issuers: half h of every stage into accumulator h ----------------
     if (lane == 0) {
+      const int h = warp - kUmMmaWarp;
       const uint32_t xaddr = smem_u32(xbuf);
+      const uint32_t dcol = tmem + kDCol + static_cast<uint32_t>(h * NB);
       bool ok = true;
       for (int it = 0; ok && it < n_iters; ++it) {
         const int xs = it % XD;
@@ -244,33 +261,31 @@ __global__ void __launch_bounds__(kUmThreads, 1)
           ok = false;
           break;
         }
-        if (it == 0) QTTS_TRACE_STAMP(2);
-        for (int h = 0; h < 2; ++h) {
-          const int hs = 2 * it + h;
-          const int slot = hs % kNA;
-          if (!mbar_wait_bounded(&afull[slot], (hs / kNA) & 1, a.wait_ns)) {
-            ok = false;
-            break;
-          }
-          QTTS_TRACE_DETAIL(0, hs);
-          tc_fence_after();
-          const uint32_t acol = tmem + kSlotCols * slot;
-#pragma unroll
-          for (int i = 0; i < 4; ++i) {
-            const uint64_t bdesc = smem_desc_k_sw128(xaddr + xs * XS + h * (NB * 128) + i * 32);
-            umma_f16_ts(tmem + kDCol, acol + 8 * i, bdesc, kIdesc, (it | h | i) != 0 ? 1u : 0u);
-          }
-          tc_commit(&aempty[slot]);
-          QTTS_TRACE_DETAIL(1, hs);
+        if (it == 0 && h == 0) QTTS_TRACE_STAMP(2);
+        const int hs = 2 * it + h;
+        const int slot = hs % kNA;
+        if (!mbar_wait_bounded(&afull[slot], (hs / kNA) & 1, a.wait_ns)) {
+          ok = false;
+          break;
         }
+        QTTS_TRACE_DETAIL(0, hs);
+        tc_fence_after();
+        const uint32_t acol = tmem + kSlotCols * slot;
+#pragma unroll
+        for (int i = 0; i < 4; ++i) {
+          const uint64_t bdesc = smem_desc_k_sw128(xaddr + xs * XS + h * (NB * 128) + i * 32);
+          umma_f16_ts(dcol, acol + 8 * i, bdesc, kIdesc, (it | i) != 0 ? 1u : 0u);
+        }
+        tc_commit(&aempty[slot]);
+        QTTS_TRACE_DETAIL(1, hs);
         tc_commit(&xempty[xs]);
       }
       if (!ok) {
         record_status(QTTS_ERR_TIMEOUT);
         *verr = 1;
       }
-      QTTS_TRACE_STAMP(3);
-      tc_commit(dfull);  // arrives once every MMA issued above has completed
+      if (h == 0) QTTS_TRACE_STAMP(3);
+      tc_commit(dfull);  // arrives once every MMA this thread issued has completed
     }
     __syncwarp();
   } else {
@@ -356,6 +371,20 @@ __global__ void __launch_bounds__(kUmThreads, 1)
     // The loaded registers are only valid after the wait: tie them to it.
 #pragma unroll
     for (int c = 0; c < HALF; ++c) asm volatile("" : "+r"(d[c]));
+    // The second issuer's accumulator (the other 64-k half of every stage).
+    {
+      constexpr int kC = HALF < 32 ? HALF : 32;
+#pragma unroll
+      for (int c0 = 0; c0 < HALF; c0 += kC) {
+        uint32_t e[kC];
+        tmem_ld<kC>(tmem + lane_base + kDCol + NB + HALF * half + c0, e);
+        tc_wait_ld();
+#pragma unroll
+        for (int c = 0; c < kC; ++c) asm volatile("" : "+r"(e[c]));
+#pragma unroll
+        for (int c = 0; c < kC; ++c) d[c0 + c] = __float_as_uint(__uint_as_float(d[c0 + c]) + __uint_as_float(e[c]));
+      }
+    }
     const bool cta_err = *verr != 0;
     float v[HALF];
 #pragma unroll
@@ -440,13 +469,13 @@ __global__ void __launch_bounds__(kUmThreads, 1)
   if (tid == 0) QTTS_TRACE_STAMP(7);
   if (warp == kUmMmaWarp) {
     tc_fence_after();
-    tmem_dealloc(tmem, kUmTmemCols);
+    tmem_dealloc(tmem, kTmemCols);
   }
   // The dequant warps waited on the cluster barrier before their remote
   // stores; the producer and MMA warps complete it here. Stores that came from
   // registers need no source kept alive, and each CTA waited for everything
   // sent to it.
-  if (split > 1 && (warp == kUmProducerWarp || warp == kUmMmaWarp)) cluster_wait();
+  if (split > 1 && (warp == kUmProducerWarp || warp == kUmMmaWarp || warp == kUmMmaWarp2)) cluster_wait();
   if (AG) ag_finish(a, ag_ep);
   if (warp == kUmProducerWarp && lane == 0 && *verr != 0) {
     // Drain our own copies in flight (weights and activations).
@@ -482,7 +511,7 @@ int launch_umma_t(const CUtensorMap& map, const CUtensorMap& xmap, const SkinnyA
   cudaLaunchConfig_t cfg = {};
   cfg.gridDim = p.grid;
   cfg.blockDim = dim3(kUmThreads, 1, 1);
-  cfg.dynamicSmemBytes = p.smem;
+  cfg.dynamicSmemBytes = umma_tmem_cols(NB) > 256 && p.smem < kUmFullTmemMinSmem ? kUmFullTmemMinSmem : p.smem;
   cfg.stream = stream;
   cudaLaunchAttribute attrs[2];
   int na = 0;
@@ -575,10 +604,11 @@ SkinnyPlan plan_umma(int M, int N, int K, int G, int split_req) {
   p.k_per_cta = kpc_for(split);
   const int n_iters = p.k_per_cta / 128;
   // Activation ring: 4 tiles (never more than the slice); weight ring: fill
-  // a ~100 KiB budget so the next kernel's CTA fits beside this one. (A
-  // deeper ring does not help: the dequant warps run at most three stages
-  // ahead of the MMAs, which are bound by the ~115-cycle cost of each
-  // 128-row tcgen05.mma.)
+  // a ~100 KiB budget (grids whose tensor memory fills the SM are raised to
+  // 116 KiB at launch). A deeper ring does not help (swept 2-12 weight stages,
+  // 2-4 activation stages, 100-220 KiB): with two MMA issuers the loop is
+  // bound by the dequantization (int8 -> bf16 costs ~2.5 instructions per
+  // weight; ~0.65 us per 128-k stage of 128 rows).
   const int xmax = nb > 64 ? 2 : 4;  // 32 KiB activation tiles at NB = 128
   int xstages = n_iters < xmax ? n_iters : xmax;
   xstages = xstages < 1 ? 1 : xstages;
