@@ -189,6 +189,20 @@ __global__ void __launch_bounds__(kSkThreads, 2)
     __syncwarp();
   } else {
     // ---------------- consumers ----------------
+    // The scale and bias of the output channel this thread finishes (every
+    // epilogue below gives thread t the owned row t mod (rows owned), which
+    // divides 256) are constants of the layer: loaded before the dependency
+    // wait, so the end of the chain does not wait on a cold global load.
+    float pre_sc = 0.f, pre_bias = 0.f;
+    {
+      const int own = split > 1 ? rpo : BN;
+      const int n = n0 + (split > 1 ? static_cast<int>(crank) * rpo : 0) + tid % own;
+      if (valid && n < a.N) {
+        const int64_t ch = static_cast<int64_t>(group) * a.N + n;
+        pre_sc = load_as_float(a.scale, a.scale_dtype, ch);
+        if (a.bias != nullptr) pre_bias = to_float(static_cast<const XT*>(a.bias)[ch]);
+      }
+    }
     pdl_wait();
     if (tid == 0) QTTS_TRACE_STAMP(2);
     if (AG) ag_ep = ag_epoch(a);  // consumed after the activation staging
@@ -490,9 +504,7 @@ __global__ void __launch_bounds__(kSkThreads, 2)
           const int row = i - m * BN;
           const int n = n0 + row;
           if (n < a.N) {
-            const int64_t ch = static_cast<int64_t>(group) * a.N + n;
-            float r = red[row * MB + m] * load_as_float(a.scale, a.scale_dtype, ch);
-            if (a.bias != nullptr) r += to_float(static_cast<const XT*>(a.bias)[ch]);
+            const float r = red[row * MB + m] * pre_sc + pre_bias;
             put_out<AG>(a, og, pbase, static_cast<int64_t>(m) * a.ldo + n, from_float<XT>(r));
           }
         }
@@ -548,9 +560,7 @@ __global__ void __launch_bounds__(kSkThreads, 2)
           if (n < a.N) {
             float r = 0.f;
             for (int p = 0; p < split; ++p) r += recv[(p * rpo + lr) * MB + m];
-            const int64_t ch = static_cast<int64_t>(group) * a.N + n;
-            r *= load_as_float(a.scale, a.scale_dtype, ch);
-            if (a.bias != nullptr) r += to_float(static_cast<const XT*>(a.bias)[ch]);
+            r = r * pre_sc + pre_bias;
             put_out<AG>(a, og, pbase, static_cast<int64_t>(m) * a.ldo + n, from_float<XT>(r));
           }
         }
@@ -571,14 +581,11 @@ __global__ void __launch_bounds__(kSkThreads, 2)
               r.z += t.z;
               r.w += t.w;
             }
-            const int64_t ch = static_cast<int64_t>(group) * a.N + n;
-            const float sc = load_as_float(a.scale, a.scale_dtype, ch);
-            const float bias = a.bias != nullptr ? to_float(static_cast<const XT*>(a.bias)[ch]) : 0.f;
             const float rv[4] = {r.x, r.y, r.z, r.w};
 #pragma unroll
             for (int q = 0; q < 4; ++q) {
               const int m = 4 * mq + q;
-              if (m < mrows) put_out<AG>(a, og, pbase, static_cast<int64_t>(m) * a.ldo + n, from_float<XT>(rv[q] * sc + bias));
+              if (m < mrows) put_out<AG>(a, og, pbase, static_cast<int64_t>(m) * a.ldo + n, from_float<XT>(rv[q] * pre_sc + pre_bias));
             }
           }
         }

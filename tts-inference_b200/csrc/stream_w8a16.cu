@@ -215,6 +215,15 @@ __global__ void __launch_bounds__(kStThreads, 2)
     __syncwarp();
   } else {
     // ---------------- consumers ----------------
+    // The scale and bias of the output channel this thread finishes (the
+    // epilogue gives thread t row t mod BN, and BN divides NT) are constants of
+    // the layer: loaded before the dependency wait.
+    float pre_sc = 0.f, pre_bias = 0.f;
+    if (valid && n0 + tid % BN < a.N) {
+      const int64_t ch = static_cast<int64_t>(group) * a.N + n0 + tid % BN;
+      pre_sc = load_as_float(a.scale, a.scale_dtype, ch);
+      if (a.bias != nullptr) pre_bias = to_float(static_cast<const XT*>(a.bias)[ch]);
+    }
     pdl_wait();
     if (tid == 0) QTTS_TRACE_STAMP(2);
     // Staged activation extent: K rounded up to whole 128-wide boxes (zeros
@@ -530,9 +539,7 @@ __global__ void __launch_bounds__(kStThreads, 2)
           for (int w = 1; w < kStConsumerWarps; ++w) xsum += xpart[w * MB + m];
           const float inv = pow2f_st(-row_exponent(__uint_as_float(xmax[m])));
           const float dot = fmaf(-kStBias, xsum, sum) * inv;
-          const int64_t ch = static_cast<int64_t>(group) * a.N + n;
-          float r = dot * load_as_float(a.scale, a.scale_dtype, ch);
-          if (a.bias != nullptr) r += to_float(static_cast<const XT*>(a.bias)[ch]);
+          const float r = dot * pre_sc + pre_bias;
           og[static_cast<int64_t>(m) * a.ldo + n] = from_float<XT>(r);
         }
       }

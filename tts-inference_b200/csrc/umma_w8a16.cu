@@ -295,6 +295,19 @@ __global__ void __launch_bounds__(kUmThreads, 1)
     const int quarter = warp & 3;
     const int half = warp >> 2;
     const int row = quarter * 32 + lane;  // weight row within the tile == TMEM lane
+    // Scale and bias of the output channel this thread finishes (split 1: its
+    // TMEM lane's row; split > 1: owned row tid mod the rows owned, which
+    // divides 256): constants of the layer, loaded now so the epilogue does
+    // not wait on them.
+    float pre_sc = 0.f, pre_bias = 0.f;
+    {
+      const int n = n0 + (split > 1 ? static_cast<int>(crank) * rpo + tid % rpo : row);
+      if (valid && n < a.N) {
+        const int64_t ch = static_cast<int64_t>(group) * a.N + n;
+        pre_sc = load_as_float(a.scale, a.scale_dtype, ch);
+        if (a.bias != nullptr) pre_bias = to_float(static_cast<const XT*>(a.bias)[ch]);
+      }
+    }
     const uint32_t wbase = smem_u32(wbuf);
     const uint32_t lane_base = static_cast<uint32_t>(quarter * 32) << 16;
     bool ok = true;
@@ -394,13 +407,10 @@ __global__ void __launch_bounds__(kUmThreads, 1)
       bool store_ok = valid && !cta_err;
       if (AG) store_ok = ag_gate_stores(a, ag_ep, gate_flag, 1, kUmDqWarps * 32, tid == 0) && store_ok;
       if (store_ok && n < a.N) {
-        const int64_t ch = static_cast<int64_t>(group) * a.N + n;
-        const float sc = load_as_float(a.scale, a.scale_dtype, ch);
-        const float bias = a.bias != nullptr ? to_float(static_cast<const XT*>(a.bias)[ch]) : 0.f;
 #pragma unroll
         for (int c = 0; c < HALF; ++c) {
           const int col = HALF * half + c;
-          if (col < mrows) put_out<AG>(a, og, pbase, static_cast<int64_t>(col) * a.ldo + n, from_float<XT>(v[c] * sc + bias));
+          if (col < mrows) put_out<AG>(a, og, pbase, static_cast<int64_t>(col) * a.ldo + n, from_float<XT>(v[c] * pre_sc + pre_bias));
         }
       }
     } else {
@@ -448,14 +458,11 @@ __global__ void __launch_bounds__(kUmThreads, 1)
               r.z += t.z;
               r.w += t.w;
             }
-            const int64_t ch = static_cast<int64_t>(group) * a.N + n;
-            const float sc = load_as_float(a.scale, a.scale_dtype, ch);
-            const float bias = a.bias != nullptr ? to_float(static_cast<const XT*>(a.bias)[ch]) : 0.f;
             const float rv[4] = {r.x, r.y, r.z, r.w};
 #pragma unroll
             for (int q = 0; q < 4; ++q) {
               const int m = 4 * mq + q;
-              if (m < mrows) put_out<AG>(a, og, pbase, static_cast<int64_t>(m) * a.ldo + n, from_float<XT>(rv[q] * sc + bias));
+              if (m < mrows) put_out<AG>(a, og, pbase, static_cast<int64_t>(m) * a.ldo + n, from_float<XT>(rv[q] * pre_sc + pre_bias));
             }
           }
         }
