@@ -202,7 +202,8 @@ def test_silu_mul_gemm_fused_equals_two_steps(variant, m):
 
 @pytest.mark.parametrize("m", [1, 8, 16, 64, 128])
 def test_talker_shapes_auto(m):
-    for n, k, which in ((12288, 2048, "rms"), (2048, 6144, "silu"), (3072, 2048, "rms")):
+    for n, k, which in ((12288, 2048, "rms"), (2048, 6144, "silu"), (3072, 2048, "rms"), (4096, 1024, "rms"),
+                        (6144, 1024, "rms"), (1024, 3072, "silu")):
         wq, ws, q, s = gemm_case(n, k, seed=250 + n)
         if which == "rms":
             x, nw = norm_rows(m, k, torch.bfloat16, seed=251)

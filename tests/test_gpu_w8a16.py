@@ -76,6 +76,23 @@ def test_talker_shapes_all_rows(label, n, k):
         assert_close_to_oracle(out, ref_all[:m], f"{label} M={m}")
 
 
+CP_SHAPES = [("cp_qkv", 4096, 1024), ("cp_o", 1024, 2048), ("cp_gate_up", 6144, 1024), ("cp_down", 1024, 3072)]
+
+
+@pytest.mark.parametrize("label,n,k", CP_SHAPES)
+def test_code_predictor_shapes_with_bias(label, n, k):
+    # The code predictor's linears at the library's own plans, bias included. Code-predictor
+    # down (1024 x 3072) splits K eight ways in 512-wide slices up to 16 rows: its last two
+    # CTAs of each cluster hold no K and add zeros to the exchange.
+    x, q, s = seeded_case(n, k, 64, seed=16)
+    bias = (torch.randn(n, generator=torch.Generator().manual_seed(17)) * 0.1).to(torch.bfloat16)
+    ref_all = oracle.w8a16_reference(x.float().numpy(), q, scale_values(s, torch.bfloat16), bias.float().numpy())
+    xd, qd, sd = to_dev(x, q, s)
+    for m in (1, 4, 8, 15, 16, 24, 64):
+        out = qk.w8_gemm(xd[:m], qd, sd, bias.cuda())
+        assert_close_to_oracle(out, ref_all[:m], f"{label} M={m} ({nat.plan(m, n, k)})")
+
+
 @pytest.mark.parametrize("label,n,k", SHAPES)
 def test_matches_reference_eager_path(label, n, k):
     # The north-star check: the reference's eager dequant-then-matmul

@@ -1,8 +1,8 @@
 """The library's kernel choice (qtts_w8a16_plan, host-only) on the talker and code-predictor shapes.
 
 Pins the rule the B200 measurements chose: up to 16 rows the split-K streaming
-kernel with the most CTAs that run two per SM (ties to the larger row tile,
-every CTA of a split owning part of K); up to 4 rows of int8 the whole-K
+kernel with the most CTAs holding a slice of K among the plans that run two per
+SM (ties to the larger row tile); up to 4 rows of int8 the whole-K
 streaming kernel where it reaches more CTAs; past 16 rows the tcgen05 kernel, whose
 batch tile grows to 128 columns past 64 rows only when 64-column tiles would not fit
 one CTA per SM.
@@ -38,8 +38,10 @@ def _lib():
         # past 64 rows: one 128-column tile when 64-column tiles would overflow a wave
         (12288, 2048, 128, "umma_w8a16_kernel", 1, 128, 96),
         (4096, 1024, 128, "umma_w8a16_kernel", 2, 128, 128),
-        # code predictor down: every 256-CTA plan would leave a split CTA without K
-        (1024, 3072, 8, "skinny_w8a16_kernel", 2, 16, 128),
+        # code predictor down: 8 splits of 512 k, the last two without K (192 of 256 CTAs with
+        # work) beat every plan whose CTAs all hold K (128 CTAs)
+        (1024, 3072, 8, "skinny_w8a16_kernel", 8, 32, 256),
+        (1024, 3072, 1, "skinny_w8a16_kernel", 8, 32, 256),
     ],
 )
 def test_auto_plans(n, k, m, kernel, split, rows, ctas):
@@ -59,14 +61,17 @@ def test_grouped_heads_and_forced_variants():
         nat.plan(1, 2048, 100)  # K % 16 != 0
 
 
-def test_every_split_owns_part_of_k():
+def test_splits_give_most_ctas_work():
+    """Slices are whole stages, so a split may leave its last CTAs without K; the planner
+    keeps that to at most a quarter of a cluster on the talker and code-predictor shapes."""
     for n, k in [(1024, 3072), (2048, 6144), (4096, 2048), (6144, 1024), (3072, 2048), (80, 272)]:
         for m in (1, 2, 4, 8, 9, 16):
             p = nat.plan(m, n, k)
             if p["kernel"] == "skinny_w8a16_kernel" and p["split"] > 1:
                 sw = 128 * (128 // p["row_tile"])  # k per stage: 8 warps / (row tile / 16) k groups
                 kpc = -(-(-(-k // p["split"])) // sw) * sw
-                assert (p["split"] - 1) * kpc < k, (n, k, m, p)
+                with_k = min(p["split"], -(-k // kpc))
+                assert 4 * with_k >= 3 * p["split"], (n, k, m, p)
 
 
 @pytest.mark.parametrize("m", [1, 2, 4, 8, 16, 17, 64])

@@ -745,23 +745,29 @@ SkinnyPlan plan_skinny(int M, int N, int K, int G, int split_req, int r_req) {
   const int rgs[4] = {8, 4, 2, 1};
   int split = split_req, r = r_req;
   if (split == 0 || r == 0) {
-    // The most CTAs that still run two to an SM (the chained decode calls are
-    // latency-bound: two CTAs per SM overlap each other's activation fetch,
-    // loop and split-K exchange), activation slice within 48 KiB; ties go to
-    // the larger row tile, then the smaller split. Measured on B200 in chains of
-    // talker linears: qkv and down_proj at M = 1..16 gain 10-15 % over one CTA
-    // per SM. When every choice exceeds two per SM: the fewest CTAs.
+    // The most CTAs with work (a slice of K) among the plans that still run
+    // two to an SM (the chained decode calls are latency-bound: two CTAs per
+    // SM overlap each other's activation fetch, loop and split-K exchange),
+    // activation slice within 48 KiB; ties go to the larger row tile, then the
+    // smaller split. Slices are whole stages, so a split may leave its last
+    // CTAs without K (they add zeros to the exchange). Measured on B200 in
+    // chains of talker linears: qkv and down_proj at M = 1..16 gain 10-15 %
+    // over one CTA per SM; code-predictor down (1024 x 3072) at M = 1 and 8
+    // runs 4.5 / 5.0 us with 8 splits of 512 k (6 with work, 192 of 256 CTAs)
+    // against 7.4 / 8.8 us with 2 splits of 16 rows (128 CTAs). When every
+    // choice exceeds two per SM: the fewest CTAs.
     int best_c = -1, best_s = 0, best_r = 0, min_c = 0, min_s = 0, min_r = 0;
     for (int ri = 0; ri < 4; ++ri) {
       if (r != 0 && rgs[ri] != r) continue;
       for (int si = 0; si < 4; ++si) {
         if (split != 0 && splits[si] != split) continue;
         if (xbytes(splits[si], rgs[ri]) > 48 * 1024) continue;
-        // Every CTA of the split must own part of K.
-        if (splits[si] > 1 && (splits[si] - 1) * kpc_for(K, splits[si], 128 * (8 / rgs[ri])) >= K) continue;
+        const int kpc = kpc_for(K, splits[si], 128 * (8 / rgs[ri]));
+        const int with_k = min(splits[si], (K + kpc - 1) / kpc);
         const int c = ctas(splits[si], rgs[ri]);
-        if (c <= kCtaSlots && c > best_c) {
-          best_c = c;
+        const int working = c / splits[si] * with_k;
+        if (c <= kCtaSlots && working > best_c) {
+          best_c = working;
           best_s = splits[si];
           best_r = rgs[ri];
         }
