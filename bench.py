@@ -1372,11 +1372,32 @@ def run_single(spec: str, calls: int = 3) -> None:
     a small case for `ncu` captures. spec = "<shape>:<M>[:<variant>]" (W8A16),
     "fp8:<shape>:<M>" (activation quantization + fp8 GEMM), "fp8w:<shape>:<M>"
     (fp8 weight-only), "rms:<shape>:<M>" / "silu:<shape>:<M>" (W8A16 with its
-    RMSNorm / SiLU·up prologue, qtts_w8a16_gemm_prologue) or "frame" (one eager
-    config-4 frame inside a CUDA profiler range)."""
+    RMSNorm / SiLU·up prologue, qtts_w8a16_gemm_prologue), "frame" (one eager
+    config-4 frame inside a CUDA profiler range) or "refframe:<bf16|triton|library>" (one
+    frame of the reference's own model and CUDA graphs, int8 on the named kernel, inside a
+    CUDA profiler range after three warm frames)."""
     from qtts_b200.quant import kernels as qk
 
     parts = spec.split(":")
+    if parts[0] == "refframe":
+        from baseline import ref_frame as rf
+
+        arm = parts[1] if len(parts) > 1 else "library"
+        if arm not in ("bf16", "triton", "library"):
+            raise ValueError(f"refframe arm must be bf16, triton or library, not {arm!r}")
+        torch.cuda.set_device(0)
+        talker, predictor, _ = rf.build_models(batch=8, quant=None if arm == "bf16" else "int8_weight_only",
+                                               seed=0, kernels="triton" if arm == "triton" else "library")
+        fr = rf.RefFrame(talker, predictor, 8, 0)
+        for _ in range(3):
+            fr.step()
+        torch.cuda.synchronize()
+        torch.cuda.profiler.start()
+        fr.step()
+        torch.cuda.synchronize()
+        torch.cuda.profiler.stop()
+        print(json.dumps({"single": spec, "ok": True}))
+        return
     if parts[0] == "frame":
         # One eager config-4 frame (batch 8, all linears int8 with the fused prologues), with
         # the CUDA profiler range opened around it only (ncu --profile-from-start off).
