@@ -11,11 +11,12 @@
 // straight into the K-major shared-memory layout tcgen05 reads. The weight
 // stream starts before the programmatic-dependent-launch wait (weights are
 // constant); the activation tiles -- written by the quantization kernel that
-// precedes this one -- after it. One thread issues tcgen05.mma kind::f8f6f4
+// precedes this one -- after it. Two threads issue tcgen05.mma kind::f8f6f4
 // (M = 128 weight rows, N = NB batch columns, K = 32 per instruction; 4096
-// weights per instruction), accumulating fp32 in tensor memory, and releases
-// each stage with tcgen05.commit. Four epilogue warps read the accumulator with
-// tcgen05.ld (one row per thread). K can be split over a cluster of up to 4
+// weights per instruction), each the MMAs of one 64-k half of every stage into
+// its own fp32 accumulator in tensor memory, and release each stage with
+// tcgen05.commit. Four epilogue warps read both accumulators with tcgen05.ld
+// (one row per thread) and add them. K can be split over a cluster of up to 4
 // CTAs whose partial sums reach the row owner by st.async. All waits are
 // bounded; tensor memory is always freed.
 //
@@ -32,8 +33,9 @@ namespace qtts {
 constexpr int kF8StageW = 16384;  // 128 rows x 128 k e4m3
 constexpr int kF8EpiWarps = 4;
 constexpr int kF8ProducerWarp = 4;
-constexpr int kF8MmaWarp = 5;
-constexpr int kF8Threads = 6 * 32;
+constexpr int kF8MmaWarp = 5;   // issues the first 64-k half of every stage into accumulator 0
+constexpr int kF8MmaWarp2 = 6;  // the second half into accumulator 1 (added in the epilogue)
+constexpr int kF8Threads = 7 * 32;
 
 template <int N>
 __device__ __forceinline__ void f8_tmem_ld(uint32_t taddr, uint32_t (&r)[N]);
@@ -70,7 +72,8 @@ __global__ void __launch_bounds__(kF8Threads, 1)
     fp8_gemm_kernel(const __grid_constant__ CUtensorMap wmap, const __grid_constant__ CUtensorMap xmap,
                     const Fp8Args a) {
   constexpr int XS = NB * 128;  // activation tile bytes per 128-k stage
-  constexpr uint32_t kCols = NB < 32 ? 32 : NB;  // TMEM allocation: power of two >= 32
+  // TMEM: two fp32 accumulators of NB columns, allocated as a power of two >= 32.
+  constexpr uint32_t kCols = 2 * NB < 32 ? 32 : 2 * NB;
   constexpr uint32_t kIdesc = I8 ? umma_idesc_i8(128, NB) : umma_idesc(0u /*E4M3*/, 0u /*E4M3*/, 128, NB);
   extern __shared__ uint8_t smem_raw[];
   uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
@@ -110,9 +113,9 @@ __global__ void __launch_bounds__(kF8Threads, 1)
     for (int s = 0; s < S; ++s) {
       mbar_init(&wfull[s], 1);
       mbar_init(&xfull[s], 1);
-      mbar_init(&sempty[s], 1);
+      mbar_init(&sempty[s], 2);  // one commit from each MMA issuer
     }
-    mbar_init(dfull, 1);
+    mbar_init(dfull, 2);
     mbar_init(recv_bar, 1);
     if (split > 1) mbar_arrive_expect_tx(recv_bar, static_cast<uint32_t>((split - 1) * rpo * NB * 4));
     err_flag[0] = 0;
@@ -162,8 +165,13 @@ __global__ void __launch_bounds__(kF8Threads, 1)
       }
     }
     __syncwarp();
-  } else if (warp == kF8MmaWarp) {
+  } else if (warp == kF8MmaWarp || warp == kF8MmaWarp2) {
+    // Two issuing threads, one per 64-k half of every stage, each into its own
+    // accumulator: a single issuer that commits to release its stages measured
+    // ~60-90 cycles per instruction, two measured ~32.
     if (lane == 0) {
+      const int h = warp - kF8MmaWarp;
+      const uint32_t dcol = tmem + static_cast<uint32_t>(h * NB);
       const uint32_t waddr = smem_u32(wbuf);
       const uint32_t xaddr = smem_u32(xbuf);
       bool ok = true;
@@ -174,32 +182,33 @@ __global__ void __launch_bounds__(kF8Threads, 1)
           ok = false;
           break;
         }
-        QTTS_TRACE_DETAIL(3, it);
+        if (h == 0) QTTS_TRACE_DETAIL(3, it);
         if (!mbar_wait_bounded(&xfull[s], ph, a.wait_ns)) {
           ok = false;
           break;
         }
-        QTTS_TRACE_DETAIL(0, it);
+        if (h == 0) QTTS_TRACE_DETAIL(0, it);
         tc_fence_after();
 #pragma unroll
-        for (int i = 0; i < 4; ++i) {
+        for (int i = 2 * h; i < 2 * h + 2; ++i) {
           const uint64_t adesc = smem_desc_k_sw128(waddr + s * kF8StageW + i * 32);
           const uint64_t bdesc = smem_desc_k_sw128(xaddr + s * XS + i * 32);
+          const uint32_t acc = (it != 0 || i != 2 * h) ? 1u : 0u;
           if (I8) {
-            umma_i8_ss(tmem, adesc, bdesc, kIdesc, (it | i) != 0 ? 1u : 0u);
+            umma_i8_ss(dcol, adesc, bdesc, kIdesc, acc);
           } else {
-            umma_f8_ss(tmem, adesc, bdesc, kIdesc, (it | i) != 0 ? 1u : 0u);
+            umma_f8_ss(dcol, adesc, bdesc, kIdesc, acc);
           }
         }
         tc_commit(&sempty[s]);
-        QTTS_TRACE_DETAIL(1, it);
+        if (h == 0) QTTS_TRACE_DETAIL(1, it);
       }
       if (!ok) {
         record_status(QTTS_ERR_TIMEOUT);
         *verr = 1;
       }
-      QTTS_TRACE_STAMP(2);
-      tc_commit(dfull);
+      if (h == 0) QTTS_TRACE_STAMP(2);
+      tc_commit(dfull);  // arrives once every MMA this thread issued has completed
     }
     __syncwarp();
   } else {
@@ -229,14 +238,20 @@ __global__ void __launch_bounds__(kF8Threads, 1)
     constexpr int kGrp = 16;
 #pragma unroll 1
     for (int g0 = 0; g0 < NB; g0 += kGrp) {
-    uint32_t dg[kGrp];
+    uint32_t dg[kGrp], dh[kGrp];
     f8_tmem_ld<16>(tmem + lane_base + g0, dg);
+    f8_tmem_ld<16>(tmem + lane_base + NB + g0, dh);
     tc_wait_ld();
     if (tid == 0) QTTS_TRACE_DETAIL(4, g0 / kGrp);
     // The loaded registers are only valid after the wait: tie them to it so no
     // use is scheduled above it.
 #pragma unroll
-    for (int q = 0; q < kGrp; ++q) asm volatile("" : "+r"(dg[q]));
+    for (int q = 0; q < kGrp; ++q) asm volatile("" : "+r"(dg[q]), "+r"(dh[q]));
+    // The two issuers' accumulators: exact int32 adds (I8) or one fp32 add.
+#pragma unroll
+    for (int q = 0; q < kGrp; ++q)
+      dg[q] = I8 ? static_cast<uint32_t>(static_cast<int>(dg[q]) + static_cast<int>(dh[q]))
+                 : __float_as_uint(__uint_as_float(dg[q]) + __uint_as_float(dh[q]));
     {
       const int c0 = g0;
       // The group's activation scales into registers before any output store:
@@ -342,7 +357,7 @@ __global__ void __launch_bounds__(kF8Threads, 1)
     tc_fence_after();
     tmem_dealloc(tmem, kCols);
   }
-  if (split > 1 && (warp == kF8ProducerWarp || warp == kF8MmaWarp)) cluster_wait();
+  if (split > 1 && (warp == kF8ProducerWarp || warp == kF8MmaWarp || warp == kF8MmaWarp2)) cluster_wait();
   if (warp == kF8ProducerWarp && lane == 0 && *verr != 0) {
     for (int s = 0; s < S && s < w_issued; ++s) {
       const int last = ((w_issued - 1 - s) / S) * S + s;
