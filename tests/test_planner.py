@@ -2,7 +2,8 @@
 
 Pins the rule the B200 measurements chose: up to 16 rows the split-K streaming
 kernel with the most CTAs holding a slice of K among the plans that run two per
-SM (ties to the larger row tile); up to 4 rows of int8 the whole-K
+SM (ties to the larger row tile), or at 9..16 rows the tcgen05 kernel where those CTAs
+would stream >= 96 KiB each; up to 4 rows of int8 the whole-K
 streaming kernel where it reaches more CTAs; past 16 rows the tcgen05 kernel, whose
 batch tile grows to 128 columns past 64 rows only when 64-column tiles would not fit
 one CTA per SM.
@@ -28,6 +29,10 @@ def _lib():
         (2048, 2048, 8, "skinny_w8a16_kernel", 8, 64, 256),  # o_proj
         (12288, 2048, 1, "stream_w8a16_kernel", 1, 48, 256),  # gate_up, few rows
         (12288, 2048, 8, "skinny_w8a16_kernel", 2, 128, 192),
+        # 9..16 rows: tcgen05 where the split-K CTAs would stream >= 96 KiB each
+        (12288, 2048, 16, "umma_w8a16_kernel", 1, 128, 96),
+        (12288, 2048, 9, "umma_w8a16_kernel", 1, 128, 96),
+        (2048, 6144, 16, "skinny_w8a16_kernel", 8, 64, 256),
         (2048, 6144, 4, "skinny_w8a16_kernel", 8, 64, 256),  # down_proj
         (4096, 2048, 32, "umma_w8a16_kernel", 4, 128, 128),
         (12288, 2048, 64, "umma_w8a16_kernel", 1, 128, 96),
@@ -77,14 +82,16 @@ def test_splits_give_most_ctas_work():
 @pytest.mark.parametrize("m", [1, 2, 4, 8, 16, 17, 64])
 def test_prologue_fuses_where_the_kernel_stages_activations(m):
     """RMSNorm / SiLU·up run inside the GEMM exactly when the chosen kernel is one of the
-    two streaming kernels (int8, up to 16 rows); past that the prologue kernel is chained."""
+    two streaming kernels (int8, up to 16 rows, not where 9..16 rows go to the tcgen05
+    kernel); otherwise the prologue kernel is chained."""
     lib = nat.lib()
     for n, k in ((4096, 2048), (12288, 2048), (2048, 6144), (3072, 1024)):
         for pro in (nat.PROLOGUE_RMSNORM, nat.PROLOGUE_SILU_MUL):
             fused = lib.qtts_w8a16_gemm_prologue_fused(m, n, k, pro, nat.VARIANT_AUTO)
             kernel = nat.plan(m, n, k)["kernel"]
             assert fused == (kernel in ("skinny_w8a16_kernel", "stream_w8a16_kernel")), (n, k, m)
-            assert fused == (m <= 16)
+            if m <= 8 or m > 16:
+                assert fused == (m <= 8)
     assert lib.qtts_w8a16_gemm_prologue_fused(8, 4096, 2048, nat.PROLOGUE_RMSNORM, nat.variant_umma(1)) == 0
     assert lib.qtts_w8a16_gemm_prologue_fused(8, 4096, 2048, nat.PROLOGUE_RMSNORM, nat.variant_skinny(2)) == 1
     assert lib.qtts_w8a16_gemm_prologue_fused(8, 4096, 2048, 0, nat.VARIANT_AUTO) == 0

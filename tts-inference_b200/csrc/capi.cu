@@ -478,7 +478,8 @@ static void set_allgather(SkinnyArgs& sa, const AllGatherForm* ag) {
 // AUTO's kernel for aligned 16-bit activations: 0x100 (split-K streaming), 0x200
 // (tcgen05) or 0x300 (whole-K streaming, with its row groups in *rgroups).
 // Up to 16 rows: the split-K streaming kernel with its planner's tile and split
-// (up to two CTAs per SM). Past 16: the tcgen05 kernel, whose per-instruction
+// (up to two CTAs per SM), except at 9..16 rows where its CTAs would stream
+// large slices (below). Past 16: the tcgen05 kernel, whose per-instruction
 // cost does not grow with M. Up to 4 rows of int8, the whole-K streaming kernel
 // where its row tiles (16..96 rows) reach more CTAs within two per SM than the
 // split-K plan can (gate_up 12288 x 2048 at M = 1: 256 CTAs, 7.2 us, vs 192
@@ -486,6 +487,17 @@ static void set_allgather(SkinnyArgs& sa, const AllGatherForm* ag) {
 static int auto_family(int M, int N, int K, int zg, int w_fmt, bool allgather, int* rgroups) {
   *rgroups = 0;
   if (M > 16) return 0x200;
+  if (M > 8 && zg == 1) {
+    // 9..16 rows: two 8-column MMA tiles per weight fragment double the
+    // split-K kernel's mma.sync work, while a tcgen05 MMA costs the same for
+    // any batch width; where the split-K plan streams >= 96 KiB per CTA the
+    // tcgen05 kernel is faster (talker gate_up 12288 x 2048 at M = 12 / 16:
+    // 12.8 / 12.8 us against 13.6 / 14.0 us; qkv, o_proj and down_proj, at
+    // 32-48 KiB per CTA, stay on the split-K kernel).
+    const SkinnyPlan sk = plan_skinny(M, N, K, zg, 0, 0);
+    const long long ctas = static_cast<long long>(sk.grid.x) * sk.grid.y * sk.grid.z;
+    if (ctas > 0 && static_cast<long long>(N) * K / ctas >= 96 * 1024) return 0x200;
+  }
   int family = 0x100;
   if (M <= 4 && w_fmt == kWInt8 && !allgather) {
     const SkinnyPlan sk = plan_skinny(M, N, K, zg, 0, 0);
