@@ -180,7 +180,8 @@ def test_two_ranks_over_peer_memory():
     import torch.multiprocessing as mp
 
     points = []
-    for n, k, m, seed in [(12288, 2048, 1, 110), (4096, 6144, 8, 111), (12288, 2048, 64, 112), (77, 96, 3, 113)]:
+    for n, k, m, seed in [(12288, 2048, 1, 110), (4096, 6144, 8, 111), (12288, 2048, 12, 114), (12288, 2048, 64, 112),
+                          (77, 96, 3, 113)]:
         x, q, s = case(n, k, m, seed)
         points.append((n, k, m, x, q, s))
     ctx = mp.get_context("spawn")
