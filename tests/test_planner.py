@@ -2,7 +2,8 @@
 
 Pins the rule the B200 measurements chose: up to 16 rows the split-K streaming
 kernel with the most CTAs holding a slice of K among the plans that run two per
-SM (ties to the larger row tile), or at 9..16 rows the tcgen05 kernel where those CTAs
+SM (ties to the larger row tile; plans of 64- or 128-row tiles with at least two stages per
+CTA first while they keep 128 CTAs with work), or at 9..16 rows the tcgen05 kernel where those CTAs
 would stream >= 96 KiB each; up to 4 rows of int8 the whole-K
 streaming kernel where it reaches more CTAs; past 16 rows the tcgen05 kernel, whose
 batch tile grows to 128 columns past 64 rows only when 64-column tiles would not fit
@@ -26,7 +27,9 @@ def _lib():
     [
         (4096, 2048, 1, "skinny_w8a16_kernel", 8, 128, 256),  # talker qkv
         (4096, 2048, 16, "skinny_w8a16_kernel", 8, 128, 256),
-        (2048, 2048, 8, "skinny_w8a16_kernel", 8, 64, 256),  # o_proj
+        # o_proj: 128 CTAs of 128 rows x 2 stages beat 256 one-stage CTAs
+        (2048, 2048, 8, "skinny_w8a16_kernel", 8, 128, 128),
+        (4096, 1024, 8, "skinny_w8a16_kernel", 4, 128, 128),  # code-predictor qkv
         (12288, 2048, 1, "stream_w8a16_kernel", 1, 48, 256),  # gate_up, few rows
         (12288, 2048, 8, "skinny_w8a16_kernel", 2, 128, 192),
         # 9..16 rows: tcgen05 where the split-K CTAs would stream >= 96 KiB each

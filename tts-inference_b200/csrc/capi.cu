@@ -481,8 +481,8 @@ static void set_allgather(SkinnyArgs& sa, const AllGatherForm* ag) {
 // (up to two CTAs per SM), except at 9..16 rows where its CTAs would stream
 // large slices (below). Past 16: the tcgen05 kernel, whose per-instruction
 // cost does not grow with M. Up to 4 rows of int8, the whole-K streaming kernel
-// where its row tiles (16..96 rows) reach more CTAs within two per SM than the
-// split-K plan can (gate_up 12288 x 2048 at M = 1: 256 CTAs, 7.2 us, vs 192
+// where the split-K plan has more CTAs than SMs and the whole-K row tiles
+// (16..96 rows) reach more CTAs within two per SM than it does (gate_up 12288 x 2048 at M = 1: 256 CTAs, 7.2 us, vs 192
 // CTAs, 9.3 us, measured on B200).
 static int auto_family(int M, int N, int K, int zg, int w_fmt, bool allgather, int* rgroups) {
   *rgroups = 0;
@@ -502,6 +502,11 @@ static int auto_family(int M, int N, int K, int zg, int w_fmt, bool allgather, i
   if (M <= 4 && w_fmt == kWInt8 && !allgather) {
     const SkinnyPlan sk = plan_skinny(M, N, K, zg, 0, 0);
     int best = static_cast<int>(sk.grid.x * sk.grid.y * sk.grid.z);
+    // Only where the split-K plan leaves SMs unevenly loaded (more CTAs than
+    // SMs, some SMs with two): a plan of at most one CTA per SM is balanced
+    // already (code-predictor qkv 4096 x 1024 at M = 4: 128 split-K CTAs
+    // 3.9 us, the whole-K kernel's 256 CTAs 4.9 us).
+    if (best <= kNumSMs) best = kCtaSlots;
     const int rows[5] = {6, 4, 3, 2, 1};
     for (int i = 0; i < 5; ++i) {
       const SkinnyPlan st = plan_stream(M, N, K, zg, rows[i]);

@@ -768,9 +768,16 @@ SkinnyPlan plan_skinny(int M, int N, int K, int G, int split_req, int r_req) {
     // chains of talker linears: qkv and down_proj at M = 1..16 gain 10-15 %
     // over one CTA per SM; code-predictor down (1024 x 3072) at M = 1 and 8
     // runs 4.5 / 5.0 us with 8 splits of 512 k (6 with work, 192 of 256 CTAs)
-    // against 7.4 / 8.8 us with 2 splits of 16 rows (128 CTAs). When every
-    // choice exceeds two per SM: the fewest CTAs.
+    // against 7.4 / 8.8 us with 2 splits of 16 rows (128 CTAs). Up to 8 rows,
+    // plans whose CTAs hold at least two stages of K go first while they keep >= 128 CTAs
+    // with work (row tiles of 64 or 128: narrower tiles reduce 4-8 k groups per
+    // stage in shared memory): a one-stage CTA's fixed costs (activation staging, exchange)
+    // are paid for 16 KiB of weights (talker o_proj 2048 x 2048 at M = 1..8:
+    // 128 CTAs of 128 rows x 2 stages 3.8-3.9 us against 256 one-stage CTAs
+    // 4.0-4.2 us; code-predictor qkv 4096 x 1024 3.7-3.9 against 4.1-4.2 us).
+    // When every choice exceeds two per SM: the fewest CTAs.
     int best_c = -1, best_s = 0, best_r = 0, min_c = 0, min_s = 0, min_r = 0;
+    int best2_c = -1, best2_s = 0, best2_r = 0;  // the same over plans of >= 2 stages per CTA
     for (int ri = 0; ri < 4; ++ri) {
       if (r != 0 && rgs[ri] != r) continue;
       for (int si = 0; si < 4; ++si) {
@@ -785,6 +792,11 @@ SkinnyPlan plan_skinny(int M, int N, int K, int G, int split_req, int r_req) {
           best_s = splits[si];
           best_r = rgs[ri];
         }
+        if (c <= kCtaSlots && rgs[ri] >= 4 && kpc >= 2 * 128 * (8 / rgs[ri]) && working > best2_c) {
+          best2_c = working;
+          best2_s = splits[si];
+          best2_r = rgs[ri];
+        }
         if (min_c == 0 || c < min_c) {
           min_c = c;
           min_s = splits[si];
@@ -792,7 +804,10 @@ SkinnyPlan plan_skinny(int M, int N, int K, int G, int split_req, int r_req) {
         }
       }
     }
-    if (best_c > 0) {
+    if (p.mt == 1 && best2_c >= 128) {
+      split = best2_s;
+      r = best2_r;
+    } else if (best_c > 0) {
       split = best_s;
       r = best_r;
     } else if (min_c > 0) {
