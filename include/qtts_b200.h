@@ -79,8 +79,13 @@ enum qtts_dtype {
 #define QTTS_FLAG_PDL 0x1u
 
 /* ---- kernel variants ---------------------------------------------------- */
-/* 0 lets the library choose from (M, N, K). The others force one kernel;
- * calibration (qtts_b200.quant.calibrate) times them per shape. */
+/* 0 lets the library choose from (M, N, K): up to 16 rows the split-K
+ * streaming kernel (up to 4 rows of int8 the whole-K streaming kernel where
+ * the split-K plan loads some SMs twice and the whole-K plan reaches more
+ * CTAs; at 9..16 rows the tcgen05 kernel where the split-K CTAs would each
+ * stream >= 96 KiB of weights), past 16 rows the tcgen05 kernel. The others
+ * force one kernel; calibration (qtts_b200.quant.calibrate) times them per
+ * shape. */
 #define QTTS_VARIANT_AUTO 0
 #define QTTS_VARIANT_GENERIC 1 /* SIMT kernel: any shape, stride, dtype    */
 /* TMA-streamed weights + mma.sync. `split`: K split over a thread-block
@@ -89,8 +94,10 @@ enum qtts_dtype {
  * warps split K inside it). 0 in either field lets the library choose. */
 #define QTTS_VARIANT_SKINNY(split) (0x100 | (split))
 #define QTTS_VARIANT_SKINNY_R(split, rows) (0x100 | (split) | ((rows) << 4))
-/* tcgen05/TMEM tile kernel (weights dequantized to bf16 in shared memory,
- * accumulator in tensor memory), split-K over a cluster of `split` CTAs. */
+/* tcgen05/TMEM tile kernel (128 weight rows per CTA converted to the
+ * activations' 16-bit type straight into tensor memory, activation tiles by
+ * TMA in shared memory, fp32 accumulators in tensor memory), split-K over a
+ * cluster of `split` CTAs. */
 #define QTTS_VARIANT_UMMA(split) (0x200 | (split))
 /* Whole-K streaming kernel for M <= 16: each CTA owns 16*`rows` output rows
  * (rows = 1, 2, 3, 4 or 6; 0 lets the library choose) over the whole of K, no
