@@ -47,7 +47,7 @@ _SPLITS = (1, 2, 4, 8)
 _ROW_GROUPS = (1, 2, 4, 8)
 #: Row tiles of the whole-K streaming kernel (16 * r rows per CTA).
 _STREAM_ROWS = (1, 2, 3, 4, 6)
-#: Split-K factors of the tcgen05 kernel (M > 16).
+#: Split-K factors of the tcgen05 kernel (calibration candidates from the 16-row bucket up).
 _UMMA_SPLITS = (1, 2, 4)
 
 

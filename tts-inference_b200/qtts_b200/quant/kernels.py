@@ -314,7 +314,8 @@ def w8_gemm_rmsnorm(x: torch.Tensor, norm_weight: torch.Tensor, eps: float, weig
                     scale: torch.Tensor, bias: torch.Tensor | None = None, *,
                     variant: int = nat.VARIANT_AUTO) -> torch.Tensor:
     """``w8_gemm(rms_norm(x, norm_weight, eps), weight, scale, bias)`` -- one launch when the
-    chosen kernel stages activations itself (M <= 16), else the norm kernel chained ahead."""
+    chosen kernel stages activations itself (one of the two streaming kernels, M <= 16), else
+    the norm kernel chained ahead (``prologue_fused`` tells which)."""
     return _prologue_gemm(x, nat.PROLOGUE_RMSNORM, norm_weight, eps, weight, scale, bias, variant)
 
 
