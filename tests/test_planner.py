@@ -30,6 +30,10 @@ def _lib():
         # o_proj: 128 CTAs of 128 rows x 2 stages beat 256 one-stage CTAs
         (2048, 2048, 8, "skinny_w8a16_kernel", 8, 128, 128),
         (4096, 1024, 8, "skinny_w8a16_kernel", 4, 128, 128),  # code-predictor qkv
+        # up to 4 rows the whole-K kernel only where the split-K plan loads some SMs twice:
+        # not for code-predictor qkv (128 CTAs), still for talker gate_up (192)
+        (4096, 1024, 1, "skinny_w8a16_kernel", 4, 128, 128),
+        (12288, 2048, 2, "stream_w8a16_kernel", 1, 48, 256),
         (12288, 2048, 1, "stream_w8a16_kernel", 1, 48, 256),  # gate_up, few rows
         (12288, 2048, 8, "skinny_w8a16_kernel", 2, 128, 192),
         # 9..16 rows: tcgen05 where the split-K CTAs would stream >= 96 KiB each
